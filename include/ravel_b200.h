@@ -1,0 +1,189 @@
+/*
+ * ravel_b200.h -- C ABI of the B200 (sm_100a) implementation of RAVEL's exact
+ * event-memory operator.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * handle (cudaStream_t passed as void*), never allocates or frees, never
+ * synchronises the host, and returns a status code (RAVEL_OK == 0).  The
+ * caller owns every buffer: outputs, the "tape" that carries the sorted event
+ * order from a forward call to its backward call, and per-call scratch.
+ * Sizes of the tape and scratch come from ravel_tape_bytes() and
+ * ravel_scratch_bytes().  Work is enqueued on `stream` and may be captured in
+ * a CUDA graph.
+ *
+ * Layouts (all C-contiguous, element strides only):
+ *   addresses     [B, T, C]         int32 or int64  (addr_dtype)
+ *   write_mask    [B, T]            uint8 0/1 or NULL (NULL: every step writes)
+ *   payloads      [B, T, C, D]      float32 / bfloat16 / float16 / float64
+ *   latest values [B, T, C, k, D]   payload dtype;  mask [B, T, C, k] uint8
+ *   sums          [B, T, C, D]      payload dtype;  mask [B, T, C]    uint8
+ *   cache values  [B, C, A, D]      payload dtype;  filled [B, C, A]  uint8
+ * A "stream" is one (b, c) pair; streams never interact.
+ *
+ * Semantics are those of the reference's ravel_lm/ravel_memory.py (paths
+ * relative to the ravel-lm project); each declaration cites the function it
+ * replaces.  Prefill addresses are reduced with a floor modulo of A after the
+ * reference's integer-width conversion; decode addresses are clamped to
+ * [0, A-1].
+ */
+#ifndef RAVEL_B200_H
+#define RAVEL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define RAVEL_OK 0
+#define RAVEL_ERR_INVALID_ARG 1   /* bad shape, dtype, k <= 0, A <= 0, null pointer */
+#define RAVEL_ERR_WORKSPACE 2     /* tape or scratch smaller than required */
+#define RAVEL_ERR_CUDA 3          /* a CUDA launch or runtime call failed */
+#define RAVEL_ERR_UNSUPPORTED 4   /* sizes beyond the supported range */
+#define RAVEL_ERR_DEVICE 5        /* a kernel flagged an error (ravel_device_error) */
+
+/* ---- dtype codes ------------------------------------------------------- */
+#define RAVEL_F32 0
+#define RAVEL_BF16 1
+#define RAVEL_F16 2
+#define RAVEL_F64 3
+#define RAVEL_I32 0
+#define RAVEL_I64 1
+
+/* ---- tape flags -------------------------------------------------------- */
+/* reads use their own addresses (read_addresses given and not the write tensor) */
+#define RAVEL_TAPE_GENERAL_READS 1
+/* a write_mask is given */
+#define RAVEL_TAPE_WRITE_MASK 2
+
+/* ---- device-side error bits (ravel_device_error) ------------------------ */
+#define RAVEL_DEVERR_SPIN 1       /* a decoupled-lookback wait hit its iteration limit */
+#define RAVEL_DEVERR_BOUNDS 2     /* an index check failed inside a kernel */
+
+/* Bytes of the tape written by a forward call and read by its backward call. */
+size_t ravel_tape_bytes(int64_t B, int64_t T, int64_t C, int64_t A, int tape_flags);
+
+/* Bytes of per-call scratch sufficient for every entry point at these sizes. */
+size_t ravel_scratch_bytes(int64_t B, int64_t T, int64_t C, int64_t D, int64_t A, int64_t k,
+                           int tape_flags);
+
+/*
+ * Sort the write events of every stream by (address, time) and, for general
+ * reads, find each read's latest earlier write.  Replaces the key build, mask
+ * compaction, torch.sort and searchsorted of ravel_lm/ravel_memory.py:126-159
+ * (and :200-216, :231-235 of causal_sum_lookup).
+ * raddr == NULL or raddr == waddr: reads alias writes.
+ */
+int ravel_tape_build(const void* waddr, const void* raddr, int addr_dtype, const uint8_t* wmask,
+                     int64_t B, int64_t T, int64_t C, int64_t A, int tape_flags,
+                     void* tape, size_t tape_bytes, void* scratch, size_t scratch_bytes,
+                     void* stream);
+
+/*
+ * Latest-k gather from a built tape: values[b,t,c,j] = payload of the j-th
+ * latest write with the same (b, c, address) strictly before t, else
+ * candidate*0; mask = validity.  Replaces ravel_lm/ravel_memory.py:160-176.
+ * raddr is needed only for general reads (NULL otherwise).
+ */
+int ravel_latestk_fwd_tape(const void* tape, int tape_flags, const void* raddr, int addr_dtype,
+                           const void* payload, int dtype, int64_t B, int64_t T, int64_t C,
+                           int64_t D, int64_t A, int64_t k, void* out_vals, uint8_t* out_mask,
+                           void* stream);
+
+/*
+ * causal_last_k_lookup forward (ravel_lm/ravel_memory.py:52-176):
+ * ravel_tape_build + ravel_latestk_fwd_tape.  The tape is kept for the backward.
+ */
+int ravel_latestk_fwd(const void* waddr, const void* raddr, int addr_dtype, const uint8_t* wmask,
+                      const void* payload, int dtype, int64_t B, int64_t T, int64_t C, int64_t D,
+                      int64_t A, int64_t k, void* out_vals, uint8_t* out_mask,
+                      void* tape, size_t tape_bytes, void* scratch, size_t scratch_bytes,
+                      void* stream);
+
+/*
+ * Gradient of the latest-k values w.r.t. payloads (the autograd of
+ * index_select + mask multiply at ravel_lm/ravel_memory.py:173-175):
+ * grad_payload[src] = sum of grad_vals over the valid slots that read src.
+ * grad_payload [B,T,C,D] is fully overwritten.  Deterministic for aliased
+ * reads without a mask; float32 atomics otherwise.
+ */
+int ravel_latestk_bwd(const void* tape, int tape_flags, const void* raddr, int addr_dtype,
+                      const void* grad_vals, int dtype, int64_t B, int64_t T, int64_t C, int64_t D,
+                      int64_t A, int64_t k, void* grad_payload, void* scratch, size_t scratch_bytes,
+                      void* stream);
+
+/*
+ * Segmented-sum lookup from a built tape: sums[b,t,c] = sum of payloads of
+ * writes with the same (b, c, address) strictly before t (float32
+ * accumulation, float64 for float64 payloads); mask = at least one such write.
+ * Replaces ravel_lm/ravel_memory.py:216-241.
+ */
+int ravel_segsum_fwd_tape(const void* tape, int tape_flags, const void* raddr, int addr_dtype,
+                          const void* payload, int dtype, int64_t B, int64_t T, int64_t C, int64_t D,
+                          int64_t A, void* out_sums, uint8_t* out_mask, void* scratch,
+                          size_t scratch_bytes, void* stream);
+
+/* causal_sum_lookup forward (ravel_lm/ravel_memory.py:179-241). */
+int ravel_segsum_fwd(const void* waddr, const void* raddr, int addr_dtype, const uint8_t* wmask,
+                     const void* payload, int dtype, int64_t B, int64_t T, int64_t C, int64_t D,
+                     int64_t A, void* out_sums, uint8_t* out_mask, void* tape, size_t tape_bytes,
+                     void* scratch, size_t scratch_bytes, void* stream);
+
+/*
+ * Gradient of the sums w.r.t. payloads (autograd of ravel_lm/ravel_memory.py:
+ * 217-240): each write receives the sum of grad_sums over later reads of its
+ * (b, c, address).  grad_payload [B,T,C,D] is fully overwritten.
+ */
+int ravel_segsum_bwd(const void* tape, int tape_flags, const void* raddr, int addr_dtype,
+                     const void* grad_sums, int dtype, int64_t B, int64_t T, int64_t C, int64_t D,
+                     int64_t A, void* grad_payload, void* scratch, size_t scratch_bytes,
+                     void* stream);
+
+/*
+ * Decode cache read (RavelLayerCache.read, ravel_lm/ravel_memory.py:271-281):
+ * out_vals[b,c] = values[b,c,clamp(addr)] * filled, out_mask[b,c] = filled.
+ */
+int ravel_cache_read(const void* values, const uint8_t* filled, const void* addr, int addr_dtype,
+                     int dtype, int64_t B, int64_t C, int64_t A, int64_t D, void* out_vals,
+                     uint8_t* out_mask, void* stream);
+
+/*
+ * Decode cache write (RavelLayerCache.write, ravel_lm/ravel_memory.py:283-292):
+ * values[b,c,clamp(addr)] = payload[b,c]; filled[...] = 1.  In place.
+ */
+int ravel_cache_write(void* values, uint8_t* filled, const void* addr, int addr_dtype,
+                      const void* payload, int dtype, int64_t B, int64_t C, int64_t A, int64_t D,
+                      void* stream);
+
+/*
+ * One decode step of a memory layer in one launch: the read of
+ * RavelMemoryLayer.step (ravel_lm/model.py:421) followed by its write (:424),
+ * for every (b, c).  The read sees the cache as it was before this step.
+ */
+int ravel_cache_step(void* values, uint8_t* filled, const void* raddr, const void* waddr,
+                     int addr_dtype, const void* payload, int dtype, int64_t B, int64_t C,
+                     int64_t A, int64_t D, void* out_vals, uint8_t* out_mask, void* stream);
+
+/* Copy the device error word (RAVEL_DEVERR_* bits) of the current device into
+ * *out after the work queued on `stream`; synchronises that stream. */
+int ravel_device_error(int* out, void* stream);
+
+/* Reset the device error word of the current device. */
+int ravel_clear_device_error(void* stream);
+
+/* Number of kernels this library has launched in this process (all devices). */
+uint64_t ravel_kernel_launches(void);
+
+/* Human-readable name of a status code. */
+const char* ravel_status_string(int status);
+
+/* Library version string. */
+const char* ravel_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RAVEL_B200_H */

@@ -1,0 +1,248 @@
+// common.cuh -- shared device helpers of the RAVEL event-memory kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "../../include/ravel_b200.h"
+
+namespace ravel {
+
+// ----------------------------------------------------------------- device error word
+// One word per device; kernels OR RAVEL_DEVERR_* bits into it.  Never traps.
+__device__ unsigned int g_error_word = 0u;
+
+__device__ __forceinline__ void flag_error(unsigned int bits) { atomicOr(&g_error_word, bits); }
+
+// ----------------------------------------------------------------- memory-order helpers
+__device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release(unsigned int* p, unsigned int v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Streaming (evict-first) 16-byte store: the latest-k outputs are written once
+// and never re-read by the producing kernel.
+__device__ __forceinline__ void st_cs_v4(void* p, uint4 v) {
+    asm volatile("st.global.cs.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y),
+                 "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+// Read-only 16-byte load through the non-coherent path.
+__device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// Asynchronous global->shared copies (16 / 8 / 4 bytes), committed as one group.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async8(void* smem, const void* gmem) {
+    unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+    unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
+__device__ __forceinline__ unsigned lanemask_lt() {
+    unsigned m;
+    asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+    return m;
+}
+
+// ----------------------------------------------------------------- address folding
+// ravel_lm/ravel_memory.py:127-128: .to(key_dtype).remainder(A).  With int32 keys
+// (B*C*A*(T+1) <= 2^31-1) an int64 address is first truncated to 32 bits.
+__device__ __forceinline__ int64_t load_addr(const void* base, int64_t i, int addr_i64) {
+    return addr_i64 ? static_cast<const int64_t*>(base)[i]
+                    : static_cast<int64_t>(static_cast<const int32_t*>(base)[i]);
+}
+
+__device__ __forceinline__ uint64_t fold_addr(int64_t a, int64_t A, int key32) {
+    if (key32) a = static_cast<int64_t>(static_cast<int32_t>(static_cast<uint32_t>(a)));
+    int64_t r = a % A;
+    if (r < 0) r += A;
+    return static_cast<uint64_t>(r);
+}
+
+// Decode-cache addresses are clamped, not wrapped (ravel_memory.py:276, :289).
+__device__ __forceinline__ int64_t clamp_addr(int64_t a, int64_t A) {
+    return a < 0 ? 0 : (a > A - 1 ? A - 1 : a);
+}
+
+// ----------------------------------------------------------------- payload dtypes
+// Element traits: storage type, accumulation type and conversions.
+template <int DT> struct Elem;
+template <> struct Elem<RAVEL_F32> {
+    using T = float; using Acc = float;
+    static __device__ __forceinline__ Acc to_acc(T v) { return v; }
+    static __device__ __forceinline__ T from_acc(Acc v) { return v; }
+};
+template <> struct Elem<RAVEL_BF16> {
+    using T = __nv_bfloat16; using Acc = float;
+    static __device__ __forceinline__ Acc to_acc(T v) { return __bfloat162float(v); }
+    static __device__ __forceinline__ T from_acc(Acc v) { return __float2bfloat16_rn(v); }
+};
+template <> struct Elem<RAVEL_F16> {
+    using T = __half; using Acc = float;
+    static __device__ __forceinline__ Acc to_acc(T v) { return __half2float(v); }
+    static __device__ __forceinline__ T from_acc(Acc v) { return __float2half_rn(v); }
+};
+template <> struct Elem<RAVEL_F64> {
+    using T = double; using Acc = double;
+    static __device__ __forceinline__ Acc to_acc(T v) { return v; }
+    static __device__ __forceinline__ T from_acc(Acc v) { return v; }
+};
+
+inline int elem_bytes(int dt) { return dt == RAVEL_F32 ? 4 : (dt == RAVEL_F64 ? 8 : 2); }
+
+// candidate * 0 on raw bits (ravel_memory.py:175, :280): a finite value keeps only
+// its sign bit (+-0); Inf/NaN become the dtype's canonical quiet NaN.
+template <int DT> __device__ __forceinline__ uint32_t zero_word(uint32_t w);
+template <> __device__ __forceinline__ uint32_t zero_word<RAVEL_F32>(uint32_t w) {
+    return ((w & 0x7f800000u) == 0x7f800000u) ? 0x7fc00000u : (w & 0x80000000u);
+}
+__device__ __forceinline__ uint32_t zero_half_pair(uint32_t w, uint32_t expmask, uint32_t qnan) {
+    uint32_t lo = w & 0xffffu, hi = w >> 16;
+    lo = ((lo & expmask) == expmask) ? qnan : (lo & 0x8000u);
+    hi = ((hi & expmask) == expmask) ? qnan : (hi & 0x8000u);
+    return lo | (hi << 16);
+}
+template <> __device__ __forceinline__ uint32_t zero_word<RAVEL_BF16>(uint32_t w) {
+    return zero_half_pair(w, 0x7f80u, 0x7fc0u);
+}
+template <> __device__ __forceinline__ uint32_t zero_word<RAVEL_F16>(uint32_t w) {
+    return zero_half_pair(w, 0x7c00u, 0x7e00u);
+}
+// float64 is handled on 32-bit word pairs: the high word carries sign and exponent.
+__device__ __forceinline__ void zero_f64_pair(uint32_t& lo, uint32_t& hi) {
+    if ((hi & 0x7ff00000u) == 0x7ff00000u) { hi = 0x7ff80000u; lo = 0u; }
+    else { hi &= 0x80000000u; lo = 0u; }
+}
+
+// Zero a vector of VB bytes (VB in {2, 4, 8, 16}) held as 32-bit words.
+template <int DT, int VB> struct VecZero {
+    static __device__ __forceinline__ uint4 apply(uint4 v) {
+        if constexpr (DT == RAVEL_F64) {
+            zero_f64_pair(v.x, v.y);
+            if constexpr (VB == 16) zero_f64_pair(v.z, v.w);
+        } else {
+            v.x = zero_word<DT>(v.x);
+            if constexpr (VB >= 8) v.y = zero_word<DT>(v.y);
+            if constexpr (VB == 16) { v.z = zero_word<DT>(v.z); v.w = zero_word<DT>(v.w); }
+        }
+        return v;
+    }
+};
+template <int DT> struct VecZero<DT, 2> {
+    static __device__ __forceinline__ uint4 apply(uint4 v) {
+        // one 16-bit element in the low half
+        if constexpr (DT == RAVEL_BF16) {
+            v.x = ((v.x & 0x7f80u) == 0x7f80u) ? 0x7fc0u : (v.x & 0x8000u);
+        } else {
+            v.x = ((v.x & 0x7c00u) == 0x7c00u) ? 0x7e00u : (v.x & 0x8000u);
+        }
+        return v;
+    }
+};
+
+// Load / store VB bytes as a uint4 (unused words are zero).
+template <int VB> __device__ __forceinline__ uint4 ld_vec(const void* p) {
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if constexpr (VB == 16) v = *static_cast<const uint4*>(p);
+    else if constexpr (VB == 8) { uint2 t = *static_cast<const uint2*>(p); v.x = t.x; v.y = t.y; }
+    else if constexpr (VB == 4) v.x = *static_cast<const uint32_t*>(p);
+    else v.x = *static_cast<const uint16_t*>(p);
+    return v;
+}
+template <int VB> __device__ __forceinline__ uint4 ldg_vec(const void* p) {
+    if constexpr (VB == 16) return ld_nc_v4(p);
+    else return ld_vec<VB>(p);
+}
+template <int VB> __device__ __forceinline__ void st_vec(void* p, uint4 v) {
+    if constexpr (VB == 16) *static_cast<uint4*>(p) = v;
+    else if constexpr (VB == 8) *static_cast<uint2*>(p) = make_uint2(v.x, v.y);
+    else if constexpr (VB == 4) *static_cast<uint32_t*>(p) = v.x;
+    else *static_cast<uint16_t*>(p) = static_cast<uint16_t>(v.x);
+}
+template <int VB> __device__ __forceinline__ void st_vec_stream(void* p, uint4 v) {
+    if constexpr (VB == 16) st_cs_v4(p, v);
+    else st_vec<VB>(p, v);
+}
+
+// Widest vector width (bytes) that divides a row of `row_bytes` and the base
+// alignment of every pointer involved.
+inline int pick_vec_bytes(int64_t row_bytes, uintptr_t align_bits) {
+    for (int vb = 16; vb >= 2; vb >>= 1) {
+        if (row_bytes % vb == 0 && (align_bits % vb) == 0) return vb;
+    }
+    return 2;
+}
+
+// ----------------------------------------------------------------- key layout
+// Per-stream event key: [invalid bit][address bits][time bits].  Keys are unique
+// within a stream because the time field is unique; sorting them is a stable
+// sort by address of a time-ordered sequence.
+struct KeyLayout {
+    int tbits;   // bits of the time field
+    int abits;   // bits of the address field
+    int mbit;    // 1 when a write mask is present (invalid bit above the address)
+    int key64;   // keys need 64 bits
+};
+
+inline int bits_for(uint64_t n) {  // bits to hold values 0..n-1 (n >= 1)
+    int b = 0;
+    while (b < 64 && (uint64_t(1) << b) < n) ++b;
+    return b;
+}
+
+inline KeyLayout key_layout(int64_t T, int64_t A, int has_mask) {
+    KeyLayout L;
+    L.tbits = bits_for(static_cast<uint64_t>(T > 1 ? T : 1));
+    if (L.tbits == 0) L.tbits = 1;
+    L.abits = bits_for(static_cast<uint64_t>(A));
+    L.mbit = has_mask ? 1 : 0;
+    L.key64 = (L.tbits + L.abits + L.mbit) > 32 ? 1 : 0;
+    return L;
+}
+
+inline size_t align_up(size_t x, size_t a = 256) { return (x + a - 1) / a * a; }
+
+// Unsigned division by a run-time constant through a multiply-high and a shift
+// (the round-up reciprocal method of Granlund & Montgomery, PLDI 1994).  Exact
+// for numerators below 2^31, which every in-kernel index it is used on is.
+struct FastDiv {
+    uint32_t d, m, s;
+    FastDiv() : d(1), m(0), s(0) {}
+    explicit FastDiv(uint32_t div) : d(div) {
+        s = 0;
+        while ((uint64_t(1) << s) < div) ++s;
+        m = static_cast<uint32_t>(((uint64_t(1) << 32) * ((uint64_t(1) << s) - div)) / div + 1);
+    }
+    __device__ __forceinline__ uint32_t div(uint32_t n) const {
+        return static_cast<uint32_t>((static_cast<uint64_t>(__umulhi(n, m)) + n) >> s);
+    }
+    __device__ __forceinline__ void divmod(uint32_t n, uint32_t& q, uint32_t& r) const {
+        q = div(n);
+        r = n - q * d;
+    }
+};
+
+}  // namespace ravel

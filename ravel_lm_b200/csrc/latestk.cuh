@@ -1,0 +1,300 @@
+// latestk.cuh -- causal latest-k lookup over the sorted event tape.
+//
+// Reference: ravel_lm/ravel_memory.py:153-176.  For a read at time t the
+// reference searches its key (base, t-1) in the sorted write keys, takes the k
+// sorted positions idx, idx-1, ..., idx-k+1, marks a slot valid when that key is
+// in the same (stream, address) group, and returns payload[order[safe]] * valid.
+// An invalid slot therefore holds candidate*0 (+-0 with the candidate's sign);
+// these kernels reproduce that bit for bit, including candidates that fall in
+// an earlier stream of the reference's global sorted order.
+//
+// Aliased reads, no mask ("fast" path): the read at sorted position p has its
+// latest earlier writes at p-1, p-2, ... (its own key is (addr, t) and every
+// key below it is <= (addr, t-1)), so one CTA handles a chunk of P sorted
+// positions with a window of P+k payload rows staged in shared memory by
+// cp.async.  Every row is read from HBM once; each output block of k*D
+// elements is one contiguous streaming store.
+//
+// General reads or a write mask: each read's latest index comes from
+// k_read_search; reads are processed in their original order so the output is
+// written sequentially, and candidate rows are gathered directly.
+#pragma once
+
+#include "common.cuh"
+
+namespace ravel {
+
+struct LkArgs {
+    const void* keys;       // [S][T] sorted per stream
+    const int* nvalid;      // general: [S]
+    const int64_t* soff;    // general: [S+1] exclusive prefix of nvalid
+    const int32_t* ridx;    // general: [N]
+    const void* raddr;      // general: [N]
+    int addr_i64, key32;
+    const void* payload;    // [N, D]
+    const void* grad;       // backward: grad of values [N, k, D]
+    void* out;              // forward: values [N, k, D]; backward: grad payload [N, D] / fp32 accum
+    uint8_t* out_mask;      // forward: [N, k]
+    int64_t B, T, C, D, A, k;
+    int tbits;
+    int64_t row_bytes;      // D * element bytes
+    int P;                  // sorted positions per CTA (fast path)
+    int64_t nchunks;        // chunks per stream (fast path)
+    FastDiv fd_rv, fd_bv, fd_k;  // divisions by vectors-per-row, vectors-per-block, k
+};
+
+// Flat payload row of (stream s, time t).
+__device__ __forceinline__ int64_t flat_row(int64_t s, int64_t t, int64_t T, int64_t C) {
+    return ((s / C) * T + t) * C + (s % C);
+}
+
+// ------------------------------------------------------------------ fast forward
+template <typename KeyT, int DT, int VB>
+__global__ void __launch_bounds__(256) k_lk_fwd_fast(LkArgs a) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int k = static_cast<int>(a.k);
+    const int W = a.P + k;
+    int64_t* wrow = reinterpret_cast<int64_t*>(smem);
+    uint64_t* wadr = reinterpret_cast<uint64_t*>(wrow + W);
+    unsigned char* rows = reinterpret_cast<unsigned char*>(wadr + W);
+    rows += (16 - (reinterpret_cast<uintptr_t>(rows) & 15)) & 15;
+
+    const int tid = threadIdx.x;
+    const int64_t T = a.T, C = a.C;
+    const int64_t s = blockIdx.x / a.nchunks;
+    const int64_t p0 = (blockIdx.x % a.nchunks) * a.P;
+    const int np = static_cast<int>((T - p0) < a.P ? (T - p0) : a.P);
+    const int nw = np + k;
+    const KeyT* keys = static_cast<const KeyT*>(a.keys);
+    const KeyT tmask = (static_cast<KeyT>(1) << a.tbits) - 1;
+
+    for (int i = tid; i < nw; i += 256) {
+        const int64_t p = p0 - k + i;
+        int64_t g = s * T + p;          // position in the reference's global order
+        uint64_t ad = ~0ull;            // "other stream": never matches
+        if (g < 0) g = 0;               // ravel_memory.py:163 clamp_min(0)
+        const KeyT key = keys[g];
+        if (p >= 0) ad = static_cast<uint64_t>(key >> a.tbits);
+        wrow[i] = flat_row(g / T, static_cast<int64_t>(key & tmask), T, C);
+        wadr[i] = ad;
+    }
+    __syncthreads();
+
+    const uint32_t rv = static_cast<uint32_t>(a.row_bytes / VB);
+    const char* pay = static_cast<const char*>(a.payload);
+    for (uint32_t e = tid; e < static_cast<uint32_t>(nw) * rv; e += 256) {
+        uint32_t i, v;
+        a.fd_rv.divmod(e, i, v);
+        const char* src = pay + wrow[i] * a.row_bytes + v * VB;
+        unsigned char* dst = rows + static_cast<int64_t>(i) * a.row_bytes + v * VB;
+        if constexpr (VB == 16) cp_async16(dst, src);
+        else if constexpr (VB == 8) cp_async8(dst, src);
+        else if constexpr (VB == 4) cp_async4(dst, src);
+        else st_vec<2>(dst, ld_vec<2>(src));
+    }
+    cp_async_wait_all();
+    __syncthreads();
+
+    char* outv = static_cast<char*>(a.out);
+    const uint32_t bv = rv * static_cast<uint32_t>(k);
+    for (uint32_t e = tid; e < static_cast<uint32_t>(np) * bv; e += 256) {
+        uint32_t i, v, j, o;
+        a.fd_bv.divmod(e, i, v);
+        a.fd_rv.divmod(v, j, o);
+        const int wi = static_cast<int>(i) + k;
+        const int src = wi - 1 - static_cast<int>(j);
+        uint4 x = ld_vec<VB>(rows + static_cast<int64_t>(src) * a.row_bytes + o * VB);
+        if (wadr[src] != wadr[wi]) x = VecZero<DT, VB>::apply(x);
+        st_vec_stream<VB>(outv + (wrow[wi] * k + j) * a.row_bytes + o * VB, x);
+    }
+    for (uint32_t e = tid; e < static_cast<uint32_t>(np * k); e += 256) {
+        uint32_t i, j;
+        a.fd_k.divmod(e, i, j);
+        const int wi = static_cast<int>(i) + k;
+        a.out_mask[wrow[wi] * k + j] = wadr[wi - 1 - j] == wadr[wi] ? 1 : 0;
+    }
+}
+
+inline size_t lk_fast_smem(int P, int64_t k, int64_t row_bytes) {
+    return static_cast<size_t>(P + k) * 16 + 16 + static_cast<size_t>(P + k) * row_bytes;
+}
+
+// ------------------------------------------------------------------ fast backward
+// grad[q] = sum_j [addr(q+1+j) == addr(q)] * grad_vals[read at q+1+j, slot j]:
+// every valid (read, slot) feeds exactly one write, so the sum is a gather and
+// needs no atomics.  Accumulates in float (double for float64).
+template <typename KeyT, int DT, int VB>
+__global__ void __launch_bounds__(256) k_lk_bwd_fast(LkArgs a) {
+    using E = Elem<DT>;
+    using Acc = typename E::Acc;
+    using V = typename E::T;
+    constexpr int EPV = VB / sizeof(V);  // elements per vector
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int k = static_cast<int>(a.k);
+    const int W = a.P + k;
+    int64_t* wrow = reinterpret_cast<int64_t*>(smem);
+    uint64_t* wadr = reinterpret_cast<uint64_t*>(wrow + W);
+
+    const int tid = threadIdx.x;
+    const int64_t T = a.T, C = a.C;
+    const int64_t s = blockIdx.x / a.nchunks;
+    const int64_t q0 = (blockIdx.x % a.nchunks) * a.P;
+    const int np = static_cast<int>((T - q0) < a.P ? (T - q0) : a.P);
+    const int64_t avail = T - q0;  // positions of this stream from q0 on
+    const int nw = static_cast<int>((np + k) < avail ? (np + k) : avail);
+    const KeyT* keys = static_cast<const KeyT*>(a.keys) + s * T;
+    const KeyT tmask = (static_cast<KeyT>(1) << a.tbits) - 1;
+    for (int i = tid; i < nw; i += 256) {
+        const KeyT key = keys[q0 + i];
+        wrow[i] = flat_row(s, static_cast<int64_t>(key & tmask), T, C);
+        wadr[i] = static_cast<uint64_t>(key >> a.tbits);
+    }
+    __syncthreads();
+
+    const uint32_t rv = static_cast<uint32_t>(a.row_bytes / VB);
+    const char* g = static_cast<const char*>(a.grad);
+    char* outp = static_cast<char*>(a.out);
+    for (uint32_t e = tid; e < static_cast<uint32_t>(np) * rv; e += 256) {
+        uint32_t i, v;
+        a.fd_rv.divmod(e, i, v);
+        Acc acc[EPV];
+#pragma unroll
+        for (int x = 0; x < EPV; ++x) acc[x] = Acc(0);
+        const uint64_t my = wadr[i];
+        for (int j = 0; j < k; ++j) {
+            const int wi = static_cast<int>(i) + 1 + j;
+            if (wi >= nw || wadr[wi] != my) break;  // segments are contiguous
+            const uint4 raw = ldg_vec<VB>(g + (wrow[wi] * k + j) * a.row_bytes + v * VB);
+            const V* vals = reinterpret_cast<const V*>(&raw);
+#pragma unroll
+            for (int x = 0; x < EPV; ++x) acc[x] += E::to_acc(vals[x]);
+        }
+        uint4 packed = make_uint4(0u, 0u, 0u, 0u);
+        V* pv = reinterpret_cast<V*>(&packed);
+#pragma unroll
+        for (int x = 0; x < EPV; ++x) pv[x] = E::from_acc(acc[x]);
+        st_vec<VB>(outp + wrow[i] * a.row_bytes + v * VB, packed);
+    }
+}
+
+inline size_t lk_bwd_fast_smem(int P, int64_t k) { return static_cast<size_t>(P + k) * 16; }
+
+// ------------------------------------------------------------------ general forward
+// One thread per (read, slot, vector); reads in their original order.
+template <typename KeyT>
+__device__ __forceinline__ void general_candidate(const LkArgs& a, int64_t r, int j, int64_t& row, bool& valid) {
+    const int64_t T = a.T, C = a.C;
+    const int64_t c = r % C, b = r / (C * T);
+    const int64_t s = b * C + c;
+    const KeyT* keys = static_cast<const KeyT*>(a.keys);
+    const KeyT tmask = (static_cast<KeyT>(1) << a.tbits) - 1;
+    const int64_t S = a.B * C;
+    if (a.soff[S] == 0) { row = -1; valid = false; return; }  // ravel_memory.py:146-149
+    const int64_t q = static_cast<int64_t>(a.ridx[r]) - j;
+    if (q >= 0) {
+        const KeyT key = keys[s * T + q];
+        const uint64_t ra = fold_addr(load_addr(a.raddr, r, a.addr_i64), a.A, a.key32);
+        valid = static_cast<uint64_t>(key >> a.tbits) == ra;
+        row = flat_row(s, static_cast<int64_t>(key & tmask), T, C);
+        return;
+    }
+    // Candidate before this stream in the global sorted order (always invalid):
+    // the stream s2 with soff[s2] <= gpos < soff[s2+1] (non-empty by construction).
+    int64_t gpos = a.soff[s] + q;
+    if (gpos < 0) gpos = 0;
+    int64_t lo = 0, hi = S - 1;
+    while (lo < hi) {  // last s2 with soff[s2] <= gpos
+        const int64_t mid = (lo + hi + 1) >> 1;
+        if (a.soff[mid] <= gpos) lo = mid; else hi = mid - 1;
+    }
+    const int64_t s2 = lo;
+    const KeyT key = keys[s2 * T + (gpos - a.soff[s2])];
+    row = flat_row(s2, static_cast<int64_t>(key & tmask), T, C);
+    valid = false;
+}
+
+template <typename KeyT, int DT, int VB>
+__global__ void __launch_bounds__(256) k_lk_fwd_general(LkArgs a, int64_t reads_per_cta) {
+    __shared__ int64_t srow[512];
+    __shared__ uint8_t sval[512];
+    const int k = static_cast<int>(a.k);
+    const int64_t N = a.B * a.T * a.C;
+    const int64_t r0 = blockIdx.x * reads_per_cta;
+    const int nr = static_cast<int>((N - r0) < reads_per_cta ? (N - r0) : reads_per_cta);
+    const int ns = nr * k;  // <= 512
+    for (int e = threadIdx.x; e < ns; e += 256) {
+        int64_t row; bool valid;
+        general_candidate<KeyT>(a, r0 + e / k, e % k, row, valid);
+        srow[e] = row;
+        sval[e] = valid;
+        a.out_mask[r0 * k + e] = valid ? 1 : 0;
+    }
+    __syncthreads();
+    const uint32_t rv = static_cast<uint32_t>(a.row_bytes / VB);
+    const char* pay = static_cast<const char*>(a.payload);
+    char* outv = static_cast<char*>(a.out) + r0 * k * a.row_bytes;
+    for (uint32_t e = threadIdx.x; e < static_cast<uint32_t>(ns) * rv; e += 256) {
+        uint32_t sl, v;
+        a.fd_rv.divmod(e, sl, v);
+        const int64_t row = srow[sl];
+        uint4 x = make_uint4(0u, 0u, 0u, 0u);
+        if (row >= 0) {
+            x = ldg_vec<VB>(pay + row * a.row_bytes + v * VB);
+            if (!sval[sl]) x = VecZero<DT, VB>::apply(x);
+        }
+        st_vec_stream<VB>(outv + static_cast<int64_t>(sl) * a.row_bytes + v * VB, x);
+    }
+}
+
+// ------------------------------------------------------------------ general backward
+// atomicAdd of grad_vals into an accumulator [N, D] (float, or double for
+// float64); the accumulator is the output itself for float32 / float64.
+template <typename KeyT, int DT>
+__global__ void __launch_bounds__(256) k_lk_bwd_general(LkArgs a, int64_t reads_per_cta) {
+    using E = Elem<DT>;
+    using Acc = typename E::Acc;
+    using V = typename E::T;
+    __shared__ int64_t srow[512];
+    const int k = static_cast<int>(a.k);
+    const int64_t N = a.B * a.T * a.C;
+    const int64_t r0 = blockIdx.x * reads_per_cta;
+    const int nr = static_cast<int>((N - r0) < reads_per_cta ? (N - r0) : reads_per_cta);
+    const int ns = nr * k;
+    for (int e = threadIdx.x; e < ns; e += 256) {
+        int64_t row; bool valid;
+        general_candidate<KeyT>(a, r0 + e / k, e % k, row, valid);
+        srow[e] = valid ? row : -1;
+    }
+    __syncthreads();
+    const int64_t D = a.D;
+    const V* g = static_cast<const V*>(a.grad) + r0 * k * D;
+    Acc* acc = static_cast<Acc*>(a.out);
+    const bool vec4 = (DT == RAVEL_F32) && (D % 4 == 0);
+    if (vec4) {
+        const uint32_t d4 = static_cast<uint32_t>(D / 4);
+        for (uint32_t e = threadIdx.x; e < static_cast<uint32_t>(ns) * d4; e += 256) {
+            const uint32_t sl = e / d4, v = e % d4;
+            const int64_t row = srow[sl];
+            if (row < 0) continue;
+            const float4 x = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(g) + sl * D + v * 4);
+            atomicAdd(reinterpret_cast<float4*>(reinterpret_cast<float*>(acc) + row * D + v * 4), x);
+        }
+    } else {
+        for (uint32_t e = threadIdx.x; e < static_cast<uint32_t>(ns * D); e += 256) {
+            const uint32_t sl = e / static_cast<uint32_t>(D), d = e % static_cast<uint32_t>(D);
+            const int64_t row = srow[sl];
+            if (row < 0) continue;
+            atomicAdd(acc + row * D + d, E::to_acc(g[static_cast<int64_t>(sl) * D + d]));
+        }
+    }
+}
+
+// Convert a float accumulator [n] to the payload dtype.
+template <int DT>
+__global__ void k_acc_to_dtype(const float* __restrict__ acc, typename Elem<DT>::T* __restrict__ out, int64_t n) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        out[i] = Elem<DT>::from_acc(acc[i]);
+}
+
+}  // namespace ravel

@@ -1,0 +1,729 @@
+// ravel_b200.cu -- C ABI of the RAVEL event-memory operator for B200 (sm_100a).
+//
+// Entry points are declared (and their reference counterparts cited) in
+// include/ravel_b200.h.  This file holds argument validation, the tape and
+// scratch layouts, and the launch plumbing; the kernels live in the headers.
+#include <atomic>
+#include <cstring>
+#include <type_traits>
+
+#include "common.cuh"
+#include "sort.cuh"
+#include "latestk.cuh"
+#include "segsum.cuh"
+#include "cache.cuh"
+
+namespace ravel {
+namespace {
+
+// ------------------------------------------------------------------ layouts
+struct TapeLayout {
+    KeyLayout kl;
+    int general;            // reads use the search path
+    int has_mask;
+    size_t key_bytes;
+    size_t off_keys, off_nvalid, off_soff, off_ridx, total;
+};
+
+TapeLayout tape_layout(int64_t B, int64_t T, int64_t C, int64_t A, int flags) {
+    TapeLayout t;
+    t.has_mask = (flags & RAVEL_TAPE_WRITE_MASK) ? 1 : 0;
+    t.general = flags != 0 ? 1 : 0;
+    t.kl = key_layout(T, A, t.has_mask);
+    t.key_bytes = t.kl.key64 ? 8 : 4;
+    const size_t S = static_cast<size_t>(B * C), N = static_cast<size_t>(B * T * C);
+    t.off_keys = 0;
+    t.off_nvalid = align_up(S * static_cast<size_t>(T) * t.key_bytes);
+    t.off_soff = t.off_nvalid + align_up(S * 4);
+    t.off_ridx = t.off_soff + align_up((S + 1) * 8);
+    t.total = t.off_ridx + (t.general ? align_up(N * 4) : 0);
+    return t;
+}
+
+struct TapeView {
+    void* keys;
+    int* nvalid;       // null unless a mask is present
+    int64_t* soff;
+    int32_t* ridx;
+};
+
+TapeView tape_view(const void* tape, const TapeLayout& t) {
+    char* base = static_cast<char*>(const_cast<void*>(tape));
+    TapeView v;
+    v.keys = base + t.off_keys;
+    v.nvalid = t.has_mask ? reinterpret_cast<int*>(base + t.off_nvalid) : nullptr;
+    v.soff = reinterpret_cast<int64_t*>(base + t.off_soff);
+    v.ridx = t.general ? reinterpret_cast<int32_t*>(base + t.off_ridx) : nullptr;
+    return v;
+}
+
+// tile sort configuration for a stream length T
+struct SortPlan {
+    int threads;
+    int64_t tiles;
+    int merge_passes;
+};
+
+SortPlan sort_plan(int64_t T) {
+    SortPlan p;
+    const int64_t tile_cap = 8192;
+    int threads = 32;
+    while (threads < 1024 && static_cast<int64_t>(threads) * 8 < T) threads *= 2;
+    p.threads = threads;
+    const int64_t tile = static_cast<int64_t>(threads) * 8;
+    p.tiles = T <= tile ? 1 : (T + tile_cap - 1) / tile_cap;
+    p.merge_passes = 0;
+    while ((int64_t(1) << p.merge_passes) < p.tiles) ++p.merge_passes;
+    return p;
+}
+
+int acc_bytes(int dtype) { return dtype == RAVEL_F64 ? 8 : 4; }
+
+struct ScanPlan {
+    int P, parts;
+    int64_t nchunks;
+};
+
+ScanPlan scan_plan(int64_t T, int64_t D, int dtype) {
+    ScanPlan s;
+    const int64_t per = (D > 0 ? D : 1) * acc_bytes(dtype);
+    int64_t P = 32768 / per;
+    if (P > 256) P = 256;
+    if (P < 16) P = 16;
+    P -= P % 8;
+    s.P = static_cast<int>(P);
+    const int ncol = D < 1 ? 1 : (D < SCAN_THREADS ? static_cast<int>(D) : SCAN_THREADS);
+    int parts = SCAN_THREADS / ncol;
+    if (parts < 1) parts = 1;
+    if (parts > s.P) parts = s.P;
+    s.parts = parts;
+    s.nchunks = (T + s.P - 1) / s.P;
+    return s;
+}
+
+struct ScratchLayout {
+    size_t off_sort, off_flags, off_ticket, off_agg, off_incl, off_big, total;
+};
+
+ScratchLayout scratch_layout(int64_t B, int64_t T, int64_t C, int64_t D, int64_t A, int dtype, int flags) {
+    ScratchLayout l;
+    const TapeLayout t = tape_layout(B, T, C, A, flags);
+    const SortPlan sp = sort_plan(T);
+    const ScanPlan sc = scan_plan(T, D, dtype);
+    const size_t S = static_cast<size_t>(B * C), N = static_cast<size_t>(B * T * C);
+    const size_t nch = S * static_cast<size_t>(sc.nchunks);
+    const size_t ab = static_cast<size_t>(acc_bytes(dtype));
+    l.off_sort = 0;
+    l.off_flags = align_up(sp.tiles > 1 ? S * static_cast<size_t>(T) * t.key_bytes : 0);
+    l.off_ticket = l.off_flags + align_up(nch * 4);
+    l.off_agg = l.off_ticket + 256;
+    l.off_incl = l.off_agg + align_up(nch * static_cast<size_t>(D) * ab);
+    l.off_big = l.off_incl + align_up(nch * static_cast<size_t>(D) * ab);
+    l.total = l.off_big + (t.general ? align_up(N * static_cast<size_t>(D) * ab) : 0);
+    return l;
+}
+
+// ------------------------------------------------------------------ dispatch helpers
+template <int V> using IC = std::integral_constant<int, V>;
+
+template <typename F>
+int with_key(int key64, F&& f) {
+    return key64 ? f(uint64_t(0)) : f(uint32_t(0));
+}
+
+template <typename F>
+int with_dtype(int dt, F&& f) {
+    switch (dt) {
+        case RAVEL_F32: return f(IC<RAVEL_F32>{});
+        case RAVEL_BF16: return f(IC<RAVEL_BF16>{});
+        case RAVEL_F16: return f(IC<RAVEL_F16>{});
+        case RAVEL_F64: return f(IC<RAVEL_F64>{});
+        default: return RAVEL_ERR_INVALID_ARG;
+    }
+}
+
+template <typename F>
+int with_vb(int vb, F&& f) {
+    switch (vb) {
+        case 16: return f(IC<16>{});
+        case 8: return f(IC<8>{});
+        case 4: return f(IC<4>{});
+        default: return f(IC<2>{});
+    }
+}
+
+// Vector widths that can occur for a dtype (a row is a whole number of elements).
+template <int DT, int VB>
+constexpr bool vb_ok() {
+    return (DT == RAVEL_F64) ? (VB >= 8) : (DT == RAVEL_F32 ? VB >= 4 : true);
+}
+
+std::atomic<uint64_t> g_launches{0};
+
+// Called once after every kernel launch of this library.
+int check_launch() {
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? RAVEL_OK : RAVEL_ERR_CUDA;
+}
+
+template <typename K>
+int set_smem(K kernel, size_t bytes) {
+    if (bytes <= 48 * 1024) return RAVEL_OK;
+    if (bytes > 227 * 1024) return RAVEL_ERR_UNSUPPORTED;
+    const cudaError_t e =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+    return e == cudaSuccess ? RAVEL_OK : RAVEL_ERR_CUDA;
+}
+
+uintptr_t addr_bits(const void* p) { return reinterpret_cast<uintptr_t>(p); }
+
+int grid_cap(int64_t blocks) {
+    const int64_t cap = 148 * 64;
+    return static_cast<int>(blocks < 1 ? 1 : (blocks > cap ? cap : blocks));
+}
+
+// ------------------------------------------------------------------ validation
+int check_sizes(int64_t B, int64_t T, int64_t C, int64_t D, int64_t A) {
+    if (B < 0 || T < 0 || C < 0 || D < 0) return RAVEL_ERR_INVALID_ARG;
+    if (A <= 0) return RAVEL_ERR_INVALID_ARG;
+    const KeyLayout kl = key_layout(T, A, 1);
+    if (kl.tbits + kl.abits + 1 > 64 || T > (int64_t(1) << 30)) return RAVEL_ERR_UNSUPPORTED;
+    const long double N = static_cast<long double>(B) * T * C;
+    if (N >= 2147483647.0L) return RAVEL_ERR_UNSUPPORTED;  // flat rows are packed in 32 bits
+    return RAVEL_OK;
+}
+
+int key32_of(int64_t B, int64_t T, int64_t C, int64_t A) {
+    const long double bound = static_cast<long double>(B) * C * A * (T + 1);
+    return bound <= 2147483647.0L ? 1 : 0;
+}
+
+// ------------------------------------------------------------------ tape build
+int tape_build(const void* waddr, const void* raddr, int addr_dtype, const uint8_t* wmask, int64_t B,
+               int64_t T, int64_t C, int64_t A, int flags, void* tape, size_t tape_bytes, void* scratch,
+               size_t scratch_bytes, cudaStream_t st) {
+    if (int e = check_sizes(B, T, C, 0, A)) return e;
+    if (addr_dtype != RAVEL_I32 && addr_dtype != RAVEL_I64) return RAVEL_ERR_INVALID_ARG;
+    if ((flags & RAVEL_TAPE_WRITE_MASK) && wmask == nullptr) return RAVEL_ERR_INVALID_ARG;
+    if ((flags & RAVEL_TAPE_GENERAL_READS) && raddr == nullptr) return RAVEL_ERR_INVALID_ARG;
+    const int64_t S = B * C, N = B * T * C;
+    if (N == 0) return RAVEL_OK;
+    if (waddr == nullptr || tape == nullptr) return RAVEL_ERR_INVALID_ARG;
+    const TapeLayout tl = tape_layout(B, T, C, A, flags);
+    const ScratchLayout sl = scratch_layout(B, T, C, 0, A, RAVEL_F32, flags);
+    if (tape_bytes < tl.total) return RAVEL_ERR_WORKSPACE;
+    const SortPlan sp = sort_plan(T);
+    if (sp.tiles > 1 && (scratch == nullptr || scratch_bytes < sl.off_flags)) return RAVEL_ERR_WORKSPACE;
+    const TapeView tv = tape_view(tape, tl);
+    if (tl.has_mask && cudaMemsetAsync(tv.nvalid, 0, S * sizeof(int), st) != cudaSuccess) return RAVEL_ERR_CUDA;
+
+    SortArgs a;
+    a.waddr = waddr;
+    a.wmask = tl.has_mask ? wmask : nullptr;
+    a.addr_i64 = addr_dtype == RAVEL_I64;
+    a.key32 = key32_of(B, T, C, A);
+    a.B = B; a.T = T; a.C = C; a.A = A;
+    a.tbits = tl.kl.tbits; a.abits = tl.kl.abits; a.mbit = tl.kl.mbit;
+    a.tiles = sp.tiles;
+    a.nvalid = tv.nvalid;
+    void* other = static_cast<char*>(scratch) + sl.off_sort;
+    void* first = (sp.merge_passes % 2 == 0) ? tv.keys : other;
+    a.keys_out = first;
+    const int64_t grid = B * sp.tiles * C;
+
+    int rc = with_key(tl.kl.key64, [&](auto kt) -> int {
+        using KeyT = decltype(kt);
+        auto launch = [&](auto th) -> int {
+            constexpr int TH = decltype(th)::value;
+            const size_t smem = tile_sort_smem<TH, 8, KeyT>();
+            if (int e = set_smem(k_tile_sort<KeyT, TH, 8>, smem)) return e;
+            k_tile_sort<KeyT, TH, 8><<<static_cast<unsigned>(grid), TH, smem, st>>>(a);
+            return check_launch();
+        };
+        int e;
+        switch (sp.threads) {
+            case 32: e = launch(IC<32>{}); break;
+            case 64: e = launch(IC<64>{}); break;
+            case 128: e = launch(IC<128>{}); break;
+            case 256: e = launch(IC<256>{}); break;
+            case 512: e = launch(IC<512>{}); break;
+            default: e = launch(IC<1024>{}); break;
+        }
+        if (e) return e;
+        const KeyT* src = static_cast<const KeyT*>(first);
+        int64_t run = static_cast<int64_t>(sp.threads) * 8;
+        const int64_t cps = (T + MERGE_OUT - 1) / MERGE_OUT;
+        for (int pass = 0; pass < sp.merge_passes; ++pass) {
+            KeyT* dst = (src == static_cast<const KeyT*>(tv.keys)) ? static_cast<KeyT*>(other)
+                                                                  : static_cast<KeyT*>(tv.keys);
+            k_merge<KeyT><<<static_cast<unsigned>(S * cps), MERGE_THREADS, 0, st>>>(src, dst, T, run, cps);
+            if (int e2 = check_launch()) return e2;
+            src = dst;
+            run *= 2;
+        }
+        if (tl.general) {
+            k_stream_offsets<<<1, 1024, 0, st>>>(tv.nvalid, tv.soff, S, T);
+            if (int e2 = check_launch()) return e2;
+            SearchArgs q;
+            q.keys = tv.keys;
+            q.nvalid = tv.nvalid;
+            q.raddr = (raddr != nullptr) ? raddr : waddr;
+            q.addr_i64 = a.addr_i64;
+            q.key32 = a.key32;
+            q.B = B; q.T = T; q.C = C; q.A = A;
+            q.tbits = tl.kl.tbits;
+            q.ridx = tv.ridx;
+            k_read_search<KeyT><<<grid_cap((N + 255) / 256), 256, 0, st>>>(q);
+            if (int e2 = check_launch()) return e2;
+        }
+        return RAVEL_OK;
+    });
+    return rc;
+}
+
+// ------------------------------------------------------------------ latest-k
+LkArgs lk_args(const TapeView& tv, const TapeLayout& tl, const void* raddr, int addr_dtype, int64_t B,
+               int64_t T, int64_t C, int64_t D, int64_t A, int64_t k, int dtype) {
+    LkArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.keys = tv.keys;
+    a.nvalid = tv.nvalid;
+    a.soff = tv.soff;
+    a.ridx = tv.ridx;
+    a.raddr = raddr;
+    a.addr_i64 = addr_dtype == RAVEL_I64;
+    a.key32 = key32_of(B, T, C, A);
+    a.B = B; a.T = T; a.C = C; a.D = D; a.A = A; a.k = k;
+    a.tbits = tl.kl.tbits;
+    a.row_bytes = D * elem_bytes(dtype);
+    return a;
+}
+
+int lk_fwd_tape(const void* tape, int flags, const void* raddr, int addr_dtype, const void* payload, int dtype,
+                int64_t B, int64_t T, int64_t C, int64_t D, int64_t A, int64_t k, void* out_vals,
+                uint8_t* out_mask, cudaStream_t st) {
+    if (int e = check_sizes(B, T, C, D, A)) return e;
+    if (k <= 0) return RAVEL_ERR_INVALID_ARG;
+    if (k > 512) return RAVEL_ERR_UNSUPPORTED;
+    if (dtype < 0 || dtype > 3) return RAVEL_ERR_INVALID_ARG;
+    const int64_t N = B * T * C;
+    if (N == 0) return RAVEL_OK;
+    if (tape == nullptr || out_mask == nullptr || (D > 0 && (payload == nullptr || out_vals == nullptr)))
+        return RAVEL_ERR_INVALID_ARG;
+    const TapeLayout tl = tape_layout(B, T, C, A, flags);
+    if (tl.general && raddr == nullptr) return RAVEL_ERR_INVALID_ARG;
+    const TapeView tv = tape_view(tape, tl);
+    LkArgs a = lk_args(tv, tl, raddr, addr_dtype, B, T, C, D, A, k, dtype);
+    a.payload = payload;
+    a.out = out_vals;
+    a.out_mask = out_mask;
+    const int vb = pick_vec_bytes(a.row_bytes, addr_bits(payload) | addr_bits(out_vals));
+    const int64_t rv = a.row_bytes / vb;
+    a.fd_rv = FastDiv(static_cast<uint32_t>(rv > 0 ? rv : 1));
+    a.fd_bv = FastDiv(static_cast<uint32_t>(rv * k > 0 ? rv * k : 1));
+    a.fd_k = FastDiv(static_cast<uint32_t>(k));
+    const int64_t S = B * C;
+    return with_key(tl.kl.key64, [&](auto kt) -> int {
+        using KeyT = decltype(kt);
+        return with_dtype(dtype, [&](auto dtc) -> int {
+            constexpr int DT = decltype(dtc)::value;
+            return with_vb(vb, [&](auto vbc) -> int {
+                constexpr int VB = decltype(vbc)::value;
+                if constexpr (!vb_ok<DT, VB>()) {
+                    return RAVEL_ERR_INVALID_ARG;
+                } else {
+                    if (!tl.general) {
+                        int64_t P = 40960 / (a.row_bytes + 16) - k;
+                        if (P > 128) P = 128;
+                        if (P < 16) P = 16;
+                        a.P = static_cast<int>(P);
+                        a.nchunks = (T + P - 1) / P;
+                        const size_t smem = lk_fast_smem(a.P, k, a.row_bytes);
+                        if (int e = set_smem(k_lk_fwd_fast<KeyT, DT, VB>, smem)) return e;
+                        k_lk_fwd_fast<KeyT, DT, VB><<<static_cast<unsigned>(S * a.nchunks), 256, smem, st>>>(a);
+                    } else {
+                        const int64_t rpc = 512 / k;
+                        k_lk_fwd_general<KeyT, DT, VB><<<static_cast<unsigned>((N + rpc - 1) / rpc), 256, 0, st>>>(a, rpc);
+                    }
+                    return check_launch();
+                }
+            });
+        });
+    });
+}
+
+int lk_bwd(const void* tape, int flags, const void* raddr, int addr_dtype, const void* grad_vals, int dtype,
+           int64_t B, int64_t T, int64_t C, int64_t D, int64_t A, int64_t k, void* grad_payload, void* scratch,
+           size_t scratch_bytes, cudaStream_t st) {
+    if (int e = check_sizes(B, T, C, D, A)) return e;
+    if (k <= 0) return RAVEL_ERR_INVALID_ARG;
+    if (k > 512) return RAVEL_ERR_UNSUPPORTED;
+    if (dtype < 0 || dtype > 3) return RAVEL_ERR_INVALID_ARG;
+    const int64_t N = B * T * C;
+    if (N == 0 || D == 0) return RAVEL_OK;
+    if (tape == nullptr || grad_vals == nullptr || grad_payload == nullptr) return RAVEL_ERR_INVALID_ARG;
+    const TapeLayout tl = tape_layout(B, T, C, A, flags);
+    if (tl.general && raddr == nullptr) return RAVEL_ERR_INVALID_ARG;
+    const TapeView tv = tape_view(tape, tl);
+    LkArgs a = lk_args(tv, tl, raddr, addr_dtype, B, T, C, D, A, k, dtype);
+    a.grad = grad_vals;
+    const int64_t S = B * C;
+    if (!tl.general) {
+        a.out = grad_payload;
+        const int vb = pick_vec_bytes(a.row_bytes, addr_bits(grad_vals) | addr_bits(grad_payload));
+        const int64_t rv = a.row_bytes / vb;
+        a.fd_rv = FastDiv(static_cast<uint32_t>(rv));
+        a.P = 128;
+        a.nchunks = (T + a.P - 1) / a.P;
+        return with_key(tl.kl.key64, [&](auto kt) -> int {
+            using KeyT = decltype(kt);
+            return with_dtype(dtype, [&](auto dtc) -> int {
+                constexpr int DT = decltype(dtc)::value;
+                return with_vb(vb, [&](auto vbc) -> int {
+                    constexpr int VB = decltype(vbc)::value;
+                    if constexpr (!vb_ok<DT, VB>()) {
+                        return RAVEL_ERR_INVALID_ARG;
+                    } else {
+                        const size_t smem = lk_bwd_fast_smem(a.P, k);
+                        k_lk_bwd_fast<KeyT, DT, VB><<<static_cast<unsigned>(S * a.nchunks), 256, smem, st>>>(a);
+                        return check_launch();
+                    }
+                });
+            });
+        });
+    }
+    // general: atomics into an accumulator
+    const ScratchLayout sl = scratch_layout(B, T, C, D, A, dtype, flags);
+    const bool direct = dtype == RAVEL_F32 || dtype == RAVEL_F64;
+    void* acc = grad_payload;
+    if (!direct) {
+        if (scratch == nullptr || scratch_bytes < sl.total) return RAVEL_ERR_WORKSPACE;
+        acc = static_cast<char*>(scratch) + sl.off_big;
+    }
+    const size_t acc_sz = static_cast<size_t>(N) * D * acc_bytes(dtype);
+    if (cudaMemsetAsync(acc, 0, acc_sz, st) != cudaSuccess) return RAVEL_ERR_CUDA;
+    a.out = acc;
+    const int64_t rpc = 512 / k;
+    return with_key(tl.kl.key64, [&](auto kt) -> int {
+        using KeyT = decltype(kt);
+        return with_dtype(dtype, [&](auto dtc) -> int {
+            constexpr int DT = decltype(dtc)::value;
+            k_lk_bwd_general<KeyT, DT><<<static_cast<unsigned>((N + rpc - 1) / rpc), 256, 0, st>>>(a, rpc);
+            if (int e = check_launch()) return e;
+            if constexpr (DT == RAVEL_BF16 || DT == RAVEL_F16) {
+                const int64_t n = N * D;
+                k_acc_to_dtype<DT><<<grid_cap((n + 255) / 256), 256, 0, st>>>(
+                    static_cast<const float*>(acc), static_cast<typename Elem<DT>::T*>(grad_payload), n);
+                return check_launch();
+            } else {
+                return RAVEL_OK;
+            }
+        });
+    });
+}
+
+// ------------------------------------------------------------------ segmented sum
+template <typename KeyT, int DT>
+int launch_segscan(const TapeView& tv, const TapeLayout& tl, int64_t B, int64_t T, int64_t C, int64_t D,
+                   const void* in, int in_sorted, void* out, int out_sorted, uint8_t* out_mask, int inclusive,
+                   int reverse, void* scratch, const ScratchLayout& sl, cudaStream_t st) {
+    using Acc = typename Elem<DT>::Acc;
+    const ScanPlan sp = scan_plan(T, D, DT);
+    ScanArgs<Acc> a;
+    a.keys = tv.keys;
+    a.nvalid = tv.nvalid;
+    a.B = B; a.T = T; a.C = C; a.D = D;
+    a.tbits = tl.kl.tbits;
+    a.in = in; a.out = out; a.out_mask = out_mask;
+    a.in_sorted = in_sorted; a.out_sorted = out_sorted; a.inclusive = inclusive; a.reverse = reverse;
+    a.P = sp.P; a.parts = sp.parts; a.nchunks = sp.nchunks;
+    char* sc = static_cast<char*>(scratch);
+    a.flags = reinterpret_cast<unsigned*>(sc + sl.off_flags);
+    a.ticket = reinterpret_cast<unsigned*>(sc + sl.off_ticket);
+    a.agg = reinterpret_cast<Acc*>(sc + sl.off_agg);
+    a.incl = reinterpret_cast<Acc*>(sc + sl.off_incl);
+    a.fd_d = FastDiv(static_cast<uint32_t>(D > 0 ? D : 1));
+    const int64_t nch = B * C * sp.nchunks;
+    if (cudaMemsetAsync(a.flags, 0, sl.off_agg - sl.off_flags, st) != cudaSuccess) return RAVEL_ERR_CUDA;
+    const size_t smem = segscan_smem<Acc>(sp.P, sp.parts, D);
+    constexpr int EPV = 16 / sizeof(typename Elem<DT>::T);
+    const bool vec = !in_sorted && !out_sorted && D % EPV == 0 && (addr_bits(in) % 16 == 0) &&
+                     (addr_bits(out) % 16 == 0);
+    const bool vec_in_only = false;
+    (void)vec_in_only;
+    if (vec) {
+        if (int e = set_smem(k_segscan<KeyT, DT, true>, smem)) return e;
+        k_segscan<KeyT, DT, true><<<static_cast<unsigned>(nch), SCAN_THREADS, smem, st>>>(a);
+    } else {
+        if (int e = set_smem(k_segscan<KeyT, DT, false>, smem)) return e;
+        k_segscan<KeyT, DT, false><<<static_cast<unsigned>(nch), SCAN_THREADS, smem, st>>>(a);
+    }
+    return check_launch();
+}
+
+int ss_fwd_tape(const void* tape, int flags, const void* raddr, int addr_dtype, const void* payload, int dtype,
+                int64_t B, int64_t T, int64_t C, int64_t D, int64_t A, void* out_sums, uint8_t* out_mask,
+                void* scratch, size_t scratch_bytes, cudaStream_t st) {
+    if (int e = check_sizes(B, T, C, D, A)) return e;
+    if (dtype < 0 || dtype > 3) return RAVEL_ERR_INVALID_ARG;
+    const int64_t N = B * T * C;
+    if (N == 0) return RAVEL_OK;
+    if (tape == nullptr || out_mask == nullptr || (D > 0 && (payload == nullptr || out_sums == nullptr)))
+        return RAVEL_ERR_INVALID_ARG;
+    const TapeLayout tl = tape_layout(B, T, C, A, flags);
+    if (tl.general && raddr == nullptr) return RAVEL_ERR_INVALID_ARG;
+    const ScratchLayout sl = scratch_layout(B, T, C, D, A, dtype, flags);
+    if (scratch == nullptr || scratch_bytes < sl.total) return RAVEL_ERR_WORKSPACE;
+    const TapeView tv = tape_view(tape, tl);
+    return with_key(tl.kl.key64, [&](auto kt) -> int {
+        using KeyT = decltype(kt);
+        return with_dtype(dtype, [&](auto dtc) -> int {
+            constexpr int DT = decltype(dtc)::value;
+            if (!tl.general) {
+                return launch_segscan<KeyT, DT>(tv, tl, B, T, C, D, payload, 0, out_sums, 0, out_mask,
+                                                /*inclusive=*/0, /*reverse=*/0, scratch, sl, st);
+            }
+            void* tapebuf = static_cast<char*>(scratch) + sl.off_big;
+            if (int e = launch_segscan<KeyT, DT>(tv, tl, B, T, C, D, payload, 0, tapebuf, 1, nullptr, 1, 0,
+                                                 scratch, sl, st))
+                return e;
+            SsGenArgs g;
+            std::memset(&g, 0, sizeof(g));
+            g.keys = tv.keys; g.soff = tv.soff; g.ridx = tv.ridx;
+            g.raddr = raddr;
+            g.addr_i64 = addr_dtype == RAVEL_I64;
+            g.key32 = key32_of(B, T, C, A);
+            g.B = B; g.T = T; g.C = C; g.D = D; g.A = A;
+            g.tbits = tl.kl.tbits;
+            g.tapebuf = tapebuf;
+            g.out = out_sums;
+            g.out_mask = out_mask;
+            k_ss_gather<KeyT, DT><<<grid_cap((N * 32 + 255) / 256), 256, 0, st>>>(g);
+            return check_launch();
+        });
+    });
+}
+
+int ss_bwd(const void* tape, int flags, const void* raddr, int addr_dtype, const void* grad_sums, int dtype,
+           int64_t B, int64_t T, int64_t C, int64_t D, int64_t A, void* grad_payload, void* scratch,
+           size_t scratch_bytes, cudaStream_t st) {
+    if (int e = check_sizes(B, T, C, D, A)) return e;
+    if (dtype < 0 || dtype > 3) return RAVEL_ERR_INVALID_ARG;
+    const int64_t N = B * T * C;
+    if (N == 0 || D == 0) return RAVEL_OK;
+    if (tape == nullptr || grad_sums == nullptr || grad_payload == nullptr) return RAVEL_ERR_INVALID_ARG;
+    const TapeLayout tl = tape_layout(B, T, C, A, flags);
+    if (tl.general && raddr == nullptr) return RAVEL_ERR_INVALID_ARG;
+    const ScratchLayout sl = scratch_layout(B, T, C, D, A, dtype, flags);
+    if (scratch == nullptr || scratch_bytes < sl.total) return RAVEL_ERR_WORKSPACE;
+    const TapeView tv = tape_view(tape, tl);
+    return with_key(tl.kl.key64, [&](auto kt) -> int {
+        using KeyT = decltype(kt);
+        return with_dtype(dtype, [&](auto dtc) -> int {
+            constexpr int DT = decltype(dtc)::value;
+            if (!tl.general) {
+                return launch_segscan<KeyT, DT>(tv, tl, B, T, C, D, grad_sums, 0, grad_payload, 0, nullptr,
+                                                /*inclusive=*/0, /*reverse=*/1, scratch, sl, st);
+            }
+            void* accbuf = static_cast<char*>(scratch) + sl.off_big;
+            const size_t acc_sz = static_cast<size_t>(B * C * T) * D * acc_bytes(DT);
+            if (cudaMemsetAsync(accbuf, 0, acc_sz, st) != cudaSuccess) return RAVEL_ERR_CUDA;
+            if (tl.has_mask &&
+                cudaMemsetAsync(grad_payload, 0, static_cast<size_t>(N) * D * elem_bytes(DT), st) != cudaSuccess)
+                return RAVEL_ERR_CUDA;
+            SsGenArgs g;
+            std::memset(&g, 0, sizeof(g));
+            g.keys = tv.keys; g.soff = tv.soff; g.ridx = tv.ridx;
+            g.raddr = raddr;
+            g.addr_i64 = addr_dtype == RAVEL_I64;
+            g.key32 = key32_of(B, T, C, A);
+            g.B = B; g.T = T; g.C = C; g.D = D; g.A = A;
+            g.tbits = tl.kl.tbits;
+            g.accbuf = accbuf;
+            g.grad = grad_sums;
+            k_ss_scatter<KeyT, DT><<<grid_cap((N * 32 + 255) / 256), 256, 0, st>>>(g);
+            if (int e = check_launch()) return e;
+            return launch_segscan<KeyT, DT>(tv, tl, B, T, C, D, accbuf, 1, grad_payload, 0, nullptr, 1, 1,
+                                            scratch, sl, st);
+        });
+    });
+}
+
+// ------------------------------------------------------------------ decode cache
+int cache_op(void* values, uint8_t* filled, const void* raddr, const void* waddr, int addr_dtype,
+             const void* payload, int dtype, int64_t B, int64_t C, int64_t A, int64_t D, void* out_vals,
+             uint8_t* out_mask, cudaStream_t st) {
+    if (B < 0 || C < 0 || D < 0 || A <= 0) return RAVEL_ERR_INVALID_ARG;
+    if (addr_dtype != RAVEL_I32 && addr_dtype != RAVEL_I64) return RAVEL_ERR_INVALID_ARG;
+    if (dtype < 0 || dtype > 3) return RAVEL_ERR_INVALID_ARG;
+    const int64_t pairs = B * C;
+    if (pairs == 0) return RAVEL_OK;
+    if (values == nullptr || filled == nullptr) return RAVEL_ERR_INVALID_ARG;
+    if (raddr != nullptr && (out_mask == nullptr || (D > 0 && out_vals == nullptr))) return RAVEL_ERR_INVALID_ARG;
+    if (waddr != nullptr && D > 0 && payload == nullptr) return RAVEL_ERR_INVALID_ARG;
+    CacheArgs a;
+    a.values = values; a.filled = filled; a.raddr = raddr; a.waddr = waddr;
+    a.addr_i64 = addr_dtype == RAVEL_I64;
+    a.payload = payload; a.out_vals = out_vals; a.out_mask = out_mask;
+    a.pairs = pairs; a.A = A;
+    a.row_bytes = D * elem_bytes(dtype);
+    const int vb = pick_vec_bytes(a.row_bytes, addr_bits(values) | addr_bits(payload) | addr_bits(out_vals));
+    const int64_t rv = a.row_bytes / vb;
+    int64_t ppc = rv > 0 ? 256 / rv : 256;
+    if (ppc < 1) ppc = 1;
+    a.pairs_per_cta = static_cast<int>(ppc);
+    a.fd_rv = FastDiv(static_cast<uint32_t>(rv > 0 ? rv : 1));
+    const unsigned grid = static_cast<unsigned>((pairs + ppc - 1) / ppc);
+    return with_dtype(dtype, [&](auto dtc) -> int {
+        constexpr int DT = decltype(dtc)::value;
+        return with_vb(vb, [&](auto vbc) -> int {
+            constexpr int VB = decltype(vbc)::value;
+            if constexpr (!vb_ok<DT, VB>()) {
+                return RAVEL_ERR_INVALID_ARG;
+            } else {
+                k_cache_step<DT, VB><<<grid, 256, 0, st>>>(a);
+                return check_launch();
+            }
+        });
+    });
+}
+
+__global__ void k_clear_error() { g_error_word = 0u; }
+
+}  // namespace
+}  // namespace ravel
+
+using namespace ravel;
+
+extern "C" {
+
+size_t ravel_tape_bytes(int64_t B, int64_t T, int64_t C, int64_t A, int tape_flags) {
+    if (B < 0 || T < 0 || C < 0 || A <= 0) return 0;
+    return tape_layout(B, T, C, A, tape_flags).total;
+}
+
+size_t ravel_scratch_bytes(int64_t B, int64_t T, int64_t C, int64_t D, int64_t A, int64_t k, int tape_flags) {
+    (void)k;
+    if (B < 0 || T < 0 || C < 0 || D < 0 || A <= 0) return 0;
+    // float64 accumulators bound every dtype
+    return scratch_layout(B, T, C, D, A, RAVEL_F64, tape_flags).total;
+}
+
+int ravel_tape_build(const void* waddr, const void* raddr, int addr_dtype, const uint8_t* wmask, int64_t B,
+                     int64_t T, int64_t C, int64_t A, int tape_flags, void* tape, size_t tape_bytes,
+                     void* scratch, size_t scratch_bytes, void* stream) {
+    return tape_build(waddr, raddr, addr_dtype, wmask, B, T, C, A, tape_flags, tape, tape_bytes, scratch,
+                      scratch_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int ravel_latestk_fwd_tape(const void* tape, int tape_flags, const void* raddr, int addr_dtype,
+                           const void* payload, int dtype, int64_t B, int64_t T, int64_t C, int64_t D,
+                           int64_t A, int64_t k, void* out_vals, uint8_t* out_mask, void* stream) {
+    return lk_fwd_tape(tape, tape_flags, raddr, addr_dtype, payload, dtype, B, T, C, D, A, k, out_vals, out_mask,
+                       static_cast<cudaStream_t>(stream));
+}
+
+int ravel_latestk_fwd(const void* waddr, const void* raddr, int addr_dtype, const uint8_t* wmask,
+                      const void* payload, int dtype, int64_t B, int64_t T, int64_t C, int64_t D, int64_t A,
+                      int64_t k, void* out_vals, uint8_t* out_mask, void* tape, size_t tape_bytes,
+                      void* scratch, size_t scratch_bytes, void* stream) {
+    if (raddr == waddr) raddr = nullptr;
+    const int flags = (raddr ? RAVEL_TAPE_GENERAL_READS : 0) | (wmask ? RAVEL_TAPE_WRITE_MASK : 0);
+    if (k <= 0) return RAVEL_ERR_INVALID_ARG;
+    if (int e = tape_build(waddr, raddr, addr_dtype, wmask, B, T, C, A, flags, tape, tape_bytes, scratch,
+                           scratch_bytes, static_cast<cudaStream_t>(stream)))
+        return e;
+    return lk_fwd_tape(tape, flags, raddr ? raddr : waddr, addr_dtype, payload, dtype, B, T, C, D, A, k,
+                       out_vals, out_mask, static_cast<cudaStream_t>(stream));
+}
+
+int ravel_latestk_bwd(const void* tape, int tape_flags, const void* raddr, int addr_dtype, const void* grad_vals,
+                      int dtype, int64_t B, int64_t T, int64_t C, int64_t D, int64_t A, int64_t k,
+                      void* grad_payload, void* scratch, size_t scratch_bytes, void* stream) {
+    return lk_bwd(tape, tape_flags, raddr, addr_dtype, grad_vals, dtype, B, T, C, D, A, k, grad_payload, scratch,
+                  scratch_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int ravel_segsum_fwd_tape(const void* tape, int tape_flags, const void* raddr, int addr_dtype,
+                          const void* payload, int dtype, int64_t B, int64_t T, int64_t C, int64_t D, int64_t A,
+                          void* out_sums, uint8_t* out_mask, void* scratch, size_t scratch_bytes, void* stream) {
+    return ss_fwd_tape(tape, tape_flags, raddr, addr_dtype, payload, dtype, B, T, C, D, A, out_sums, out_mask,
+                       scratch, scratch_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int ravel_segsum_fwd(const void* waddr, const void* raddr, int addr_dtype, const uint8_t* wmask,
+                     const void* payload, int dtype, int64_t B, int64_t T, int64_t C, int64_t D, int64_t A,
+                     void* out_sums, uint8_t* out_mask, void* tape, size_t tape_bytes, void* scratch,
+                     size_t scratch_bytes, void* stream) {
+    if (raddr == waddr) raddr = nullptr;
+    const int flags = (raddr ? RAVEL_TAPE_GENERAL_READS : 0) | (wmask ? RAVEL_TAPE_WRITE_MASK : 0);
+    if (int e = tape_build(waddr, raddr, addr_dtype, wmask, B, T, C, A, flags, tape, tape_bytes, scratch,
+                           scratch_bytes, static_cast<cudaStream_t>(stream)))
+        return e;
+    return ss_fwd_tape(tape, flags, raddr ? raddr : waddr, addr_dtype, payload, dtype, B, T, C, D, A, out_sums,
+                       out_mask, scratch, scratch_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int ravel_segsum_bwd(const void* tape, int tape_flags, const void* raddr, int addr_dtype, const void* grad_sums,
+                     int dtype, int64_t B, int64_t T, int64_t C, int64_t D, int64_t A, void* grad_payload,
+                     void* scratch, size_t scratch_bytes, void* stream) {
+    return ss_bwd(tape, tape_flags, raddr, addr_dtype, grad_sums, dtype, B, T, C, D, A, grad_payload, scratch,
+                  scratch_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int ravel_cache_read(const void* values, const uint8_t* filled, const void* addr, int addr_dtype, int dtype,
+                     int64_t B, int64_t C, int64_t A, int64_t D, void* out_vals, uint8_t* out_mask, void* stream) {
+    if (addr == nullptr) return RAVEL_ERR_INVALID_ARG;
+    return cache_op(const_cast<void*>(values), const_cast<uint8_t*>(filled), addr, nullptr, addr_dtype, nullptr,
+                    dtype, B, C, A, D, out_vals, out_mask, static_cast<cudaStream_t>(stream));
+}
+
+int ravel_cache_write(void* values, uint8_t* filled, const void* addr, int addr_dtype, const void* payload,
+                      int dtype, int64_t B, int64_t C, int64_t A, int64_t D, void* stream) {
+    if (addr == nullptr) return RAVEL_ERR_INVALID_ARG;
+    return cache_op(values, filled, nullptr, addr, addr_dtype, payload, dtype, B, C, A, D, nullptr, nullptr,
+                    static_cast<cudaStream_t>(stream));
+}
+
+int ravel_cache_step(void* values, uint8_t* filled, const void* raddr, const void* waddr, int addr_dtype,
+                     const void* payload, int dtype, int64_t B, int64_t C, int64_t A, int64_t D, void* out_vals,
+                     uint8_t* out_mask, void* stream) {
+    if (raddr == nullptr || waddr == nullptr) return RAVEL_ERR_INVALID_ARG;
+    return cache_op(values, filled, raddr, waddr, addr_dtype, payload, dtype, B, C, A, D, out_vals, out_mask,
+                    static_cast<cudaStream_t>(stream));
+}
+
+int ravel_device_error(int* out, void* stream) {
+    if (out == nullptr) return RAVEL_ERR_INVALID_ARG;
+    unsigned int v = 0;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (cudaMemcpyFromSymbolAsync(&v, g_error_word, sizeof(v), 0, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+        return RAVEL_ERR_CUDA;
+    if (cudaStreamSynchronize(st) != cudaSuccess) return RAVEL_ERR_CUDA;
+    *out = static_cast<int>(v);
+    return RAVEL_OK;
+}
+
+int ravel_clear_device_error(void* stream) {
+    k_clear_error<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>();
+    return check_launch();
+}
+
+uint64_t ravel_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
+
+const char* ravel_status_string(int status) {
+    switch (status) {
+        case RAVEL_OK: return "ok";
+        case RAVEL_ERR_INVALID_ARG: return "invalid argument";
+        case RAVEL_ERR_WORKSPACE: return "tape or scratch buffer too small";
+        case RAVEL_ERR_CUDA: return "CUDA launch or runtime error";
+        case RAVEL_ERR_UNSUPPORTED: return "sizes beyond the supported range";
+        case RAVEL_ERR_DEVICE: return "a kernel reported an error";
+        default: return "unknown status";
+    }
+}
+
+const char* ravel_version(void) { return "ravel_b200 0.1.0 (sm_100a)"; }
+
+}  // extern "C"

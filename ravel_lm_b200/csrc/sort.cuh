@@ -1,0 +1,291 @@
+// sort.cuh -- per-stream event sort: the "tape" of RAVEL's event memory.
+//
+// The reference builds composite keys ((b*C + c)*A + addr)*(T+1) + t and calls
+// torch.sort on all B*T*C of them (ravel_lm/ravel_memory.py:126-151).  The stream
+// id (b, c) is the key's most significant part, so that global sort is the
+// concatenation of independent per-stream sorts.  Here every stream's events are
+// sorted on their own, as 32-bit keys (addr << tbits | t) when they fit (64-bit
+// otherwise), which needs far fewer radix digits than a global 64-bit key.
+//
+//   k_tile_sort   one CTA per (stream, tile of up to 8192 steps): loads and folds
+//                 the addresses, builds keys, and runs an LSD radix sort on the
+//                 address bits only (the input is time-ordered and the sort is
+//                 stable) in shared memory.  Ranking uses __match_any_sync per
+//                 warp, warp-private digit histograms and a block-wide scan.
+//   k_merge       merge-path merge of sorted runs for streams longer than a
+//                 tile (log2(tiles) passes, global memory ping-pong).
+//   k_read_search per read: lower bound of (addr, t) in its stream's sorted keys
+//                 = searchsorted(right=True)-1 of ravel_memory.py:159, restricted
+//                 to the stream.
+#pragma once
+
+#include "common.cuh"
+
+namespace ravel {
+
+struct SortArgs {
+    const void* waddr;
+    const uint8_t* wmask;  // [B, T] or null
+    int addr_i64;
+    int key32;             // reference key dtype is int32 (address truncation)
+    int64_t B, T, C, A;
+    int tbits, abits, mbit;
+    int64_t tiles;         // tiles per stream
+    void* keys_out;        // [S][T]
+    int* nvalid;           // [S], pre-zeroed, or null when there is no mask
+};
+
+template <typename KeyT, int THREADS, int ITEMS>
+__global__ void __launch_bounds__(THREADS) k_tile_sort(SortArgs a) {
+    constexpr int TILE = THREADS * ITEMS;
+    constexpr int NW = THREADS / 32;
+    extern __shared__ __align__(16) unsigned char smem[];
+    KeyT* ka = reinterpret_cast<KeyT*>(smem);
+    KeyT* kb = ka + TILE;
+    uint16_t* whist = reinterpret_cast<uint16_t*>(kb + TILE);
+    uint32_t* dbase = reinterpret_cast<uint32_t*>(whist + NW * 256);
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t C = a.C, T = a.T;
+    int64_t blk = blockIdx.x;
+    // c varies fastest so that the C streams of one (b, tile) read the same
+    // address sectors back to back (addresses are [B, T, C]).
+    const int64_t c = blk % C;
+    blk /= C;
+    const int64_t tile = blk % a.tiles;
+    const int64_t b = blk / a.tiles;
+    const int64_t s = b * C + c;
+    const int64_t t0 = tile * TILE;
+
+    int nvalid_local = 0;
+    for (int i = tid; i < TILE; i += THREADS) {
+        const int64_t t = t0 + i;
+        KeyT key;
+        if (t < T) {
+            const uint64_t ad = fold_addr(load_addr(a.waddr, (b * T + t) * C + c, a.addr_i64), a.A, a.key32);
+            const bool valid = a.wmask == nullptr || a.wmask[b * T + t] != 0;
+            if (valid) {
+                key = (static_cast<KeyT>(ad) << a.tbits) | static_cast<KeyT>(t);
+                ++nvalid_local;
+            } else {
+                // masked write: invalid bit above the address field, sorts last
+                key = (static_cast<KeyT>(1) << (a.tbits + a.abits)) | static_cast<KeyT>(t);
+            }
+        } else {
+            key = ~static_cast<KeyT>(0);  // tile padding: sorts after everything
+        }
+        ka[i] = key;
+    }
+    if (a.nvalid != nullptr) {
+        const int w = __reduce_add_sync(0xffffffffu, static_cast<unsigned>(nvalid_local));
+        if (lane == 0 && w) atomicAdd(a.nvalid + s, w);
+    }
+    __syncthreads();
+
+    const int top = a.tbits + a.abits + a.mbit;
+    for (int shift = a.tbits; shift < top; shift += 8) {
+        const int nb = (top - shift) < 8 ? (top - shift) : 8;
+        const unsigned dmask = (1u << nb) - 1u;
+        for (int d = lane; d < 256; d += 32) whist[warp * 256 + d] = 0;
+        __syncwarp();
+        KeyT kv[ITEMS];
+        uint16_t loc[ITEMS];
+        uint16_t dig[ITEMS];
+#pragma unroll
+        for (int it = 0; it < ITEMS; ++it) {
+            const int idx = warp * (32 * ITEMS) + it * 32 + lane;
+            const KeyT key = ka[idx];
+            const unsigned d = static_cast<unsigned>(key >> shift) & dmask;
+            const unsigned peers = __match_any_sync(0xffffffffu, d);
+            const unsigned rank = __popc(peers & lanemask_lt());
+            const unsigned before = whist[warp * 256 + d];
+            __syncwarp();
+            if (rank == 0) whist[warp * 256 + d] = static_cast<uint16_t>(before + __popc(peers));
+            __syncwarp();
+            kv[it] = key;
+            loc[it] = static_cast<uint16_t>(before + rank);
+            dig[it] = static_cast<uint16_t>(d);
+        }
+        __syncthreads();
+        // per digit: exclusive prefix over warps (warp order == time order)
+        for (int d = tid; d < 256; d += THREADS) {
+            uint32_t run = 0;
+#pragma unroll 4
+            for (int w = 0; w < NW; ++w) {
+                const uint32_t v = whist[w * 256 + d];
+                whist[w * 256 + d] = static_cast<uint16_t>(run);
+                run += v;
+            }
+            dbase[d] = run;
+        }
+        __syncthreads();
+        if (warp == 0) {  // exclusive scan of the 256 digit totals
+            uint32_t v[8];
+            uint32_t sum = 0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) { v[i] = dbase[lane * 8 + i]; sum += v[i]; }
+            uint32_t incl = sum;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t n = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += n;
+            }
+            uint32_t run = incl - sum;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) { dbase[lane * 8 + i] = run; run += v[i]; }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int it = 0; it < ITEMS; ++it) {
+            const uint32_t dst = dbase[dig[it]] + whist[warp * 256 + dig[it]] + loc[it];
+            kb[dst] = kv[it];
+        }
+        __syncthreads();
+        KeyT* tmp = ka; ka = kb; kb = tmp;
+    }
+
+    const int64_t cnt = (T - t0) < TILE ? (T - t0) : TILE;
+    KeyT* out = static_cast<KeyT*>(a.keys_out) + s * T + t0;
+    for (int i = tid; i < cnt; i += THREADS) out[i] = ka[i];
+}
+
+template <int THREADS, int ITEMS, typename KeyT>
+inline size_t tile_sort_smem() {
+    return 2 * sizeof(KeyT) * THREADS * ITEMS + sizeof(uint16_t) * (THREADS / 32) * 256 + 4 * 256;
+}
+
+// Number of elements of A among the first d outputs of merge(A, B) (unique keys).
+template <typename KeyT>
+__device__ __forceinline__ int64_t co_rank(const KeyT* A, int64_t la, const KeyT* Bk, int64_t lb, int64_t d) {
+    int64_t lo = d - lb > 0 ? d - lb : 0;
+    int64_t hi = d < la ? d : la;
+    while (lo < hi) {
+        const int64_t mid = (lo + hi) >> 1;
+        if (A[mid] < Bk[d - mid - 1]) lo = mid + 1; else hi = mid;
+    }
+    return lo;
+}
+
+constexpr int MERGE_THREADS = 256;
+constexpr int MERGE_ITEMS = 8;
+constexpr int MERGE_OUT = MERGE_THREADS * MERGE_ITEMS;  // divides every run length (>= 2048)
+
+// Merge pairs of sorted runs of length `run` within each stream.
+template <typename KeyT>
+__global__ void __launch_bounds__(MERGE_THREADS) k_merge(const KeyT* __restrict__ in, KeyT* __restrict__ out,
+                                                         int64_t T, int64_t run, int64_t ctas_per_stream) {
+    __shared__ KeyT sm[MERGE_OUT];
+    __shared__ KeyT so[MERGE_OUT];
+    __shared__ int64_t cr[2];
+    const int tid = threadIdx.x;
+    const int64_t s = blockIdx.x / ctas_per_stream;
+    const int64_t o0 = (blockIdx.x % ctas_per_stream) * MERGE_OUT;
+    if (o0 >= T) return;
+    const int64_t o1 = (o0 + MERGE_OUT) < T ? (o0 + MERGE_OUT) : T;
+    const int64_t ps = (o0 / (2 * run)) * (2 * run);
+    const int64_t a0 = ps, a1 = (ps + run) < T ? (ps + run) : T;
+    const int64_t b1 = (ps + 2 * run) < T ? (ps + 2 * run) : T;
+    const int64_t la = a1 - a0, lb = b1 - a1;
+    const KeyT* Ap = in + s * T + a0;
+    const KeyT* Bp = in + s * T + a1;
+    const int64_t d0 = o0 - ps, d1 = o1 - ps;
+    if (tid < 2) cr[tid] = co_rank(Ap, la, Bp, lb, tid ? d1 : d0);
+    __syncthreads();
+    const int64_t i0 = cr[0], i1 = cr[1];
+    const int64_t j0 = d0 - i0, j1 = d1 - i1;
+    const int na = static_cast<int>(i1 - i0), nb = static_cast<int>(j1 - j0);
+    for (int i = tid; i < na; i += MERGE_THREADS) sm[i] = Ap[i0 + i];
+    for (int i = tid; i < nb; i += MERGE_THREADS) sm[na + i] = Bp[j0 + i];
+    __syncthreads();
+    const int n = na + nb;
+    const int dd = tid * MERGE_ITEMS;
+    if (dd < n) {
+        int i = static_cast<int>(co_rank(sm, na, sm + na, nb, dd));
+        int j = dd - i;
+#pragma unroll
+        for (int e = 0; e < MERGE_ITEMS; ++e) {
+            if (dd + e >= n) break;
+            const bool takeA = (j >= nb) || (i < na && sm[i] < sm[na + j]);
+            so[dd + e] = takeA ? sm[i] : sm[na + j];
+            if (takeA) ++i; else ++j;
+        }
+    }
+    __syncthreads();
+    KeyT* dst = out + s * T + o0;
+    for (int i = tid; i < n; i += MERGE_THREADS) dst[i] = so[i];
+}
+
+// Exclusive prefix of the per-stream valid-write counts: soff[s] = writes of the
+// streams before s in the reference's global sorted order; soff[S] = total.
+__global__ void k_stream_offsets(const int* __restrict__ nvalid, int64_t* __restrict__ soff, int64_t S,
+                                 int64_t T) {
+    __shared__ int64_t carry;
+    if (threadIdx.x == 0) carry = 0;
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __shared__ int64_t wsum[32];
+    for (int64_t base = 0; base < S; base += blockDim.x) {
+        const int64_t s = base + threadIdx.x;
+        const int64_t v = s < S ? (nvalid ? nvalid[s] : T) : 0;
+        int64_t incl = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int64_t n = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += n;
+        }
+        if (lane == 31) wsum[warp] = incl;
+        __syncthreads();
+        if (warp == 0) {
+            const int nw = blockDim.x / 32;
+            int64_t x = lane < nw ? wsum[lane] : 0;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int64_t n = __shfl_up_sync(0xffffffffu, x, o);
+                if (lane >= o) x += n;
+            }
+            if (lane < nw) wsum[lane] = x;  // inclusive over warps
+        }
+        __syncthreads();
+        const int64_t before = carry + (warp ? wsum[warp - 1] : 0) + incl - v;
+        if (s < S) soff[s] = before;
+        __syncthreads();
+        if (threadIdx.x == blockDim.x - 1) carry = before + v;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) soff[S] = carry;
+}
+
+struct SearchArgs {
+    const void* keys;
+    const int* nvalid;     // null: every stream holds T writes
+    const void* raddr;
+    int addr_i64, key32;
+    int64_t B, T, C, A;
+    int tbits;
+    int32_t* ridx;         // [N] local index of the latest earlier write (may be any address), -1 if none
+};
+
+// ravel_memory.py:153-159 restricted to the read's stream: the number of the
+// stream's valid keys below (addr, t), minus one.
+template <typename KeyT>
+__global__ void __launch_bounds__(256) k_read_search(SearchArgs a) {
+    const int64_t N = a.B * a.T * a.C;
+    for (int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; r < N;
+         r += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t c = r % a.C;
+        const int64_t t = (r / a.C) % a.T;
+        const int64_t b = r / (a.C * a.T);
+        const int64_t s = b * a.C + c;
+        const uint64_t ra = fold_addr(load_addr(a.raddr, r, a.addr_i64), a.A, a.key32);
+        const KeyT q = (static_cast<KeyT>(ra) << a.tbits) | static_cast<KeyT>(t);
+        const KeyT* k = static_cast<const KeyT*>(a.keys) + s * a.T;
+        int64_t lo = 0, hi = a.nvalid ? a.nvalid[s] : a.T;
+        while (lo < hi) {
+            const int64_t mid = (lo + hi) >> 1;
+            if (k[mid] < q) lo = mid + 1; else hi = mid;
+        }
+        a.ridx[r] = static_cast<int32_t>(lo - 1);
+    }
+}
+
+}  // namespace ravel

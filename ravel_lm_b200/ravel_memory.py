@@ -1,0 +1,442 @@
+"""Drop-in replacement of the reference's ``ravel_lm/ravel_memory.py`` on B200.
+
+Same names, signatures, tensor layouts, return values and error behaviour as
+the reference module (``ravel_lm/ravel_memory.py:16-292``):
+
+* ``causal_last_k_lookup(write_addresses, payloads, read_addresses=None, *,
+  address_space, k=1, write_mask=None) -> (values [B,T,C,k,D], mask [B,T,C,k])``
+* ``causal_sum_lookup(write_addresses, payloads, read_addresses=None, *,
+  address_space, write_mask=None) -> (sums [B,T,C,D], mask [B,T,C])``
+* ``RavelLayerCache(values, filled)`` with ``empty``, ``read``, ``write``.
+
+The computation runs in the CUDA library ``libravel_b200.so`` (C ABI in
+``include/ravel_b200.h``), reached through ctypes.  The two lookups are
+``torch.library`` custom ops with fake (meta) implementations and autograd
+formulas, so they work under autograd, ``torch.compile`` and CUDA-graph
+capture.  Tensors must live on a CUDA device: there is no CPU path and no
+fallback.
+
+Differences from the reference that a caller can observe:
+* sums (and all gradients) accumulate in float32 (float64 for float64
+  payloads) instead of the payload dtype, so bf16/fp16 sums are more accurate
+  than the reference's own (which differ from the exact sum by ~10% at long T);
+* an invalid slot of ``causal_sum_lookup`` is +0.0 (the reference's is
+  ``segcum * 0`` and may be -0.0); latest-k invalid slots do match the
+  reference's ``candidate * 0`` bit for bit;
+* ``causal_sum_lookup`` also validates ``write_mask`` and ``read_addresses``
+  shapes (ValueError) where the reference fails later or not at all.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+
+Tensor = torch.Tensor
+
+_PAYLOAD_CODES = {torch.float32: _lib.RAVEL_F32, torch.bfloat16: _lib.RAVEL_BF16,
+                  torch.float16: _lib.RAVEL_F16, torch.float64: _lib.RAVEL_F64}
+_SMALL_INTS = (torch.int8, torch.int16, torch.uint8)
+
+
+# ------------------------------------------------------------------ helpers
+def _composite_key_dtype(B: int, T: int, C: int, address_space: int) -> torch.dtype:
+    """ravel_lm/ravel_memory.py:45-49: int32 keys iff B*C*A*(T+1) <= 2^31-1.
+
+    The CUDA path sorts 32-bit per-stream keys regardless; this decides only
+    the reference's int64 -> int32 address truncation, which is reproduced.
+    """
+    key_bound = int(B) * int(C) * int(address_space) * (int(T) + 1)
+    return torch.int32 if key_bound <= torch.iinfo(torch.int32).max else torch.int64
+
+
+def _addr(t: Tensor) -> Tuple[Tensor, int]:
+    if t.dtype == torch.int64:
+        return t.contiguous(), _lib.RAVEL_I64
+    if t.dtype == torch.int32:
+        return t.contiguous(), _lib.RAVEL_I32
+    if t.dtype in _SMALL_INTS:
+        return t.to(torch.int32).contiguous(), _lib.RAVEL_I32
+    raise TypeError(f"addresses must be an integer tensor, got {t.dtype}")
+
+
+def _payload_code(t: Tensor) -> int:
+    try:
+        return _PAYLOAD_CODES[t.dtype]
+    except KeyError:
+        raise TypeError(f"payloads must be float32, bfloat16, float16 or float64, got {t.dtype}") from None
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(*tensors: Optional[Tensor]) -> torch.device:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if t.device.type != "cuda":
+            raise RuntimeError(
+                f"ravel_lm_b200 runs on CUDA tensors only (got a {t.device.type} tensor); "
+                "there is no CPU fallback")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"tensors are on different devices: {dev} and {t.device}")
+    return dev
+
+
+def _aliases(read: Optional[Tensor], write: Tensor) -> bool:
+    if read is None or read is write:
+        return True
+    return (read.dtype == write.dtype and read.shape == write.shape and read.stride() == write.stride()
+            and read.device == write.device and read.data_ptr() == write.data_ptr())
+
+
+def _flags(read: Optional[Tensor], write_mask: Optional[Tensor]) -> int:
+    f = 0
+    if read is not None:
+        f |= _lib.RAVEL_TAPE_GENERAL_READS
+    if write_mask is not None:
+        f |= _lib.RAVEL_TAPE_WRITE_MASK
+    return f
+
+
+def _ptr(t: Optional[Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def tape_bytes(B: int, T: int, C: int, A: int, flags: int) -> int:
+    return int(_lib.load().ravel_tape_bytes(B, T, C, A, flags))
+
+
+def scratch_bytes(B: int, T: int, C: int, D: int, A: int, k: int, flags: int) -> int:
+    return int(_lib.load().ravel_scratch_bytes(B, T, C, D, A, k, flags))
+
+
+def _build_tape(write: Tensor, read: Optional[Tensor], write_mask: Optional[Tensor], A: int, D: int, k: int,
+                device: torch.device) -> Tuple[Tensor, Tensor, Tensor, int, int]:
+    """Sort the write events; returns (tape, scratch, read-or-write addresses, addr code, flags)."""
+    B, T, C = write.shape
+    flags = _flags(read, write_mask)
+    w, code = _addr(write)
+    if read is not None:
+        r, rcode = _addr(read)
+        if rcode != code:
+            w, r = w.to(torch.int64), r.to(torch.int64)
+            code = _lib.RAVEL_I64
+    else:
+        r = w
+    m = None
+    if write_mask is not None:
+        m = write_mask.to(torch.bool).contiguous()
+    tape = torch.empty(tape_bytes(B, T, C, A, flags), dtype=torch.uint8, device=device)
+    scratch = torch.empty(scratch_bytes(B, T, C, D, A, k, flags), dtype=torch.uint8, device=device)
+    st = _stream(device)
+    _lib.call("ravel_tape_build", w.data_ptr(), r.data_ptr() if read is not None else None, code, _ptr(m),
+              B, T, C, A, flags, tape.data_ptr(), tape.numel(), scratch.data_ptr(), scratch.numel(), st)
+    return tape, scratch, r, code, flags
+
+
+# ------------------------------------------------------------------ latest-k custom ops
+@torch.library.custom_op("ravel_b200::latestk_fwd", mutates_args=())
+def _latestk_fwd(write: Tensor, payload: Tensor, read: Optional[Tensor], write_mask: Optional[Tensor],
+                 address_space: int, k: int) -> Tuple[Tensor, Tensor, Tensor]:
+    B, T, C = write.shape
+    D = payload.shape[-1]
+    device = _require_cuda(write, payload, read, write_mask)
+    vals = payload.new_empty(B, T, C, k, D)
+    mask = torch.empty(B, T, C, k, dtype=torch.bool, device=device)
+    tape, _scratch, r, code, flags = _build_tape(write, read, write_mask, address_space, D, k, device)
+    p = payload.contiguous()
+    _lib.call("ravel_latestk_fwd_tape", tape.data_ptr(), flags, r.data_ptr() if flags else None, code,
+              p.data_ptr(), _payload_code(p), B, T, C, D, address_space, k, vals.data_ptr(), mask.data_ptr(),
+              _stream(device))
+    return vals, mask, tape
+
+
+@_latestk_fwd.register_fake
+def _latestk_fwd_fake(write, payload, read, write_mask, address_space, k):
+    B, T, C = write.shape
+    D = payload.shape[-1]
+    flags = _flags(read, write_mask)
+    return (payload.new_empty(B, T, C, k, D),
+            torch.empty(B, T, C, k, dtype=torch.bool, device=payload.device),
+            torch.empty(tape_bytes(B, T, C, address_space, flags), dtype=torch.uint8, device=payload.device))
+
+
+@torch.library.custom_op("ravel_b200::latestk_bwd", mutates_args=())
+def _latestk_bwd(tape: Tensor, grad_vals: Tensor, raddr: Tensor, flags: int, B: int, T: int, C: int,
+                 address_space: int, k: int) -> Tensor:
+    D = grad_vals.shape[-1]
+    device = _require_cuda(tape, grad_vals)
+    g = grad_vals.contiguous()
+    grad = torch.empty(B, T, C, D, dtype=g.dtype, device=device)
+    scratch = torch.empty(scratch_bytes(B, T, C, D, address_space, k, flags), dtype=torch.uint8, device=device)
+    r, code = _addr(raddr)
+    _lib.call("ravel_latestk_bwd", tape.data_ptr(), flags, r.data_ptr() if flags else None, code,
+              g.data_ptr(), _payload_code(g), B, T, C, D, address_space, k, grad.data_ptr(), scratch.data_ptr(),
+              scratch.numel(), _stream(device))
+    return grad
+
+
+@_latestk_bwd.register_fake
+def _latestk_bwd_fake(tape, grad_vals, raddr, flags, B, T, C, address_space, k):
+    return grad_vals.new_empty(B, T, C, grad_vals.shape[-1])
+
+
+def _latestk_setup(ctx, inputs, output):
+    write, payload, read, write_mask, address_space, k = inputs
+    _, mask, tape = output
+    ctx.save_for_backward(tape, write if read is None else read)
+    ctx.meta = (_flags(read, write_mask), *write.shape, int(address_space), int(k))
+    ctx.mark_non_differentiable(mask, tape)
+
+
+def _latestk_backward(ctx, grad_vals, _gm, _gt):
+    if grad_vals is None:
+        return None, None, None, None, None, None
+    tape, raddr = ctx.saved_tensors
+    flags, B, T, C, A, k = ctx.meta
+    grad = _latestk_bwd(tape, grad_vals, raddr, flags, B, T, C, A, k)
+    return None, grad, None, None, None, None
+
+
+_latestk_fwd.register_autograd(_latestk_backward, setup_context=_latestk_setup)
+
+
+# ------------------------------------------------------------------ sum custom ops
+@torch.library.custom_op("ravel_b200::segsum_fwd", mutates_args=())
+def _segsum_fwd(write: Tensor, payload: Tensor, read: Optional[Tensor], write_mask: Optional[Tensor],
+                address_space: int) -> Tuple[Tensor, Tensor, Tensor]:
+    B, T, C = write.shape
+    D = payload.shape[-1]
+    device = _require_cuda(write, payload, read, write_mask)
+    sums = payload.new_empty(B, T, C, D)
+    mask = torch.empty(B, T, C, dtype=torch.bool, device=device)
+    tape, scratch, r, code, flags = _build_tape(write, read, write_mask, address_space, D, 1, device)
+    p = payload.contiguous()
+    _lib.call("ravel_segsum_fwd_tape", tape.data_ptr(), flags, r.data_ptr() if flags else None, code,
+              p.data_ptr(), _payload_code(p), B, T, C, D, address_space, sums.data_ptr(), mask.data_ptr(),
+              scratch.data_ptr(), scratch.numel(), _stream(device))
+    return sums, mask, tape
+
+
+@_segsum_fwd.register_fake
+def _segsum_fwd_fake(write, payload, read, write_mask, address_space):
+    B, T, C = write.shape
+    D = payload.shape[-1]
+    flags = _flags(read, write_mask)
+    return (payload.new_empty(B, T, C, D),
+            torch.empty(B, T, C, dtype=torch.bool, device=payload.device),
+            torch.empty(tape_bytes(B, T, C, address_space, flags), dtype=torch.uint8, device=payload.device))
+
+
+@torch.library.custom_op("ravel_b200::segsum_bwd", mutates_args=())
+def _segsum_bwd(tape: Tensor, grad_sums: Tensor, raddr: Tensor, flags: int, B: int, T: int, C: int,
+                address_space: int) -> Tensor:
+    D = grad_sums.shape[-1]
+    device = _require_cuda(tape, grad_sums)
+    g = grad_sums.contiguous()
+    grad = torch.empty(B, T, C, D, dtype=g.dtype, device=device)
+    scratch = torch.empty(scratch_bytes(B, T, C, D, address_space, 1, flags), dtype=torch.uint8, device=device)
+    r, code = _addr(raddr)
+    _lib.call("ravel_segsum_bwd", tape.data_ptr(), flags, r.data_ptr() if flags else None, code,
+              g.data_ptr(), _payload_code(g), B, T, C, D, address_space, grad.data_ptr(), scratch.data_ptr(),
+              scratch.numel(), _stream(device))
+    return grad
+
+
+@_segsum_bwd.register_fake
+def _segsum_bwd_fake(tape, grad_sums, raddr, flags, B, T, C, address_space):
+    return grad_sums.new_empty(B, T, C, grad_sums.shape[-1])
+
+
+def _segsum_setup(ctx, inputs, output):
+    write, payload, read, write_mask, address_space = inputs
+    _, mask, tape = output
+    ctx.save_for_backward(tape, write if read is None else read)
+    ctx.meta = (_flags(read, write_mask), *write.shape, int(address_space))
+    ctx.mark_non_differentiable(mask, tape)
+
+
+def _segsum_backward(ctx, grad_sums, _gm, _gt):
+    if grad_sums is None:
+        return None, None, None, None, None
+    tape, raddr = ctx.saved_tensors
+    flags, B, T, C, A = ctx.meta
+    return None, _segsum_bwd(tape, grad_sums, raddr, flags, B, T, C, A), None, None, None
+
+
+_segsum_fwd.register_autograd(_segsum_backward, setup_context=_segsum_setup)
+
+
+# ------------------------------------------------------------------ public API
+def causal_last_k_lookup(
+    write_addresses: Tensor,
+    payloads: Tensor,
+    read_addresses: Optional[Tensor] = None,
+    *,
+    address_space: int,
+    k: int = 1,
+    write_mask: Optional[Tensor] = None,
+) -> Tuple[Tensor, Tensor]:
+    """Exact causal last-k lookup over an event tape (ravel_lm/ravel_memory.py:52-176).
+
+    For every read at time ``t`` returns the latest ``k`` payloads written with
+    the same ``(batch, head, address)`` at a time ``< t``.
+
+    Args:
+        write_addresses: [B, T, C] integer addresses for writes.
+        payloads:        [B, T, C, D] float32 / bfloat16 / float16 / float64.
+        read_addresses:  [B, T, C] integer read addresses. Defaults to writes.
+        address_space:   number of legal addresses per memory head; addresses
+                         are reduced modulo it (negative values wrap).
+        k:               number of latest records to return.
+        write_mask:      optional [B, T] boolean mask; false entries do not write.
+
+    Returns:
+        values: [B, T, C, k, D] (payload dtype), mask: [B, T, C, k] bool.
+    """
+    if read_addresses is None:
+        read_addresses = write_addresses
+    if write_addresses.shape != read_addresses.shape:
+        raise ValueError("write_addresses and read_addresses must have the same shape")
+    if write_addresses.ndim != 3:
+        raise ValueError("addresses must have shape [B, T, C]")
+    if payloads.ndim != 4:
+        raise ValueError("payloads must have shape [B, T, C, D]")
+    B, T, C = write_addresses.shape
+    if payloads.shape[:3] != (B, T, C):
+        raise ValueError("payloads leading dimensions must match addresses")
+    if k <= 0:
+        raise ValueError("k must be positive")
+    if write_mask is not None and write_mask.shape != (B, T):
+        raise ValueError("write_mask must have shape [B, T]")
+    _require_cuda(write_addresses, payloads, read_addresses, write_mask)
+    read = None if _aliases(read_addresses, write_addresses) else read_addresses
+    if B * T * C == 0:
+        return payloads.new_zeros(B, T, C, k, payloads.shape[-1]), torch.zeros(
+            B, T, C, k, dtype=torch.bool, device=payloads.device)
+    vals, mask, _tape = _latestk_fwd(write_addresses, payloads, read, write_mask, int(address_space), int(k))
+    return vals, mask
+
+
+def causal_sum_lookup(
+    write_addresses: Tensor,
+    payloads: Tensor,
+    read_addresses: Optional[Tensor] = None,
+    *,
+    address_space: int,
+    write_mask: Optional[Tensor] = None,
+) -> Tuple[Tensor, Tensor]:
+    """Exact causal segmented prefix-sum lookup (ravel_lm/ravel_memory.py:179-241).
+
+    For every read at time ``t`` returns the sum of all payloads with matching
+    ``(batch, head, address)`` and time ``< t``; differentiable w.r.t. payloads.
+    """
+    if read_addresses is None:
+        read_addresses = write_addresses
+    if write_addresses.ndim != 3 or payloads.ndim != 4:
+        raise ValueError("expected write_addresses [B,T,C] and payloads [B,T,C,D]")
+    B, T, C = write_addresses.shape
+    if read_addresses.shape != write_addresses.shape:
+        raise ValueError("write_addresses and read_addresses must have the same shape")
+    if payloads.shape[:3] != (B, T, C):
+        raise ValueError("payloads leading dimensions must match addresses")
+    if write_mask is not None and write_mask.shape != (B, T):
+        raise ValueError("write_mask must have shape [B, T]")
+    _require_cuda(write_addresses, payloads, read_addresses, write_mask)
+    read = None if _aliases(read_addresses, write_addresses) else read_addresses
+    if B * T * C == 0:
+        return payloads.new_zeros(B, T, C, payloads.shape[-1]), torch.zeros(
+            B, T, C, dtype=torch.bool, device=payloads.device)
+    sums, mask, _tape = _segsum_fwd(write_addresses, payloads, read, write_mask, int(address_space))
+    return sums, mask
+
+
+# ------------------------------------------------------------------ decode cache
+@dataclass
+class RavelLayerCache:
+    """Latest-value cache for decoding (ravel_lm/ravel_memory.py:244-292).
+
+    ``values [B, C, A, D]`` and ``filled [B, C, A]`` stay plain tensors, so the
+    cache pickles and state-dicts exactly like the reference's.  ``read`` and
+    ``write`` are one kernel launch each on the current stream; ``step`` does a
+    read followed by a write in a single launch.  Addresses are clamped to
+    [0, A-1] as in the reference.
+    """
+
+    values: Tensor
+    filled: Tensor
+
+    @classmethod
+    def empty(cls, batch_size: int, n_heads: int, address_space: int, payload_dim: int, *,
+              device: torch.device | str, dtype: torch.dtype) -> "RavelLayerCache":
+        values = torch.zeros(batch_size, n_heads, address_space, payload_dim, device=device, dtype=dtype)
+        filled = torch.zeros(batch_size, n_heads, address_space, device=device, dtype=torch.bool)
+        return cls(values=values, filled=filled)
+
+    def _check_storage(self) -> None:
+        if not (self.values.is_contiguous() and self.filled.is_contiguous()):
+            raise ValueError("cache tensors must be contiguous")
+        if self.filled.dtype != torch.bool:
+            raise ValueError("cache.filled must be a bool tensor")
+        _payload_code(self.values)
+
+    def read(self, addresses: Tensor) -> Tuple[Tensor, Tensor]:
+        """Read latest values for addresses [B, C]. Returns ([B,C,D], [B,C])."""
+        B, C = addresses.shape
+        if self.values.shape[:2] != (B, C):
+            raise ValueError(f"cache shape {self.values.shape[:2]} does not match addresses {(B, C)}")
+        device = _require_cuda(self.values, self.filled, addresses)
+        self._check_storage()
+        A, D = self.values.shape[2], self.values.shape[3]
+        a, code = _addr(addresses)
+        vals = self.values.new_empty(B, C, D)
+        mask = torch.empty(B, C, dtype=torch.bool, device=device)
+        _lib.call("ravel_cache_read", self.values.data_ptr(), self.filled.data_ptr(), a.data_ptr(), code,
+                  _payload_code(self.values), B, C, A, D, vals.data_ptr(), mask.data_ptr(), _stream(device))
+        return vals, mask
+
+    def write(self, addresses: Tensor, payloads: Tensor) -> None:
+        """Write latest payloads. addresses [B,C], payloads [B,C,D]."""
+        B, C = addresses.shape
+        D = payloads.shape[-1]
+        if self.values.shape[:2] != (B, C) or self.values.shape[-1] != D:
+            raise ValueError("cache and payload shapes do not match")
+        if payloads.shape[:2] != (B, C):
+            raise ValueError("cache and payload shapes do not match")
+        device = _require_cuda(self.values, self.filled, addresses, payloads)
+        self._check_storage()
+        a, code = _addr(addresses)
+        p = payloads.to(self.values.dtype).contiguous()
+        _lib.call("ravel_cache_write", self.values.data_ptr(), self.filled.data_ptr(), a.data_ptr(), code,
+                  p.data_ptr(), _payload_code(self.values), B, C, self.values.shape[2], D, _stream(device))
+
+    def step(self, read_addresses: Tensor, write_addresses: Tensor, payloads: Tensor) -> Tuple[Tensor, Tensor]:
+        """``read(read_addresses)`` then ``write(write_addresses, payloads)`` in one launch."""
+        B, C = read_addresses.shape
+        D = payloads.shape[-1]
+        if write_addresses.shape != (B, C) or self.values.shape[:2] != (B, C) or self.values.shape[-1] != D:
+            raise ValueError("cache and payload shapes do not match")
+        device = _require_cuda(self.values, self.filled, read_addresses, write_addresses, payloads)
+        self._check_storage()
+        ra, rcode = _addr(read_addresses)
+        wa, wcode = _addr(write_addresses)
+        if rcode != wcode:
+            ra, wa, rcode = ra.to(torch.int64), wa.to(torch.int64), _lib.RAVEL_I64
+        p = payloads.to(self.values.dtype).contiguous()
+        vals = self.values.new_empty(B, C, D)
+        mask = torch.empty(B, C, dtype=torch.bool, device=device)
+        _lib.call("ravel_cache_step", self.values.data_ptr(), self.filled.data_ptr(), ra.data_ptr(), wa.data_ptr(),
+                  rcode, p.data_ptr(), _payload_code(self.values), B, C, self.values.shape[2], D, vals.data_ptr(),
+                  mask.data_ptr(), _stream(device))
+        return vals, mask
+
+
+__all__ = ["RavelLayerCache", "causal_last_k_lookup", "causal_sum_lookup", "_composite_key_dtype"]

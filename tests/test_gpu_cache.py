@@ -1,0 +1,119 @@
+"""Decode cache (RavelLayerCache) on the GPU vs the reference and vs prefill."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden
+from gpu_helpers import assert_bits_equal
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    yield
+    import ravel_lm_b200._lib as L
+    torch.cuda.synchronize()
+    assert L.device_error(torch.cuda.current_stream().cuda_stream) == 0
+
+
+def test_cache_sequence_golden():
+    """Reference read/write sequence with out-of-range addresses (clamped)."""
+    from ravel_lm_b200 import RavelLayerCache
+    z = load_golden("cache_sequence")
+    B, C, A, D = (int(z[x]) for x in ("B", "C", "A", "D"))
+    cache = RavelLayerCache.empty(B, C, A, D, device="cuda", dtype=torch.float32)
+    for s in range(z["raddr"].shape[0]):
+        v, m = cache.read(torch.from_numpy(z["raddr"][s]).cuda())
+        assert_bits_equal(v, z["vals"][s].view(np.uint32), f"read {s}")
+        assert np.array_equal(m.cpu().numpy(), z["mask"][s].astype(bool))
+        cache.write(torch.from_numpy(z["waddr"][s]).cuda(), torch.from_numpy(z["payload"][s]).cuda())
+    assert np.array_equal(cache.values.cpu().numpy(), z["final_values"])
+    assert np.array_equal(cache.filled.cpu().numpy(), z["final_filled"].astype(bool))
+
+
+def test_kat_write_then_read():
+    """tests/test_memory.py:70-79 of the reference."""
+    from ravel_lm_b200 import RavelLayerCache
+    cache = RavelLayerCache.empty(1, 2, 16, 3, device="cuda", dtype=torch.float32)
+    addrs = torch.tensor([[5, 7]], device="cuda")
+    _, mask = cache.read(addrs)
+    assert not mask.any()
+    payload = torch.tensor([[[1.0, 2.0, 3.0], [4.0, 5.0, 6.0]]], device="cuda")
+    cache.write(addrs, payload)
+    vals, mask = cache.read(addrs)
+    assert mask.all()
+    assert torch.equal(vals, payload)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32, torch.float16, torch.float64])
+def test_step_equals_read_then_write(oracle_mod, dtype):
+    from ravel_lm_b200 import RavelLayerCache
+    g = torch.Generator().manual_seed(11)
+    B, C, A, D = 5, 4, 64, 12
+    c1 = RavelLayerCache.empty(B, C, A, D, device="cuda", dtype=dtype)
+    c2 = RavelLayerCache.empty(B, C, A, D, device="cuda", dtype=dtype)
+    vals_np = np.zeros((B, C, A, D), np.float64)
+    filled_np = np.zeros((B, C, A), bool)
+    for _ in range(40):
+        ra = torch.randint(-4, A + 4, (B, C), generator=g)
+        wa = torch.randint(-4, A + 4, (B, C), generator=g)
+        p = torch.randn(B, C, D, generator=g).to(dtype)
+        v1, m1 = c1.read(ra.cuda())
+        c1.write(wa.cuda(), p.cuda())
+        v2, m2 = c2.step(ra.cuda(), wa.cuda(), p.cuda())
+        assert torch.equal(v1, v2) and torch.equal(m1, m2)
+        ov, om = oracle_mod.cache_read(vals_np, filled_np, ra.numpy())
+        assert np.array_equal(m1.cpu().numpy(), om)
+        assert np.array_equal(v1.double().cpu().numpy(), ov)
+        oracle_mod.cache_write(vals_np, filled_np, wa.numpy(), p.double().numpy())
+    assert torch.equal(c1.values, c2.values) and torch.equal(c1.filled, c2.filled)
+
+
+def test_decode_matches_prefill_latest1():
+    """Token-by-token cache steps == latest-1 prefill over the same tape
+    (the property behind tests/test_model.py:78-91 of the reference)."""
+    from ravel_lm_b200 import RavelLayerCache, causal_last_k_lookup
+    g = torch.Generator().manual_seed(3)
+    B, T, C, A, D = 6, 300, 4, 50, 16
+    addr = torch.randint(0, A, (B, T, C), generator=g).cuda()
+    pay = torch.randn(B, T, C, D, generator=g).to(torch.bfloat16).cuda()
+    vals, mask = causal_last_k_lookup(addr, pay, address_space=A, k=1)
+    cache = RavelLayerCache.empty(B, C, A, D, device="cuda", dtype=torch.bfloat16)
+    for t in range(T):
+        v, m = cache.step(addr[:, t], addr[:, t], pay[:, t])
+        assert torch.equal(m, mask[:, t, :, 0])
+        assert torch.equal(v, vals[:, t, :, 0])  # value equality (+0 == -0)
+
+
+def test_decode_cuda_graph_replay():
+    """Steps captured once in a CUDA graph and replayed give the eager result."""
+    from ravel_lm_b200 import RavelLayerCache
+    g = torch.Generator().manual_seed(9)
+    S, H, A, D, steps = 16, 4, 128, 64, 12
+    ra = torch.randint(0, A, (steps, S, H), generator=g).cuda()
+    wa = torch.randint(0, A, (steps, S, H), generator=g).cuda()
+    pay = torch.randn(steps, S, H, D, generator=g).to(torch.bfloat16).cuda()
+    eager = RavelLayerCache.empty(S, H, A, D, device="cuda", dtype=torch.bfloat16)
+    ev = [eager.step(ra[i], wa[i], pay[i]) for i in range(steps)]
+    graphed = RavelLayerCache.empty(S, H, A, D, device="cuda", dtype=torch.bfloat16)
+    outs = []
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(steps):
+                outs.append(graphed.step(ra[i], wa[i], pay[i]))
+    torch.cuda.current_stream().wait_stream(stream)
+    graphed.values.zero_()
+    graphed.filled.zero_()
+    graph.replay()
+    torch.cuda.synchronize()
+    for (v1, m1), (v2, m2) in zip(ev, outs):
+        assert torch.equal(v1, v2) and torch.equal(m1, m2)
+    assert torch.equal(eager.values, graphed.values)
+    del graph

@@ -1,0 +1,183 @@
+"""CUDA path vs the reference: golden vectors and the CPU oracle.
+
+Every test calls the public drop-in API (which runs ``libravel_b200.so``
+through its C ABI) on ``cuda:0`` and checks it against either the committed
+golden outputs of the reference itself or the C oracle on identical seeded
+inputs.
+"""
+from __future__ import annotations
+
+import zlib
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden_cases, load_golden, payload_as_float64, payload_code
+from gpu_helpers import SUM_TOL, assert_bits_equal, assert_close, payload_np, to_f64
+
+pytestmark = pytest.mark.gpu
+
+DT = {"float32": torch.float32, "bfloat16": torch.bfloat16, "float16": torch.float16, "float64": torch.float64}
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    import ravel_lm_b200._lib as L
+    L.load()
+    yield
+    torch.cuda.synchronize()
+    assert L.device_error(torch.cuda.current_stream().cuda_stream) == 0
+
+
+def _payload_tensor(case) -> torch.Tensor:
+    p = case["payload"]
+    dt = DT[str(case["dtype"])]
+    if dt == torch.bfloat16:
+        return torch.from_numpy(p.view(np.int16).copy()).view(torch.bfloat16)
+    if dt == torch.float16:
+        return torch.from_numpy(p.view(np.int16).copy()).view(torch.float16)
+    return torch.from_numpy(p.copy())
+
+
+def _run(w, p, r, m, A, k, g_lk, g_ss, dev="cuda"):
+    from ravel_lm_b200 import causal_last_k_lookup, causal_sum_lookup
+    pw = p.to(dev).requires_grad_(True)
+    wd = w.to(dev)
+    rd = None if r is None else r.to(dev)
+    md = None if m is None else m.to(dev)
+    vals, mask = causal_last_k_lookup(wd, pw, rd, address_space=A, k=k, write_mask=md)
+    sums, smask = causal_sum_lookup(wd, pw, rd, address_space=A, write_mask=md)
+    glk = torch.autograd.grad(vals, pw, g_lk.to(dev).to(p.dtype), retain_graph=True, allow_unused=True)[0]
+    gss = torch.autograd.grad(sums, pw, g_ss.to(dev).to(p.dtype), allow_unused=True)[0]
+    torch.cuda.synchronize()
+    return vals, mask, sums, smask, glk, gss
+
+
+@pytest.mark.parametrize("name", golden_cases())
+def test_golden_vectors(name):
+    """Reference outputs on its own known-answer and seeded cases."""
+    case = load_golden(name)
+    A, k = int(case["A"]), int(case["k"])
+    w = torch.from_numpy(case["waddr"])
+    r = torch.from_numpy(case["raddr"]) if "raddr" in case else None
+    m = torch.from_numpy(case["wmask"]).bool() if "wmask" in case else None
+    p = _payload_tensor(case)
+    vals, mask, sums, smask, glk, gss = _run(w, p, r, m, A, k, torch.from_numpy(case["g_lk"]),
+                                             torch.from_numpy(case["g_ss"]))
+    assert_bits_equal(vals, case["lk_vals"], f"{name} latest-k values")
+    assert np.array_equal(mask.cpu().numpy(), case["lk_mask"].astype(bool)), f"{name} latest-k mask"
+    assert np.array_equal(smask.cpu().numpy(), case["ss_mask"].astype(bool)), f"{name} sum mask"
+    tol = SUM_TOL[p.dtype]
+    assert_close(to_f64(sums), case["ss_sums64"], tol, f"{name} sums")
+    if glk is not None:
+        assert_close(to_f64(glk), case["lk_grad64"], tol, f"{name} latest-k grad")
+    if gss is not None:
+        assert_close(to_f64(gss), case["ss_grad64"], tol, f"{name} sum grad")
+
+
+def _oracle_check(oracle, w, p, r, m, A, k, g_lk, g_ss, *, check_grads=True):
+    vals, mask, sums, smask, glk, gss = _run(w, p, r, m, A, k, g_lk, g_ss)
+    code = {torch.bfloat16: "bf16", torch.float16: "f16"}.get(p.dtype)
+    wn = w.numpy()
+    rn = None if r is None else r.numpy()
+    mn = None if m is None else m.numpy()
+    ov, om, osrc, tape = oracle.latestk_fwd(wn, payload_np(p), rn, address_space=A, k=k, write_mask=mn, dtype=code)
+    assert_bits_equal(vals, ov.view({2: np.uint16, 4: np.uint32, 8: np.uint64}[ov.dtype.itemsize]), "values")
+    assert np.array_equal(mask.cpu().numpy(), om), "latest-k mask"
+    p64 = to_f64(p)
+    osum, osm, _ = oracle.segsum_fwd(wn, p64, rn, address_space=A, write_mask=mn, tape=tape)
+    assert np.array_equal(smask.cpu().numpy(), osm), "sum mask"
+    tol = SUM_TOL[p.dtype]
+    assert_close(to_f64(sums), osum, tol, "sums")
+    if check_grads:
+        B, T, C, D = p.shape
+        olk = oracle.latestk_bwd(om, osrc, to_f64(g_lk), B * T * C).reshape(B, T, C, D)
+        oss = oracle.segsum_bwd(tape, osm, to_f64(g_ss))
+        assert_close(to_f64(glk), olk, tol, "latest-k grad")
+        assert_close(to_f64(gss), oss, tol, "sum grad")
+
+
+CASES = [
+    # name, B, T, C, D, A, k, dtype, reads, mask, address dist
+    ("cfg1", 8, 256, 4, 16, 256, 1, torch.float32, False, False, "zipf1.1"),
+    ("cfg2_fast", 16, 2048, 8, 32, 4096, 4, torch.float32, False, False, "product"),
+    ("multitile_bf16", 1, 20000, 3, 64, 65536, 8, torch.bfloat16, False, False, "zipf1.05"),
+    ("long_t32k_bf16", 1, 32768, 2, 64, 65536, 8, torch.bfloat16, False, False, "zipf1.05"),
+    ("hot_segments", 2, 9000, 2, 16, 3, 6, torch.float32, False, False, "uniform"),
+    ("general_reads", 4, 700, 5, 24, 97, 3, torch.float32, True, False, "uniform"),
+    ("general_mask", 3, 1500, 4, 8, 40, 2, torch.float32, True, True, "uniform"),
+    ("mask_aliased", 3, 900, 3, 16, 30, 4, torch.bfloat16, False, True, "uniform"),
+    ("general_long_multitile", 1, 17000, 2, 32, 500, 3, torch.float32, True, True, "uniform"),
+    ("odd_d_f16", 2, 300, 3, 5, 11, 3, torch.float16, True, False, "uniform"),
+    ("f64_fast", 2, 513, 3, 7, 17, 2, torch.float64, False, False, "uniform"),
+    ("d1_k_gt_t", 3, 5, 2, 1, 3, 8, torch.float32, False, False, "uniform"),
+    ("key64", 2, 4096, 2, 8, 2**31, 2, torch.float32, False, False, "huge"),
+    ("key64_general", 2, 3000, 2, 8, 2**31, 2, torch.float32, True, True, "huge"),
+]
+
+
+def _gen_addresses(gen, dist, shape, A):
+    if dist.startswith("zipf"):
+        from ravel_lm_b200.workloads import zipf_ranks
+        return zipf_ranks(A, float(dist[4:]), shape, gen)
+    if dist == "product":
+        return torch.randint(0, 64, shape, generator=gen) * 64 + torch.randint(0, 64, shape, generator=gen)
+    if dist == "huge":
+        pool = torch.randint(0, 2**31 - 1, (64,), generator=gen)
+        return pool[torch.randint(0, 64, shape, generator=gen)]
+    return torch.randint(-A, 2 * A, shape, generator=gen)
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
+def test_seeded_vs_oracle(oracle_mod, case):
+    name, B, T, C, D, A, k, dt, reads, mask, dist = case
+    gen = torch.Generator().manual_seed(zlib.crc32(name.encode()))
+    w = _gen_addresses(gen, dist, (B, T, C), A)
+    r = _gen_addresses(gen, dist, (B, T, C), A) if reads else None
+    m = (torch.rand(B, T, generator=gen) < 0.7) if mask else None
+    if m is not None and B > 1:
+        m[1] = False  # an all-masked batch row: empty streams inside the tape
+    p = torch.randn(B, T, C, D, generator=gen).to(dt)
+    g_lk = torch.randn(B, T, C, k, D, generator=gen).to(dt)
+    g_ss = torch.randn(B, T, C, D, generator=gen).to(dt)
+    _oracle_check(oracle_mod, w, p, r, m, A, k, g_lk, g_ss)
+
+
+def test_int32_addresses_match_int64(oracle_mod):
+    gen = torch.Generator().manual_seed(5)
+    w = torch.randint(-50, 50, (2, 400, 3), generator=gen)
+    r = torch.randint(-50, 50, (2, 400, 3), generator=gen)
+    p = torch.randn(2, 400, 3, 8, generator=gen)
+    g1 = torch.randn(2, 400, 3, 2, 8, generator=gen)
+    g2 = torch.randn(2, 400, 3, 8, generator=gen)
+    a = _run(w, p, r, None, 37, 2, g1, g2)
+    b = _run(w.int(), p, r.int(), None, 37, 2, g1, g2)
+    for x, y in zip(a[:4], b[:4]):
+        assert torch.equal(x, y)
+    for x, y in zip(a[4:], b[4:]):  # float32 atomics: order may differ
+        torch.testing.assert_close(x, y, rtol=1e-5, atol=1e-5)
+
+
+def test_model_config5_op_shapes(oracle_mod):
+    """Config 5 (literal + learned heads, read != write) at its per-GPU size."""
+    from ravel_lm_b200.workloads import CONFIGS, make_inputs
+    cfg = CONFIGS[5]
+    x = make_inputs(cfg)
+    _oracle_check(oracle_mod, x["write"], x["payload"], x["read"], None, cfg.A, cfg.k, x["g_vals"], x["g_sums"])
+
+
+def test_config2_full(oracle_mod):
+    from ravel_lm_b200.workloads import CONFIGS, make_inputs
+    cfg = CONFIGS[2]
+    x = make_inputs(cfg)
+    _oracle_check(oracle_mod, x["write"], x["payload"], None, None, cfg.A, cfg.k, x["g_vals"], x["g_sums"])
+
+
+def test_config3_full(oracle_mod):
+    """The long-context configuration at full size (B4 T32768 H16 D64 bf16 k8)."""
+    from ravel_lm_b200.workloads import CONFIGS, make_inputs
+    cfg = CONFIGS[3]
+    x = make_inputs(cfg)
+    _oracle_check(oracle_mod, x["write"], x["payload"], None, None, cfg.A, cfg.k, x["g_vals"], x["g_sums"])
