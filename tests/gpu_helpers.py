@@ -53,11 +53,20 @@ def assert_close(actual: np.ndarray, expected: np.ndarray, tol: float, what: str
 
 
 def assert_bits_equal(actual: torch.Tensor, expected_bits: np.ndarray, what: str = "") -> None:
+    """Bitwise equality; a float ``expected_bits`` array is compared through its raw bits."""
+    if expected_bits.dtype.kind == "f":
+        expected_bits = expected_bits.view({2: np.uint16, 4: np.uint32, 8: np.uint64}[expected_bits.itemsize])
     a = to_np_bits(actual)
     if a.shape != expected_bits.shape:
         raise AssertionError(f"{what}: shape {a.shape} != {expected_bits.shape}")
     if not np.array_equal(a, expected_bits):
-        n = int((a != expected_bits).sum())
-        i = np.argwhere(a != expected_bits)[0]
-        raise AssertionError(f"{what}: {n} of {a.size} elements differ bitwise; first at {tuple(i)}: "
-                             f"{a[tuple(i)]:#x} vs {expected_bits[tuple(i)]:#x}")
+        diff = a != expected_bits
+        n = int(diff.sum())
+        idx = np.argwhere(diff)
+        width = a.dtype.itemsize * 8
+        sign = np.uint64(1) << np.uint64(width - 1)
+        only_sign = int(((a.astype(np.uint64) ^ expected_bits.astype(np.uint64)) == sign)[diff].sum())
+        first = ", ".join(f"{tuple(int(x) for x in i)}: {int(a[tuple(i)]):#x} vs {int(expected_bits[tuple(i)]):#x}"
+                          for i in idx[:6])
+        raise AssertionError(f"{what}: {n} of {a.size} elements differ bitwise ({only_sign} only in the sign "
+                             f"bit); first: {first}")

@@ -181,3 +181,35 @@ def test_config3_full(oracle_mod):
     cfg = CONFIGS[3]
     x = make_inputs(cfg)
     _oracle_check(oracle_mod, x["write"], x["payload"], None, None, cfg.A, cfg.k, x["g_vals"], x["g_sums"])
+
+
+@pytest.mark.parametrize("T,A,mask", [(256, 256, False), (300, 50, False), (20000, 65536, False),
+                                      (1500, 40, True), (5, 3, False)])
+def test_tape_sort_order(oracle_mod, T, A, mask):
+    """The per-stream sorted keys of the tape equal the reference's sort order."""
+    import ravel_lm_b200.ravel_memory as rm
+    gen = torch.Generator().manual_seed(T + A)
+    B, C = 2, 3
+    w = torch.randint(-A, 2 * A, (B, T, C), generator=gen)
+    m = (torch.rand(B, T, generator=gen) < 0.6) if mask else None
+    p = torch.randn(B, T, C, 4, generator=gen)
+    _, _, tape = rm._latestk_fwd(w.cuda(), p.cuda(), None, None if m is None else m.cuda(), A, 1)
+    torch.cuda.synchronize()
+    ot = oracle_mod.Tape(w.numpy(), None, None if m is None else m.numpy(), A)
+    tbits = max(1, (T - 1).bit_length())
+    abits = (A - 1).bit_length()
+    key64 = tbits + abits + (1 if mask else 0) > 32
+    keys = tape.cpu().numpy().view(np.uint64 if key64 else np.uint32)[: B * C * T].reshape(B * C, T)
+    # oracle: global sorted keys -> per-stream (addr, t)
+    sk = ot.sorted_keys[: ot.nw]
+    base = sk // (T + 1)
+    stream = base // A
+    addr = base % A
+    t = sk % (T + 1)
+    pos = 0
+    for s in range(B * C):
+        n = int((stream == s).sum())
+        got = keys[s, :n].astype(np.int64)
+        exp = (addr[pos:pos + n].astype(np.int64) << tbits) | t[pos:pos + n]
+        assert np.array_equal(got, exp), f"stream {s}: sorted keys differ at {np.argwhere(got != exp)[:5].ravel()}"
+        pos += n
