@@ -166,6 +166,28 @@ int ravel_cache_step(void* values, uint8_t* filled, const void* raddr, const voi
                      int addr_dtype, const void* payload, int dtype, int64_t B, int64_t C,
                      int64_t A, int64_t D, void* out_vals, uint8_t* out_mask, void* stream);
 
+/*
+ * causal_sum_lookup forward for callers that cannot allocate device memory.
+ * No counterpart in the reference: it exists for hosts that may not call
+ * cudaMalloc or a caching allocator on this path -- plugin interfaces whose
+ * enqueue step must not allocate, code running inside a CUDA-graph capture,
+ * or foreign-language callers with no CUDA allocator of their own.  Same
+ * arguments and results as ravel_segsum_fwd, minus tape and scratch: both live
+ * in one file-scope device array of RAVEL_NOALLOC_SCRATCH_BYTES that every GPU
+ * loading this library holds until the process exits.  Returns
+ * RAVEL_ERR_WORKSPACE, launching nothing, when ravel_tape_bytes() +
+ * ravel_scratch_bytes() of the call exceed that size.  The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress) with that
+ * device current; make that first call before any stream capture.  All calls
+ * share the array, so calls that overlap on the GPU (other streams, other host
+ * threads) race; serialise them.  No backward: the tape is not kept.
+ */
+#define RAVEL_NOALLOC_SCRATCH_BYTES (32u << 20)
+int ravel_segsum_fwd_noalloc(const void* waddr, const void* raddr, int addr_dtype,
+                             const uint8_t* wmask, const void* payload, int dtype, int64_t B,
+                             int64_t T, int64_t C, int64_t D, int64_t A, void* out_sums,
+                             uint8_t* out_mask, void* stream);
+
 /* Copy the device error word (RAVEL_DEVERR_* bits) of the current device into
  * *out after the work queued on `stream`; synchronises that stream. */
 int ravel_device_error(int* out, void* stream);

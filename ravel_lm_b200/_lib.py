@@ -24,6 +24,7 @@ RAVEL_F32, RAVEL_BF16, RAVEL_F16, RAVEL_F64 = 0, 1, 2, 3
 RAVEL_I32, RAVEL_I64 = 0, 1
 RAVEL_TAPE_GENERAL_READS = 1
 RAVEL_TAPE_WRITE_MASK = 2
+RAVEL_NOALLOC_SCRATCH_BYTES = 32 << 20
 RAVEL_DEVERR_SPIN = 1
 RAVEL_DEVERR_BOUNDS = 2
 
@@ -50,6 +51,8 @@ SIGNATURES = {
                          [_c_vp, _c_vp, _c_vp, _c_sz, _c_vp, _c_sz, _c_vp]),
     "ravel_segsum_bwd": (_c_int, [_c_vp, _c_int, _c_vp, _c_int, _c_vp, _c_int] + [_c_i64] * 5 +
                          [_c_vp, _c_vp, _c_sz, _c_vp]),
+    "ravel_segsum_fwd_noalloc": (_c_int, [_c_vp, _c_vp, _c_int, _c_vp, _c_vp, _c_int] + [_c_i64] * 5 +
+                                 [_c_vp, _c_vp, _c_vp]),
     "ravel_cache_read": (_c_int, [_c_vp, _c_vp, _c_vp, _c_int, _c_int] + [_c_i64] * 4 + [_c_vp, _c_vp, _c_vp]),
     "ravel_cache_write": (_c_int, [_c_vp, _c_vp, _c_vp, _c_int, _c_vp, _c_int] + [_c_i64] * 4 + [_c_vp]),
     "ravel_cache_step": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_vp, _c_int] + [_c_i64] * 4 +

@@ -5,6 +5,7 @@
 // scratch layouts, and the launch plumbing; the kernels live in the headers.
 #include <atomic>
 #include <cstring>
+#include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
@@ -594,6 +595,33 @@ __global__ void k_clear_error() { g_error_word = 0u; }
 }  // namespace
 }  // namespace ravel
 
+// ------------------------------------------------------------------ no-allocation variant
+// Tape and scratch of ravel_segsum_fwd_noalloc.  Host code must not use the
+// array's name as a device pointer; its device address is looked up once per
+// device below.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[RAVEL_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_base[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device (set up on first use).
+int noalloc_base(void** out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return RAVEL_ERR_CUDA;
+    if (dev < 0 || dev >= kMaxDevices) return RAVEL_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_base[dev] == nullptr) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return RAVEL_ERR_CUDA;
+        g_noalloc_base[dev] = p;
+    }
+    *out = g_noalloc_base[dev];
+    return RAVEL_OK;
+}
+}  // namespace
+
 using namespace ravel;
 
 extern "C" {
@@ -663,6 +691,27 @@ int ravel_segsum_fwd(const void* waddr, const void* raddr, int addr_dtype, const
         return e;
     return ss_fwd_tape(tape, flags, raddr ? raddr : waddr, addr_dtype, payload, dtype, B, T, C, D, A, out_sums,
                        out_mask, scratch, scratch_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int ravel_segsum_fwd_noalloc(const void* waddr, const void* raddr, int addr_dtype, const uint8_t* wmask,
+                             const void* payload, int dtype, int64_t B, int64_t T, int64_t C, int64_t D, int64_t A,
+                             void* out_sums, uint8_t* out_mask, void* stream) {
+    if (raddr == waddr) raddr = nullptr;
+    const int flags = (raddr ? RAVEL_TAPE_GENERAL_READS : 0) | (wmask ? RAVEL_TAPE_WRITE_MASK : 0);
+    if (int e = check_sizes(B, T, C, D, A)) return e;
+    if (dtype < 0 || dtype > 3) return RAVEL_ERR_INVALID_ARG;
+    const size_t tape_sz = align_up(tape_layout(B, T, C, A, flags).total);
+    const size_t scratch_sz = scratch_layout(B, T, C, D, A, dtype, flags).total;
+    if (tape_sz + scratch_sz > RAVEL_NOALLOC_SCRATCH_BYTES) return RAVEL_ERR_WORKSPACE;
+    void* base = nullptr;
+    if (int e = noalloc_base(&base)) return e;
+    void* tape = base;
+    void* scratch = static_cast<char*>(base) + tape_sz;
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (int e = tape_build(waddr, raddr, addr_dtype, wmask, B, T, C, A, flags, tape, tape_sz, scratch, scratch_sz, st))
+        return e;
+    return ss_fwd_tape(tape, flags, raddr ? raddr : waddr, addr_dtype, payload, dtype, B, T, C, D, A, out_sums,
+                       out_mask, scratch, scratch_sz, st);
 }
 
 int ravel_segsum_bwd(const void* tape, int tape_flags, const void* raddr, int addr_dtype, const void* grad_sums,
