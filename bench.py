@@ -57,6 +57,7 @@ def parse():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-streams", type=int, default=8, help="streams in the CPU baseline sample")
+    ap.add_argument("--batch", type=int, default=None, help="override B per GPU (small profiling cases)")
     return ap.parse_args()
 
 
@@ -283,6 +284,8 @@ def main():
     args = parse()
     from ravel_lm_b200.workloads import CONFIGS
     cfg = CONFIGS[args.config]
+    if args.batch is not None:
+        cfg = cfg.with_batch(args.batch)
     rank, world, local = (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
                           int(os.environ.get("LOCAL_RANK", "0")))
 
@@ -303,6 +306,7 @@ def main():
     import torch
     import ravel_lm_b200._lib as L
     from ravel_lm_b200 import causal_last_k_lookup, causal_sum_lookup
+    from ravel_lm_b200.ravel_memory import clear_tape_cache
     from ravel_lm_b200.workloads import make_inputs
 
     rank, world, local = dist_setup()
@@ -316,6 +320,9 @@ def main():
     A, k = cfg.A, cfg.k
 
     def step():
+        # Each step stands for a new batch: forget the tape of the previous step
+        # (only the latest-k -> sum reuse inside one step is legitimate).
+        clear_tape_cache()
         p.grad = None
         vals, _m = causal_last_k_lookup(w, p, r, address_space=A, k=k)
         sums, _s = causal_sum_lookup(w, p, r, address_space=A)
@@ -437,6 +444,7 @@ def run_e2e(cfg, x, dev, steps, world):
     """The same step through the public API from pinned host buffers, with copies in the timed region."""
     import torch
     from ravel_lm_b200 import causal_last_k_lookup, causal_sum_lookup
+    from ravel_lm_b200.ravel_memory import clear_tape_cache
     host = {n: x[n].detach().to("cpu").pin_memory() for n in ("write", "payload", "g_vals", "g_sums")}
     if x["read"] is not None:
         host["read"] = x["read"].to("cpu").pin_memory()
@@ -450,6 +458,7 @@ def run_e2e(cfg, x, dev, steps, world):
     d2h = sum(t.numel() * t.element_size() for t in out.values())
 
     def one():
+        clear_tape_cache()
         w = host["write"].to(dev, non_blocking=True)
         r = host["read"].to(dev, non_blocking=True) if "read" in host else None
         p = host["payload"].to(dev, non_blocking=True).requires_grad_(True)

@@ -65,9 +65,10 @@ extern "C" {
 /* Bytes of the tape written by a forward call and read by its backward call. */
 size_t ravel_tape_bytes(int64_t B, int64_t T, int64_t C, int64_t A, int tape_flags);
 
-/* Bytes of per-call scratch sufficient for every entry point at these sizes. */
+/* Bytes of per-call scratch sufficient for every entry point at these sizes
+ * and this payload dtype. */
 size_t ravel_scratch_bytes(int64_t B, int64_t T, int64_t C, int64_t D, int64_t A, int64_t k,
-                           int tape_flags);
+                           int dtype, int tape_flags);
 
 /*
  * Sort the write events of every stream by (address, time) and, for general

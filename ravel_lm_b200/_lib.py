@@ -36,7 +36,7 @@ _c_sz = ctypes.c_size_t
 # name -> (restype, argtypes); the order follows include/ravel_b200.h
 SIGNATURES = {
     "ravel_tape_bytes": (_c_sz, [_c_i64, _c_i64, _c_i64, _c_i64, _c_int]),
-    "ravel_scratch_bytes": (_c_sz, [_c_i64] * 6 + [_c_int]),
+    "ravel_scratch_bytes": (_c_sz, [_c_i64] * 6 + [_c_int, _c_int]),
     "ravel_tape_build": (_c_int, [_c_vp, _c_vp, _c_int, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_int,
                                   _c_vp, _c_sz, _c_vp, _c_sz, _c_vp]),
     "ravel_latestk_fwd_tape": (_c_int, [_c_vp, _c_int, _c_vp, _c_int, _c_vp, _c_int] + [_c_i64] * 6 +

@@ -95,23 +95,55 @@ __global__ void __launch_bounds__(256) k_lk_fwd_fast(LkArgs a) {
     cp_async_wait_all();
     __syncthreads();
 
+    // Output: warp w walks positions w, w+8, ...; within a position the block of
+    // k*rv vectors is covered by the 32 lanes in passes.  Each lane's (position
+    // offset, slot, vector) decomposition is computed once, not per element.
     char* outv = static_cast<char*>(a.out);
-    const uint32_t bv = rv * static_cast<uint32_t>(k);
-    for (uint32_t e = tid; e < static_cast<uint32_t>(np) * bv; e += 256) {
-        uint32_t i, v, j, o;
-        a.fd_bv.divmod(e, i, v);
-        a.fd_rv.divmod(v, j, o);
-        const int wi = static_cast<int>(i) + k;
-        const int src = wi - 1 - static_cast<int>(j);
-        uint4 x = ld_vec<VB>(rows + static_cast<int64_t>(src) * a.row_bytes + o * VB);
-        if (wadr[src] != wadr[wi]) x = VecZero<DT, VB>::apply(x);
-        st_vec_stream<VB>(outv + (wrow[wi] * k + j) * a.row_bytes + o * VB, x);
+    const int lane = tid & 31, warp = tid >> 5;
+    const uint32_t bv = rv * static_cast<uint32_t>(k);  // vectors per output block
+    if (bv == 0) {
+        for (int e = tid; e < np * k; e += 256) {
+            const int i = e / k, j = e % k;
+            a.out_mask[wrow[i + k] * k + j] = wadr[i + k - 1 - j] == wadr[i + k] ? 1 : 0;
+        }
+        return;
     }
-    for (uint32_t e = tid; e < static_cast<uint32_t>(np * k); e += 256) {
-        uint32_t i, j;
-        a.fd_k.divmod(e, i, j);
-        const int wi = static_cast<int>(i) + k;
-        a.out_mask[wrow[wi] * k + j] = wadr[wi - 1 - j] == wadr[wi] ? 1 : 0;
+    if (bv <= 32) {
+        // several positions per warp pass
+        const int gp = static_cast<int>(32 / bv);
+        uint32_t dp, v, j, o;
+        a.fd_bv.divmod(static_cast<uint32_t>(lane), dp, v);
+        a.fd_rv.divmod(v, j, o);
+        const bool lane_on = static_cast<int>(dp) < gp;
+        for (int i0 = warp * gp; i0 < np; i0 += 8 * gp) {
+            const int i = i0 + static_cast<int>(dp);
+            if (!lane_on || i >= np) continue;
+            const int wi = i + k;
+            const int src = wi - 1 - static_cast<int>(j);
+            const bool valid = wadr[src] == wadr[wi];
+            uint4 x = ld_vec<VB>(rows + static_cast<int64_t>(src) * a.row_bytes + o * VB);
+            if (!valid) x = VecZero<DT, VB>::apply(x);
+            const int64_t blk = wrow[wi] * k + j;
+            st_vec_stream<VB>(outv + blk * a.row_bytes + o * VB, x);
+            if (o == 0) a.out_mask[blk] = valid ? 1 : 0;
+        }
+    } else {
+        // one position per warp, ceil(bv/32) passes
+        for (int i = warp; i < np; i += 8) {
+            const int wi = i + k;
+            const uint64_t my = wadr[wi];
+            const int64_t base = wrow[wi] * k;
+            for (uint32_t v = lane; v < bv; v += 32) {
+                uint32_t j, o;
+                a.fd_rv.divmod(v, j, o);
+                const int src = wi - 1 - static_cast<int>(j);
+                const bool valid = wadr[src] == my;
+                uint4 x = ld_vec<VB>(rows + static_cast<int64_t>(src) * a.row_bytes + o * VB);
+                if (!valid) x = VecZero<DT, VB>::apply(x);
+                st_vec_stream<VB>(outv + (base + j) * a.row_bytes + o * VB, x);
+                if (o == 0) a.out_mask[base + j] = valid ? 1 : 0;
+            }
+        }
     }
 }
 

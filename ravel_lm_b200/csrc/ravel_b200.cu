@@ -81,10 +81,21 @@ SortPlan sort_plan(int64_t T) {
 int acc_bytes(int dtype) { return dtype == RAVEL_F64 ? 8 : 4; }
 
 struct ScanPlan {
-    int P, parts;
-    int64_t nchunks;
+    int P, parts, min_P;
+    int64_t nchunks;      // chunks per stream of the fallback kernel
+    int64_t max_nchunks;  // chunks per stream of the smallest chunk size in use
 };
 
+// Chunk size of the warp-register scan kernel (0 when it does not apply).
+int scanw_positions(int64_t D, int elem_bytes_in) {
+    for (int el = 1; el <= 8; el *= 2) {
+        if (D > 0 && D % el == 0 && D / el <= 32) return SCANW_WARPS * scanw_rows(el, elem_bytes_in);
+    }
+    return 0;
+}
+
+// Plan of the shared-memory scan kernel (the fallback); the look-back state in
+// scratch is sized for the smallest chunk either kernel may use (min_P).
 ScanPlan scan_plan(int64_t T, int64_t D, int dtype) {
     ScanPlan s;
     const int64_t per = (D > 0 ? D : 1) * acc_bytes(dtype);
@@ -93,12 +104,19 @@ ScanPlan scan_plan(int64_t T, int64_t D, int dtype) {
     if (P < 16) P = 16;
     P -= P % 8;
     s.P = static_cast<int>(P);
+    int min_p = s.P;
+    for (int eb : {elem_bytes(dtype), acc_bytes(dtype)}) {
+        const int pw = scanw_positions(D, eb);
+        if (pw > 0 && pw < min_p) min_p = pw;
+    }
+    s.min_P = min_p;
     const int ncol = D < 1 ? 1 : (D < SCAN_THREADS ? static_cast<int>(D) : SCAN_THREADS);
     int parts = SCAN_THREADS / ncol;
     if (parts < 1) parts = 1;
     if (parts > s.P) parts = s.P;
     s.parts = parts;
     s.nchunks = (T + s.P - 1) / s.P;
+    s.max_nchunks = (T + s.min_P - 1) / s.min_P;
     return s;
 }
 
@@ -112,7 +130,7 @@ ScratchLayout scratch_layout(int64_t B, int64_t T, int64_t C, int64_t D, int64_t
     const SortPlan sp = sort_plan(T);
     const ScanPlan sc = scan_plan(T, D, dtype);
     const size_t S = static_cast<size_t>(B * C), N = static_cast<size_t>(B * T * C);
-    const size_t nch = S * static_cast<size_t>(sc.nchunks);
+    const size_t nch = S * static_cast<size_t>(sc.max_nchunks);
     const size_t ab = static_cast<size_t>(acc_bytes(dtype));
     l.off_sort = 0;
     l.off_flags = align_up(sp.tiles > 1 ? S * static_cast<size_t>(T) * t.key_bytes : 0);
@@ -235,6 +253,33 @@ int tape_build(const void* waddr, const void* raddr, int addr_dtype, const uint8
 
     int rc = with_key(tl.kl.key64, [&](auto kt) -> int {
         using KeyT = decltype(kt);
+        bool sorted = false;
+        if (sp.tiles > 1 && sp.tiles <= 8) {
+            // one cluster of `tiles` CTAs per stream, straight into the tape
+            const size_t smem = cluster_sort_smem<1024, 8, KeyT>();
+            if (set_smem(k_cluster_sort<KeyT, 1024, 8>, smem) == RAVEL_OK) {
+                SortArgs ca = a;
+                ca.keys_out = tv.keys;
+                cudaLaunchConfig_t cfg = {};
+                cfg.gridDim = dim3(static_cast<unsigned>(S * sp.tiles));
+                cfg.blockDim = dim3(1024);
+                cfg.dynamicSmemBytes = smem;
+                cfg.stream = st;
+                cudaLaunchAttribute attr[1];
+                attr[0].id = cudaLaunchAttributeClusterDimension;
+                attr[0].val.clusterDim.x = static_cast<unsigned>(sp.tiles);
+                attr[0].val.clusterDim.y = 1;
+                attr[0].val.clusterDim.z = 1;
+                cfg.attrs = attr;
+                cfg.numAttrs = 1;
+                if (cudaLaunchKernelEx(&cfg, k_cluster_sort<KeyT, 1024, 8>, ca) == cudaSuccess) {
+                    if (int e = check_launch()) return e;
+                    sorted = true;
+                } else {
+                    (void)cudaGetLastError();  // not schedulable here: use tiles + merges
+                }
+            }
+        }
         auto launch = [&](auto th) -> int {
             constexpr int TH = decltype(th)::value;
             const size_t smem = tile_sort_smem<TH, 8, KeyT>();
@@ -242,20 +287,22 @@ int tape_build(const void* waddr, const void* raddr, int addr_dtype, const uint8
             k_tile_sort<KeyT, TH, 8><<<static_cast<unsigned>(grid), TH, smem, st>>>(a);
             return check_launch();
         };
-        int e;
-        switch (sp.threads) {
-            case 32: e = launch(IC<32>{}); break;
-            case 64: e = launch(IC<64>{}); break;
-            case 128: e = launch(IC<128>{}); break;
-            case 256: e = launch(IC<256>{}); break;
-            case 512: e = launch(IC<512>{}); break;
-            default: e = launch(IC<1024>{}); break;
+        int e = RAVEL_OK;
+        if (!sorted) {
+            switch (sp.threads) {
+                case 32: e = launch(IC<32>{}); break;
+                case 64: e = launch(IC<64>{}); break;
+                case 128: e = launch(IC<128>{}); break;
+                case 256: e = launch(IC<256>{}); break;
+                case 512: e = launch(IC<512>{}); break;
+                default: e = launch(IC<1024>{}); break;
+            }
         }
         if (e) return e;
         const KeyT* src = static_cast<const KeyT*>(first);
         int64_t run = static_cast<int64_t>(sp.threads) * 8;
         const int64_t cps = (T + MERGE_OUT - 1) / MERGE_OUT;
-        for (int pass = 0; pass < sp.merge_passes; ++pass) {
+        for (int pass = 0; pass < (sorted ? 0 : sp.merge_passes); ++pass) {
             KeyT* dst = (src == static_cast<const KeyT*>(tv.keys)) ? static_cast<KeyT*>(other)
                                                                   : static_cast<KeyT*>(tv.keys);
             k_merge<KeyT><<<static_cast<unsigned>(S * cps), MERGE_THREADS, 0, st>>>(src, dst, T, run, cps);
@@ -447,6 +494,74 @@ int launch_segscan(const TapeView& tv, const TapeLayout& tl, int64_t B, int64_t 
     a.fd_d = FastDiv(static_cast<uint32_t>(D > 0 ? D : 1));
     const int64_t nch = B * C * sp.nchunks;
     if (cudaMemsetAsync(a.flags, 0, sl.off_agg - sl.off_flags, st) != cudaSuccess) return RAVEL_ERR_CUDA;
+    // warp-register kernel when one warp access covers a row
+    using V = typename Elem<DT>::T;
+    int el = 0;
+    for (int cand = 1; cand <= 8; cand *= 2) {
+        if (D > 0 && D % cand == 0 && D / cand <= 32) { el = cand; break; }
+    }
+    if (el) {
+        const size_t in_es = in_sorted ? sizeof(Acc) : sizeof(V);
+        const size_t out_es = out_sorted ? sizeof(Acc) : sizeof(V);
+        const bool tma_ok = (D * in_es) % 16 == 0 && addr_bits(in) % 16 == 0 &&
+                            addr_bits(out) % (el * out_es) == 0 && SCANT_P >= sp.min_P &&
+                            segscan_t_smem<Acc>(D, in_es) <= 200 * 1024;
+        if (tma_ok) {
+            a.P = SCANT_P;
+            a.nchunks = (T + SCANT_P - 1) / SCANT_P;
+            const int64_t ncht = B * C * a.nchunks;
+            const size_t smem = segscan_t_smem<Acc>(D, in_es);
+            auto go = [&](auto elc, auto inc, auto outc) -> int {
+                constexpr int EL = decltype(elc)::value;
+                constexpr bool IS = decltype(inc)::value != 0;
+                constexpr bool OS = decltype(outc)::value != 0;
+                auto kern = k_segscan_t<KeyT, DT, EL, IS, OS>;
+                if (int e = set_smem(kern, smem)) return e;
+                kern<<<static_cast<unsigned>(ncht), SCANT_WARPS * 32, smem, st>>>(a);
+                return check_launch();
+            };
+            auto by_mode = [&](auto elc) -> int {
+                if (in_sorted) return go(elc, IC<1>{}, IC<0>{});
+                if (out_sorted) return go(elc, IC<0>{}, IC<1>{});
+                return go(elc, IC<0>{}, IC<0>{});
+            };
+            switch (el) {
+                case 1: return by_mode(IC<1>{});
+                case 2: return by_mode(IC<2>{});
+                case 4: return by_mode(IC<4>{});
+                default: return by_mode(IC<8>{});
+            }
+        }
+        const bool aligned = addr_bits(in) % (el * in_es) == 0 && addr_bits(out) % (el * out_es) == 0;
+        const int P = scanw_positions(D, static_cast<int>(in_es));
+        if (aligned && P >= sp.min_P) {
+            a.P = P;
+            a.nchunks = (T + P - 1) / P;
+            const int64_t nchw = B * C * a.nchunks;
+            const size_t smem = segscan_w_smem<Acc>(D);
+            auto go = [&](auto elc, auto inc, auto outc) -> int {
+                constexpr int EL = decltype(elc)::value;
+                constexpr bool IS = decltype(inc)::value != 0;
+                constexpr bool OS = decltype(outc)::value != 0;
+                constexpr int R = scanw_rows(EL, IS ? static_cast<int>(sizeof(Acc)) : static_cast<int>(sizeof(V)));
+                auto kern = k_segscan_w<KeyT, DT, EL, IS, OS, R>;
+                if (int e = set_smem(kern, smem)) return e;
+                kern<<<static_cast<unsigned>(nchw), SCANW_WARPS * 32, smem, st>>>(a);
+                return check_launch();
+            };
+            auto by_mode = [&](auto elc) -> int {
+                if (in_sorted) return go(elc, IC<1>{}, IC<0>{});
+                if (out_sorted) return go(elc, IC<0>{}, IC<1>{});
+                return go(elc, IC<0>{}, IC<0>{});
+            };
+            switch (el) {
+                case 1: return by_mode(IC<1>{});
+                case 2: return by_mode(IC<2>{});
+                case 4: return by_mode(IC<4>{});
+                default: return by_mode(IC<8>{});
+            }
+        }
+    }
     const size_t smem = segscan_smem<Acc>(sp.P, sp.parts, D);
     constexpr int EPV = 16 / sizeof(typename Elem<DT>::T);
     const bool vec = !in_sorted && !out_sorted && D % EPV == 0 && (addr_bits(in) % 16 == 0) &&
@@ -631,11 +746,11 @@ size_t ravel_tape_bytes(int64_t B, int64_t T, int64_t C, int64_t A, int tape_fla
     return tape_layout(B, T, C, A, tape_flags).total;
 }
 
-size_t ravel_scratch_bytes(int64_t B, int64_t T, int64_t C, int64_t D, int64_t A, int64_t k, int tape_flags) {
+size_t ravel_scratch_bytes(int64_t B, int64_t T, int64_t C, int64_t D, int64_t A, int64_t k, int dtype,
+                           int tape_flags) {
     (void)k;
-    if (B < 0 || T < 0 || C < 0 || D < 0 || A <= 0) return 0;
-    // float64 accumulators bound every dtype
-    return scratch_layout(B, T, C, D, A, RAVEL_F64, tape_flags).total;
+    if (B < 0 || T < 0 || C < 0 || D < 0 || A <= 0 || dtype < 0 || dtype > 3) return 0;
+    return scratch_layout(B, T, C, D, A, dtype, tape_flags).total;
 }
 
 int ravel_tape_build(const void* waddr, const void* raddr, int addr_dtype, const uint8_t* wmask, int64_t B,

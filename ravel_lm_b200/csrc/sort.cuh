@@ -19,6 +19,8 @@
 //                 to the stream.
 #pragma once
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 namespace ravel {
@@ -147,6 +149,143 @@ __global__ void __launch_bounds__(THREADS) k_tile_sort(SortArgs a) {
     const int64_t cnt = (T - t0) < TILE ? (T - t0) : TILE;
     KeyT* out = static_cast<KeyT*>(a.keys_out) + s * T + t0;
     for (int i = tid; i < cnt; i += THREADS) out[i] = ka[i];
+}
+
+// One stream per thread-block cluster: CTA r of the cluster loads tile r of the
+// stream (8192 steps), and every LSD pass ranks locally, exchanges the 256
+// digit totals of all CTAs through distributed shared memory, and scatters each
+// key straight into the shared memory of the CTA that owns its destination
+// (st.shared::cluster).  After the last pass CTA r holds sorted positions
+// [r*8192, (r+1)*8192) of the stream: no global round trips, no merge passes.
+// Used for streams of 2..8 tiles (T <= 65536); cluster size = tiles.
+template <typename KeyT, int THREADS, int ITEMS>
+__global__ void __launch_bounds__(THREADS) k_cluster_sort(SortArgs a) {
+    namespace cg = cooperative_groups;
+    constexpr int TILE = THREADS * ITEMS;
+    constexpr int NW = THREADS / 32;
+    extern __shared__ __align__(16) unsigned char smem[];
+    KeyT* ka = reinterpret_cast<KeyT*>(smem);
+    KeyT* kb = ka + TILE;
+    uint16_t* whist = reinterpret_cast<uint16_t*>(kb + TILE);
+    uint32_t* tot = reinterpret_cast<uint32_t*>(whist + NW * 256);  // this CTA's digit totals
+    uint32_t* dbase = tot + 256;                                    // destination base per digit
+    uint32_t* before = dbase + 256;                                 // keys of the digit in lower CTAs
+
+    cg::cluster_group cluster = cg::this_cluster();
+    const int crank = static_cast<int>(cluster.block_rank());
+    const int csize = static_cast<int>(cluster.num_blocks());
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t C = a.C, T = a.T;
+    const int64_t s = blockIdx.x / csize;
+    const int64_t b = s / C, c = s % C;
+    const int64_t t0 = static_cast<int64_t>(crank) * TILE;
+
+    int nvalid_local = 0;
+    for (int i = tid; i < TILE; i += THREADS) {
+        const int64_t t = t0 + i;
+        KeyT key;
+        if (t < T) {
+            const uint64_t ad = fold_addr(load_addr(a.waddr, (b * T + t) * C + c, a.addr_i64), a.A, a.key32);
+            const bool valid = a.wmask == nullptr || a.wmask[b * T + t] != 0;
+            if (valid) {
+                key = (static_cast<KeyT>(ad) << a.tbits) | static_cast<KeyT>(t);
+                ++nvalid_local;
+            } else {
+                key = (static_cast<KeyT>(1) << (a.tbits + a.abits)) | static_cast<KeyT>(t);
+            }
+        } else {
+            key = ~static_cast<KeyT>(0);
+        }
+        ka[i] = key;
+    }
+    if (a.nvalid != nullptr) {
+        const int w = __reduce_add_sync(0xffffffffu, static_cast<unsigned>(nvalid_local));
+        if (lane == 0 && w) atomicAdd(a.nvalid + s, w);
+    }
+    __syncthreads();
+
+    const int top = a.tbits + a.abits + a.mbit;
+    for (int shift = a.tbits; shift < top; shift += 8) {
+        const int nb = (top - shift) < 8 ? (top - shift) : 8;
+        const unsigned dmask = (1u << nb) - 1u;
+        for (int d = lane; d < 256; d += 32) whist[warp * 256 + d] = 0;
+        __syncwarp();
+        KeyT kv[ITEMS];
+        uint16_t loc[ITEMS];
+        uint16_t dig[ITEMS];
+#pragma unroll
+        for (int it = 0; it < ITEMS; ++it) {
+            const int idx = warp * (32 * ITEMS) + it * 32 + lane;
+            const KeyT key = ka[idx];
+            const unsigned d = static_cast<unsigned>(key >> shift) & dmask;
+            const unsigned peers = __match_any_sync(0xffffffffu, d);
+            const unsigned rank = __popc(peers & lanemask_lt());
+            const unsigned before = whist[warp * 256 + d];
+            __syncwarp();
+            if (rank == 0) whist[warp * 256 + d] = static_cast<uint16_t>(before + __popc(peers));
+            __syncwarp();
+            kv[it] = key;
+            loc[it] = static_cast<uint16_t>(before + rank);
+            dig[it] = static_cast<uint16_t>(d);
+        }
+        __syncthreads();
+        for (int d = tid; d < 256; d += THREADS) {
+            uint32_t run = 0;
+#pragma unroll 4
+            for (int w = 0; w < NW; ++w) {
+                const uint32_t v = whist[w * 256 + d];
+                whist[w * 256 + d] = static_cast<uint16_t>(run);
+                run += v;
+            }
+            tot[d] = run;
+        }
+        cluster.sync();  // every CTA's totals are visible cluster-wide
+        // per digit: keys of this digit in lower-ranked CTAs, and over the cluster
+        for (int d = tid; d < 256; d += THREADS) {
+            uint32_t lower = 0, all = 0;
+            for (int r = 0; r < csize; ++r) {
+                const uint32_t v = *cluster.map_shared_rank(tot + d, r);
+                if (r < crank) lower += v;
+                all += v;
+            }
+            dbase[d] = all;
+            before[d] = lower;
+        }
+        __syncthreads();
+        if (warp == 0) {  // exclusive scan of the cluster-wide digit totals
+            uint32_t v[8];
+            uint32_t sum = 0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) { v[i] = dbase[lane * 8 + i]; sum += v[i]; }
+            uint32_t incl = sum;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t n = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += n;
+            }
+            uint32_t run = incl - sum;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) { dbase[lane * 8 + i] = run + before[lane * 8 + i]; run += v[i]; }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int it = 0; it < ITEMS; ++it) {
+            const uint32_t dst = dbase[dig[it]] + whist[warp * 256 + dig[it]] + loc[it];
+            KeyT* remote = cluster.map_shared_rank(kb, static_cast<int>(dst / TILE));
+            remote[dst % TILE] = kv[it];
+        }
+        cluster.sync();  // all keys have landed before anyone reads them or reuses tot
+        KeyT* tmp = ka; ka = kb; kb = tmp;
+    }
+
+    const int64_t cnt = (T - t0) < TILE ? (T - t0) : TILE;
+    KeyT* out = static_cast<KeyT*>(a.keys_out) + s * T + t0;
+    for (int i = tid; i < cnt; i += THREADS) out[i] = ka[i];
+}
+
+template <int THREADS, int ITEMS, typename KeyT>
+inline size_t cluster_sort_smem() {
+    return 2 * sizeof(KeyT) * THREADS * ITEMS + sizeof(uint16_t) * (THREADS / 32) * 256 + 4 * 768;
 }
 
 template <int THREADS, int ITEMS, typename KeyT>

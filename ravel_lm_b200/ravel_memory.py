@@ -114,15 +114,76 @@ def tape_bytes(B: int, T: int, C: int, A: int, flags: int) -> int:
     return int(_lib.load().ravel_tape_bytes(B, T, C, A, flags))
 
 
-def scratch_bytes(B: int, T: int, C: int, D: int, A: int, k: int, flags: int) -> int:
-    return int(_lib.load().ravel_scratch_bytes(B, T, C, D, A, k, flags))
+def scratch_bytes(B: int, T: int, C: int, D: int, A: int, k: int, dtype_code: int, flags: int) -> int:
+    return int(_lib.load().ravel_scratch_bytes(B, T, C, D, A, k, dtype_code, flags))
+
+
+class _TapeCache:
+    """The last sorted tape, reused when the next lookup sees the same addresses.
+
+    ``RavelMemoryLayer.forward`` calls ``causal_last_k_lookup`` and then
+    ``causal_sum_lookup`` on the same address tensors; both sort the same
+    write events.  The cache keeps the last tape and returns it when the write
+    / read / mask tensors are the very same objects (checked through weak
+    references, so a freed tensor whose memory is reused never matches), none
+    of them was modified in place since (torch version counters), and the
+    address space, flags and stream agree.  It is bypassed while a CUDA graph
+    is being captured.  Writing into an address tensor behind torch's back
+    (raw pointers) is not detected: call ``clear_tape_cache()`` after that.
+    """
+
+    def __init__(self):
+        self.key = None
+        self.refs = None
+        self.value = None
+
+    @staticmethod
+    def _key(write, read, mask, A, stream):
+        return (A, _flags(read, mask), tuple(write.shape), write.dtype, write.device, stream, write._version,
+                None if read is None else (read.dtype, read._version),
+                None if mask is None else (mask.dtype, mask._version))
+
+    def get(self, write, read, mask, A, stream):
+        if self.key is None or torch.cuda.is_current_stream_capturing():
+            return None
+        if self._key(write, read, mask, A, stream) != self.key:
+            return None
+        w, r, m = (ref() if ref is not None else None for ref in self.refs)
+        if w is not write or r is not read or m is not mask:
+            return None
+        return self.value
+
+    def put(self, write, read, mask, A, stream, value):
+        if torch.cuda.is_current_stream_capturing():
+            return
+        import weakref
+        self.key = self._key(write, read, mask, A, stream)
+        self.refs = tuple(None if t is None else weakref.ref(t) for t in (write, read, mask))
+        self.value = value
+
+    def clear(self):
+        self.key = self.refs = self.value = None
+
+
+_tape_cache = _TapeCache()
+
+
+def clear_tape_cache() -> None:
+    """Forget the cached tape (see ``_TapeCache``)."""
+    _tape_cache.clear()
 
 
 def _build_tape(write: Tensor, read: Optional[Tensor], write_mask: Optional[Tensor], A: int, D: int, k: int,
-                device: torch.device) -> Tuple[Tensor, Tensor, Tensor, int, int]:
+                dcode: int, device: torch.device) -> Tuple[Tensor, Tensor, Tensor, int, int]:
     """Sort the write events; returns (tape, scratch, read-or-write addresses, addr code, flags)."""
     B, T, C = write.shape
     flags = _flags(read, write_mask)
+    st = _stream(device)
+    hit = _tape_cache.get(write, read, write_mask, A, st)
+    if hit is not None:
+        tape, r, code = hit
+        scratch = torch.empty(scratch_bytes(B, T, C, D, A, k, dcode, flags), dtype=torch.uint8, device=device)
+        return tape, scratch, r, code, flags
     w, code = _addr(write)
     if read is not None:
         r, rcode = _addr(read)
@@ -135,10 +196,10 @@ def _build_tape(write: Tensor, read: Optional[Tensor], write_mask: Optional[Tens
     if write_mask is not None:
         m = write_mask.to(torch.bool).contiguous()
     tape = torch.empty(tape_bytes(B, T, C, A, flags), dtype=torch.uint8, device=device)
-    scratch = torch.empty(scratch_bytes(B, T, C, D, A, k, flags), dtype=torch.uint8, device=device)
-    st = _stream(device)
+    scratch = torch.empty(scratch_bytes(B, T, C, D, A, k, dcode, flags), dtype=torch.uint8, device=device)
     _lib.call("ravel_tape_build", w.data_ptr(), r.data_ptr() if read is not None else None, code, _ptr(m),
               B, T, C, A, flags, tape.data_ptr(), tape.numel(), scratch.data_ptr(), scratch.numel(), st)
+    _tape_cache.put(write, read, write_mask, A, st, (tape, r, code))
     return tape, scratch, r, code, flags
 
 
@@ -151,7 +212,8 @@ def _latestk_fwd(write: Tensor, payload: Tensor, read: Optional[Tensor], write_m
     device = _require_cuda(write, payload, read, write_mask)
     vals = payload.new_empty(B, T, C, k, D)
     mask = torch.empty(B, T, C, k, dtype=torch.bool, device=device)
-    tape, _scratch, r, code, flags = _build_tape(write, read, write_mask, address_space, D, k, device)
+    tape, _scratch, r, code, flags = _build_tape(write, read, write_mask, address_space, D, k,
+                                                 _payload_code(payload), device)
     p = payload.contiguous()
     _lib.call("ravel_latestk_fwd_tape", tape.data_ptr(), flags, r.data_ptr() if flags else None, code,
               p.data_ptr(), _payload_code(p), B, T, C, D, address_space, k, vals.data_ptr(), mask.data_ptr(),
@@ -176,7 +238,8 @@ def _latestk_bwd(tape: Tensor, grad_vals: Tensor, raddr: Tensor, flags: int, B: 
     device = _require_cuda(tape, grad_vals)
     g = grad_vals.contiguous()
     grad = torch.empty(B, T, C, D, dtype=g.dtype, device=device)
-    scratch = torch.empty(scratch_bytes(B, T, C, D, address_space, k, flags), dtype=torch.uint8, device=device)
+    scratch = torch.empty(scratch_bytes(B, T, C, D, address_space, k, _payload_code(g), flags),
+                          dtype=torch.uint8, device=device)
     r, code = _addr(raddr)
     _lib.call("ravel_latestk_bwd", tape.data_ptr(), flags, r.data_ptr() if flags else None, code,
               g.data_ptr(), _payload_code(g), B, T, C, D, address_space, k, grad.data_ptr(), scratch.data_ptr(),
@@ -195,6 +258,7 @@ def _latestk_setup(ctx, inputs, output):
     ctx.save_for_backward(tape, write if read is None else read)
     ctx.meta = (_flags(read, write_mask), *write.shape, int(address_space), int(k))
     ctx.mark_non_differentiable(mask, tape)
+    ctx.set_materialize_grads(False)
 
 
 def _latestk_backward(ctx, grad_vals, _gm, _gt):
@@ -218,7 +282,8 @@ def _segsum_fwd(write: Tensor, payload: Tensor, read: Optional[Tensor], write_ma
     device = _require_cuda(write, payload, read, write_mask)
     sums = payload.new_empty(B, T, C, D)
     mask = torch.empty(B, T, C, dtype=torch.bool, device=device)
-    tape, scratch, r, code, flags = _build_tape(write, read, write_mask, address_space, D, 1, device)
+    tape, scratch, r, code, flags = _build_tape(write, read, write_mask, address_space, D, 1,
+                                                _payload_code(payload), device)
     p = payload.contiguous()
     _lib.call("ravel_segsum_fwd_tape", tape.data_ptr(), flags, r.data_ptr() if flags else None, code,
               p.data_ptr(), _payload_code(p), B, T, C, D, address_space, sums.data_ptr(), mask.data_ptr(),
@@ -243,7 +308,8 @@ def _segsum_bwd(tape: Tensor, grad_sums: Tensor, raddr: Tensor, flags: int, B: i
     device = _require_cuda(tape, grad_sums)
     g = grad_sums.contiguous()
     grad = torch.empty(B, T, C, D, dtype=g.dtype, device=device)
-    scratch = torch.empty(scratch_bytes(B, T, C, D, address_space, 1, flags), dtype=torch.uint8, device=device)
+    scratch = torch.empty(scratch_bytes(B, T, C, D, address_space, 1, _payload_code(g), flags),
+                          dtype=torch.uint8, device=device)
     r, code = _addr(raddr)
     _lib.call("ravel_segsum_bwd", tape.data_ptr(), flags, r.data_ptr() if flags else None, code,
               g.data_ptr(), _payload_code(g), B, T, C, D, address_space, grad.data_ptr(), scratch.data_ptr(),
@@ -262,6 +328,7 @@ def _segsum_setup(ctx, inputs, output):
     ctx.save_for_backward(tape, write if read is None else read)
     ctx.meta = (_flags(read, write_mask), *write.shape, int(address_space))
     ctx.mark_non_differentiable(mask, tape)
+    ctx.set_materialize_grads(False)
 
 
 def _segsum_backward(ctx, grad_sums, _gm, _gt):
@@ -439,4 +506,5 @@ class RavelLayerCache:
         return vals, mask
 
 
-__all__ = ["RavelLayerCache", "causal_last_k_lookup", "causal_sum_lookup", "_composite_key_dtype"]
+__all__ = ["RavelLayerCache", "causal_last_k_lookup", "causal_sum_lookup", "clear_tape_cache",
+           "_composite_key_dtype"]

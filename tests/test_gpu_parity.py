@@ -115,6 +115,11 @@ CASES = [
     ("d1_k_gt_t", 3, 5, 2, 1, 3, 8, torch.float32, False, False, "uniform"),
     ("key64", 2, 4096, 2, 8, 2**31, 2, torch.float32, False, False, "huge"),
     ("key64_general", 2, 3000, 2, 8, 2**31, 2, torch.float32, True, True, "huge"),
+    ("wide_d300_fallback", 2, 700, 2, 300, 60, 2, torch.float32, True, True, "uniform"),
+    ("d33_fallback_bf16", 2, 900, 3, 33, 70, 3, torch.bfloat16, False, False, "uniform"),
+    ("d256_bf16_el8", 1, 3000, 2, 256, 90, 2, torch.bfloat16, False, False, "uniform"),
+    ("d128_f32_el4", 1, 2500, 2, 128, 40, 2, torch.float32, True, False, "uniform"),
+    ("d48_f64_el2", 1, 1700, 2, 48, 30, 2, torch.float64, False, True, "uniform"),
 ]
 
 
@@ -184,7 +189,8 @@ def test_config3_full(oracle_mod):
 
 
 @pytest.mark.parametrize("T,A,mask", [(256, 256, False), (300, 50, False), (20000, 65536, False),
-                                      (1500, 40, True), (5, 3, False)])
+                                      (1500, 40, True), (5, 3, False), (65536, 4096, False),
+                                      (70000, 1000, True), (16385, 2**20, True)])
 def test_tape_sort_order(oracle_mod, T, A, mask):
     """The per-stream sorted keys of the tape equal the reference's sort order."""
     import ravel_lm_b200.ravel_memory as rm
@@ -213,3 +219,31 @@ def test_tape_sort_order(oracle_mod, T, A, mask):
         exp = (addr[pos:pos + n].astype(np.int64) << tbits) | t[pos:pos + n]
         assert np.array_equal(got, exp), f"stream {s}: sorted keys differ at {np.argwhere(got != exp)[:5].ravel()}"
         pos += n
+
+
+def test_tape_cache_reuse_and_invalidation():
+    """causal_sum_lookup after causal_last_k_lookup on the same tensors reuses the
+    sorted tape; an in-place change of the addresses must not."""
+    import ravel_lm_b200.ravel_memory as rm
+    from ravel_lm_b200 import causal_last_k_lookup, causal_sum_lookup
+    g = torch.Generator().manual_seed(21)
+    B, T, C, D, A = 2, 3000, 3, 16, 50
+    w = torch.randint(0, A, (B, T, C), generator=g).cuda()
+    p = torch.randn(B, T, C, D, generator=g).cuda()
+    rm.clear_tape_cache()
+    causal_last_k_lookup(w, p, address_space=A, k=2)
+    hit = rm._tape_cache.get(w, None, None, A, torch.cuda.current_stream().cuda_stream)
+    assert hit is not None
+    s_cached, m_cached = causal_sum_lookup(w, p, address_space=A)
+    rm.clear_tape_cache()
+    s_fresh, m_fresh = causal_sum_lookup(w, p, address_space=A)
+    assert torch.equal(s_cached, s_fresh) and torch.equal(m_cached, m_fresh)
+    # in-place edit after the latest-k call: the sum must see the new addresses
+    causal_last_k_lookup(w, p, address_space=A, k=2)
+    w[:, ::2] = (w[:, ::2] + 7) % A
+    assert rm._tape_cache.get(w, None, None, A, torch.cuda.current_stream().cuda_stream) is None
+    s_new, _ = causal_sum_lookup(w, p, address_space=A)
+    rm.clear_tape_cache()
+    s_ref, _ = causal_sum_lookup(w, p, address_space=A)
+    assert torch.equal(s_new, s_ref)
+    assert not torch.equal(s_new, s_fresh)

@@ -46,7 +46,7 @@ def test_tape_and_scratch_sizes():
     # 64-bit keys when address + time bits exceed 32
     assert lib.ravel_tape_bytes(1, 4096, 1, 2**31, 0) >= 4096 * 8
     assert lib.ravel_tape_bytes(1, 4, 1, 0, 0) == 0  # A must be positive
-    s = lib.ravel_scratch_bytes(4, 32768, 16, 64, 65536, 8, 0)
+    s = lib.ravel_scratch_bytes(4, 32768, 16, 64, 65536, 8, L.RAVEL_BF16, 0)
     assert s > 0
 
 

@@ -50,7 +50,7 @@ def _allocating(L, w, r, m, p, A):
     B, T, C, D = p.shape
     fl = _flags(L, r, m)
     tape = torch.empty(lib.ravel_tape_bytes(B, T, C, A, fl), dtype=torch.uint8, device="cuda")
-    scratch = torch.empty(lib.ravel_scratch_bytes(B, T, C, D, A, 1, fl), dtype=torch.uint8, device="cuda")
+    scratch = torch.empty(lib.ravel_scratch_bytes(B, T, C, D, A, 1, _code(p.dtype), fl), dtype=torch.uint8, device="cuda")
     sums = torch.empty_like(p)
     mask = torch.empty(B, T, C, dtype=torch.bool, device="cuda")
     st = torch.cuda.current_stream().cuda_stream
@@ -97,7 +97,7 @@ def test_no_alloc_refuses_sizes_beyond_its_array():
     import ravel_lm_b200._lib as L
     lib = L.load()
     B, T, C, D, A = 4, 32768, 16, 256, 65536  # tape + scratch well above the array
-    need = lib.ravel_tape_bytes(B, T, C, A, 0) + lib.ravel_scratch_bytes(B, T, C, D, A, 1, 0)
+    need = lib.ravel_tape_bytes(B, T, C, A, 0) + lib.ravel_scratch_bytes(B, T, C, D, A, 1, L.RAVEL_F32, 0)
     assert need > L.RAVEL_NOALLOC_SCRATCH_BYTES
     w = torch.zeros(1, dtype=torch.int64, device="cuda")  # never read: the call is refused first
     out = torch.zeros(1, device="cuda")
