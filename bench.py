@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-streams", type=int, default=8, help="streams in the CPU baseline sample")
     ap.add_argument("--batch", type=int, default=None, help="override B per GPU (small profiling cases)")
+    ap.add_argument("--ops", choices=["all", "lk", "ss"], default="all",
+                    help="ops in a step (profiling a single op; the benchmark runs all)")
     return ap.parse_args()
 
 
@@ -314,6 +316,9 @@ def main():
     dev = torch.device("cuda", local)
     seed = 1000 + cfg.cfg + 7919 * rank
     x = make_inputs(cfg, seed=seed, device=dev)
+    if args.ops == "ss":  # the latest-k gradient is not needed
+        x["g_vals"] = None
+        torch.cuda.empty_cache()
     w, r = x["write"], x["read"]
     p = x["payload"].requires_grad_(True)
     gv, gs = x["g_vals"], x["g_sums"]
@@ -324,9 +329,16 @@ def main():
         # (only the latest-k -> sum reuse inside one step is legitimate).
         clear_tape_cache()
         p.grad = None
-        vals, _m = causal_last_k_lookup(w, p, r, address_space=A, k=k)
-        sums, _s = causal_sum_lookup(w, p, r, address_space=A)
-        torch.autograd.backward([vals, sums], [gv, gs])
+        outs, grads = [], []
+        if args.ops in ("all", "lk"):
+            vals, _m = causal_last_k_lookup(w, p, r, address_space=A, k=k)
+            outs.append(vals)
+            grads.append(gv)
+        if args.ops in ("all", "ss"):
+            sums, _s = causal_sum_lookup(w, p, r, address_space=A)
+            outs.append(sums)
+            grads.append(gs)
+        torch.autograd.backward(outs, grads)
 
     for _ in range(args.warmup):
         step()

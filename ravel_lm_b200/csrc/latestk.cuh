@@ -41,9 +41,25 @@ struct LkArgs {
     int P;                  // sorted positions per CTA (fast path)
     int64_t nchunks;        // chunks per stream (fast path)
     FastDiv fd_rv, fd_bv, fd_k;  // divisions by vectors-per-row, vectors-per-block, k
+    FastDiv fd_C, fd_T;          // flat row -> (b, t, c)
 };
 
-// Flat payload row of (stream s, time t).
+// Flat payload row of (stream s, time t) = ((s / C) * T + t) * C + s % C,
+// computed as base + t*C with the stream's base precomputed once (rows are
+// below 2^31: the entry points reject larger B*T*C).
+struct RowMap {
+    uint32_t base, C;
+    __device__ __forceinline__ RowMap(int64_t s, int64_t T, int64_t Cn) {
+        const int64_t b = s / Cn, c = s - (s / Cn) * Cn;
+        base = static_cast<uint32_t>(b * T * Cn + c);
+        C = static_cast<uint32_t>(Cn);
+    }
+    __device__ __forceinline__ uint32_t operator()(uint64_t t) const {
+        return base + static_cast<uint32_t>(t) * C;
+    }
+};
+
+// Row of (stream s, time t) for a stream that is not the thread's own (rare paths).
 __device__ __forceinline__ int64_t flat_row(int64_t s, int64_t t, int64_t T, int64_t C) {
     return ((s / C) * T + t) * C + (s % C);
 }
@@ -68,15 +84,22 @@ __global__ void __launch_bounds__(256) k_lk_fwd_fast(LkArgs a) {
     const KeyT* keys = static_cast<const KeyT*>(a.keys);
     const KeyT tmask = (static_cast<KeyT>(1) << a.tbits) - 1;
 
+    const RowMap rows_of(s, T, C);
     for (int i = tid; i < nw; i += 256) {
         const int64_t p = p0 - k + i;
-        int64_t g = s * T + p;          // position in the reference's global order
-        uint64_t ad = ~0ull;            // "other stream": never matches
-        if (g < 0) g = 0;               // ravel_memory.py:163 clamp_min(0)
-        const KeyT key = keys[g];
-        if (p >= 0) ad = static_cast<uint64_t>(key >> a.tbits);
-        wrow[i] = flat_row(g / T, static_cast<int64_t>(key & tmask), T, C);
-        wadr[i] = ad;
+        if (p >= 0) {
+            const KeyT key = keys[s * T + p];
+            wrow[i] = rows_of(key & tmask);
+            wadr[i] = static_cast<uint64_t>(key >> a.tbits);
+        } else {
+            // candidate in an earlier stream of the reference's global order:
+            // never valid, only its sign bits are used (ravel_memory.py:163 clamp)
+            int64_t g = s * T + p;
+            if (g < 0) g = 0;
+            const KeyT key = keys[g];
+            wrow[i] = flat_row(g / T, static_cast<int64_t>(key & tmask), T, C);
+            wadr[i] = ~0ull;
+        }
     }
     __syncthreads();
 
@@ -176,9 +199,10 @@ __global__ void __launch_bounds__(256) k_lk_bwd_fast(LkArgs a) {
     const int nw = static_cast<int>((np + k) < avail ? (np + k) : avail);
     const KeyT* keys = static_cast<const KeyT*>(a.keys) + s * T;
     const KeyT tmask = (static_cast<KeyT>(1) << a.tbits) - 1;
+    const RowMap rows_of(s, T, C);
     for (int i = tid; i < nw; i += 256) {
         const KeyT key = keys[q0 + i];
-        wrow[i] = flat_row(s, static_cast<int64_t>(key & tmask), T, C);
+        wrow[i] = rows_of(key & tmask);
         wadr[i] = static_cast<uint64_t>(key >> a.tbits);
     }
     __syncthreads();
@@ -216,8 +240,10 @@ inline size_t lk_bwd_fast_smem(int P, int64_t k) { return static_cast<size_t>(P 
 template <typename KeyT>
 __device__ __forceinline__ void general_candidate(const LkArgs& a, int64_t r, int j, int64_t& row, bool& valid) {
     const int64_t T = a.T, C = a.C;
-    const int64_t c = r % C, b = r / (C * T);
-    const int64_t s = b * C + c;
+    uint32_t bt, c32, b32, t32;
+    a.fd_C.divmod(static_cast<uint32_t>(r), bt, c32);  // r = (b*T + t)*C + c
+    a.fd_T.divmod(bt, b32, t32);
+    const int64_t s = static_cast<int64_t>(b32) * C + c32;
     const KeyT* keys = static_cast<const KeyT*>(a.keys);
     const KeyT tmask = (static_cast<KeyT>(1) << a.tbits) - 1;
     const int64_t S = a.B * C;
@@ -227,7 +253,7 @@ __device__ __forceinline__ void general_candidate(const LkArgs& a, int64_t r, in
         const KeyT key = keys[s * T + q];
         const uint64_t ra = fold_addr(load_addr(a.raddr, r, a.addr_i64), a.A, a.key32);
         valid = static_cast<uint64_t>(key >> a.tbits) == ra;
-        row = flat_row(s, static_cast<int64_t>(key & tmask), T, C);
+        row = r + (static_cast<int64_t>(key & tmask) - static_cast<int64_t>(t32)) * C;  // same (b, c), time t'
         return;
     }
     // Candidate before this stream in the global sorted order (always invalid):

@@ -120,8 +120,40 @@ ScanPlan scan_plan(int64_t T, int64_t D, int dtype) {
     return s;
 }
 
+// Ranges per stream for the range scan: exactly one wave of CTAs (`slots` =
+// resident CTAs per SM x SMs) over all streams, at least one 256-position chunk
+// per range.  Scratch is sized for the most ranges any plan can use.
+struct RangePlan {
+    int64_t R, RL;
+};
+
+RangePlan range_plan(int64_t S, int64_t T, int64_t slots) {
+    RangePlan p;
+    int64_t R = S > 0 ? slots / S : 1;
+    if (R < 1) R = 1;
+    int64_t RL = (T + R - 1) / R;
+    RL = (RL + 31) / 32 * 32;
+    if (RL < 64) RL = 64;
+    p.RL = RL;
+    p.R = T > 0 ? (T + RL - 1) / RL : 1;
+    return p;
+}
+
+int64_t max_ranges(int64_t T) { return T > 0 ? (T + 63) / 64 : 1; }
+
+int sm_count() {
+    static int n = 0;
+    if (n == 0) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+            n = 148;
+    }
+    return n;
+}
+
 struct ScratchLayout {
-    size_t off_sort, off_flags, off_ticket, off_agg, off_incl, off_big, total;
+    size_t off_sort, off_flags, off_ticket, off_agg, off_incl, off_tail, off_tail_hs, off_bounds, off_big, total;
 };
 
 ScratchLayout scratch_layout(int64_t B, int64_t T, int64_t C, int64_t D, int64_t A, int dtype, int flags) {
@@ -137,7 +169,11 @@ ScratchLayout scratch_layout(int64_t B, int64_t T, int64_t C, int64_t D, int64_t
     l.off_ticket = l.off_flags + align_up(nch * 4);
     l.off_agg = l.off_ticket + 256;
     l.off_incl = l.off_agg + align_up(nch * static_cast<size_t>(D) * ab);
-    l.off_big = l.off_incl + align_up(nch * static_cast<size_t>(D) * ab);
+    const size_t nr = S * static_cast<size_t>(max_ranges(T));
+    l.off_tail = l.off_incl + align_up(nch * static_cast<size_t>(D) * ab);
+    l.off_tail_hs = l.off_tail + align_up(nr * static_cast<size_t>(D) * ab);
+    l.off_bounds = l.off_tail_hs + align_up(nr * 4);
+    l.off_big = l.off_bounds + align_up((nr + S) * 8);
     l.total = l.off_big + (t.general ? align_up(N * static_cast<size_t>(D) * ab) : 0);
     return l;
 }
@@ -322,6 +358,8 @@ int tape_build(const void* waddr, const void* raddr, int addr_dtype, const uint8
             q.B = B; q.T = T; q.C = C; q.A = A;
             q.tbits = tl.kl.tbits;
             q.ridx = tv.ridx;
+            q.fd_C = FastDiv(static_cast<uint32_t>(C));
+            q.fd_T = FastDiv(static_cast<uint32_t>(T));
             k_read_search<KeyT><<<grid_cap((N + 255) / 256), 256, 0, st>>>(q);
             if (int e2 = check_launch()) return e2;
         }
@@ -345,6 +383,8 @@ LkArgs lk_args(const TapeView& tv, const TapeLayout& tl, const void* raddr, int 
     a.B = B; a.T = T; a.C = C; a.D = D; a.A = A; a.k = k;
     a.tbits = tl.kl.tbits;
     a.row_bytes = D * elem_bytes(dtype);
+    a.fd_C = FastDiv(static_cast<uint32_t>(C > 0 ? C : 1));
+    a.fd_T = FastDiv(static_cast<uint32_t>(T > 0 ? T : 1));
     return a;
 }
 
@@ -503,21 +543,44 @@ int launch_segscan(const TapeView& tv, const TapeLayout& tl, int64_t B, int64_t 
     if (el) {
         const size_t in_es = in_sorted ? sizeof(Acc) : sizeof(V);
         const size_t out_es = out_sorted ? sizeof(Acc) : sizeof(V);
-        const bool tma_ok = (D * in_es) % 16 == 0 && addr_bits(in) % 16 == 0 &&
-                            addr_bits(out) % (el * out_es) == 0 && SCANT_P >= sp.min_P &&
-                            segscan_t_smem<Acc>(D, in_es) <= 200 * 1024;
-        if (tma_ok) {
-            a.P = SCANT_P;
-            a.nchunks = (T + SCANT_P - 1) / SCANT_P;
-            const int64_t ncht = B * C * a.nchunks;
-            const size_t smem = segscan_t_smem<Acc>(D, in_es);
+        const bool range_ok = (D * in_es) % 16 == 0 && addr_bits(in) % 16 == 0 &&
+                              addr_bits(out) % (el * out_es) == 0 &&
+                              range_scan_smem<Acc>(D, in_es) <= 200 * 1024;
+        if (range_ok) {
+            RangeArgs ra;
+            ra.keys = tv.keys;
+            ra.nvalid = tv.nvalid;
+            ra.T = T; ra.C = C;
+            ra.D = static_cast<uint32_t>(D);
+            ra.tbits = tl.kl.tbits;
+            ra.reverse = reverse;
+            ra.inclusive = inclusive;
+            ra.in = in; ra.out = out; ra.out_mask = out_mask;
+            ra.tail = sc + sl.off_tail;
+            ra.tail_hs = reinterpret_cast<uint32_t*>(sc + sl.off_tail_hs);
+            ra.bounds = reinterpret_cast<int64_t*>(sc + sl.off_bounds);
+            ra.fd_vpr = FastDiv(static_cast<uint32_t>(D * in_es / 16));
+            const size_t smem = range_scan_smem<Acc>(D, in_es);
             auto go = [&](auto elc, auto inc, auto outc) -> int {
                 constexpr int EL = decltype(elc)::value;
                 constexpr bool IS = decltype(inc)::value != 0;
                 constexpr bool OS = decltype(outc)::value != 0;
-                auto kern = k_segscan_t<KeyT, DT, EL, IS, OS>;
+                auto kern = inclusive ? k_range_scan<KeyT, DT, EL, IS, OS, true>
+                                      : k_range_scan<KeyT, DT, EL, IS, OS, false>;
                 if (int e = set_smem(kern, smem)) return e;
-                kern<<<static_cast<unsigned>(ncht), SCANT_WARPS * 32, smem, st>>>(a);
+                int occ = 0;
+                if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, RS_WARPS * 32, smem) != cudaSuccess ||
+                    occ < 1)
+                    occ = 1;
+                // one range per warp, one wave of warps
+                const RangePlan rp = range_plan(B * C, T, static_cast<int64_t>(occ) * RS_WARPS * sm_count());
+                ra.R = rp.R;
+                ra.RL = rp.RL;
+                ra.S = B * C;
+                const int64_t nranges = B * C * rp.R;
+                k_range_tail<KeyT, DT, EL, IS><<<static_cast<unsigned>(nranges), RS_WARPS * 32, 0, st>>>(ra);
+                if (int e = check_launch()) return e;
+                kern<<<static_cast<unsigned>((nranges + RS_WARPS - 1) / RS_WARPS), RS_WARPS * 32, smem, st>>>(ra);
                 return check_launch();
             };
             auto by_mode = [&](auto elc) -> int {
@@ -612,6 +675,8 @@ int ss_fwd_tape(const void* tape, int flags, const void* raddr, int addr_dtype, 
             g.key32 = key32_of(B, T, C, A);
             g.B = B; g.T = T; g.C = C; g.D = D; g.A = A;
             g.tbits = tl.kl.tbits;
+            g.fd_C = FastDiv(static_cast<uint32_t>(C));
+            g.fd_T = FastDiv(static_cast<uint32_t>(T));
             g.tapebuf = tapebuf;
             g.out = out_sums;
             g.out_mask = out_mask;
@@ -656,6 +721,8 @@ int ss_bwd(const void* tape, int flags, const void* raddr, int addr_dtype, const
             g.key32 = key32_of(B, T, C, A);
             g.B = B; g.T = T; g.C = C; g.D = D; g.A = A;
             g.tbits = tl.kl.tbits;
+            g.fd_C = FastDiv(static_cast<uint32_t>(C));
+            g.fd_T = FastDiv(static_cast<uint32_t>(T));
             g.accbuf = accbuf;
             g.grad = grad_sums;
             k_ss_scatter<KeyT, DT><<<grid_cap((N * 32 + 255) / 256), 256, 0, st>>>(g);

@@ -52,6 +52,7 @@ struct ScanArgs {
     Acc* agg;                // [S*nchunks, D]
     Acc* incl;               // [S*nchunks, D]
     FastDiv fd_d;
+    FastDiv fd_vpr;          // 16-byte vectors per staged row
 };
 
 template <typename KeyT, int DT, bool VEC>
@@ -89,13 +90,14 @@ __global__ void __launch_bounds__(SCAN_THREADS) k_segscan(ScanArgs<typename Elem
     const KeyT* keys = static_cast<const KeyT*>(a.keys) + s * T;
     const KeyT tmask = (static_cast<KeyT>(1) << a.tbits) - 1;
 
+    const RowMap rows_of(s, T, C);
     // tape positions in scan order
     for (int i = tid; i < np; i += SCAN_THREADS) {
         const int64_t si = i0 + i;
         const int64_t p = a.reverse ? (n_s - 1 - si) : si;
         const KeyT key = keys[p];
         sadr[i] = static_cast<uint64_t>(key >> a.tbits);
-        srow[i] = flat_row(s, static_cast<int64_t>(key & tmask), T, C);
+        srow[i] = rows_of(key & tmask);
         if (a.in_sorted || a.out_sorted) srow[i] = (srow[i] << 32) | p;  // pack (flat row, tape index)
     }
     __syncthreads();
@@ -380,18 +382,31 @@ __device__ __forceinline__ void windowed_lookback(unsigned* flags, const Acc* ag
             if (f == 3u) flag_error(RAVEL_DEVERR_SPIN);
         }
         const unsigned term = __ballot_sync(0xffffffffu, f >= 2u);
-        const int stop = term ? __ffs(term) - 1 : 31;
-        for (int c = 0; c <= stop; ++c) {
-            const unsigned fc = __shfl_sync(0xffffffffu, f, c);
-            const int64_t jc = j - c;
-            if (jc < jmin || fc == 3u) break;
-            const Acc* src = (fc == 2u) ? incl + jc * D : agg + jc * D;
-            if (active) {
+        int stop = term ? __ffs(term) - 1 : 31;
+        // never step past the stream's first chunk or a timed-out slot
+        const unsigned bad = __ballot_sync(0xffffffffu, (j - lane) < jmin || f == 3u);
+        if (bad) {
+            const int b = __ffs(bad) - 1;
+            if (b <= stop) stop = b - 1 + ((j - b) >= jmin && __shfl_sync(0xffffffffu, f, b) == 2u ? 1 : 0);
+        }
+        // add the published vectors of chunks j .. j-stop, eight loads in flight
+        for (int c0 = 0; c0 <= stop; c0 += 8) {
+            Acc tmp[8][EL];
 #pragma unroll
-                for (int q = 0; q < EL; ++q) cin[q] += src[col + q];
+            for (int u = 0; u < 8; ++u) {
+                const int c = c0 + u;
+                const unsigned fc = __shfl_sync(0xffffffffu, f, c & 31);
+                const Acc* src = (fc == 2u) ? incl + (j - c) * D : agg + (j - c) * D;
+#pragma unroll
+                for (int q = 0; q < EL; ++q) tmp[u][q] = (c <= stop && active) ? src[col + q] : Acc(0);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+#pragma unroll
+                for (int q = 0; q < EL; ++q) cin[q] += tmp[u][q];
             }
         }
-        if (term) return;
+        if (term || bad) return;
         j -= 32;
     }
 }
@@ -440,7 +455,7 @@ __global__ void __launch_bounds__(SCANW_WARPS * 32) k_segscan_w(ScanArgs<typenam
         const int64_t si = w0 + lane;
         const int64_t p = a.reverse ? (n_s - 1 - si) : si;
         const KeyT key = keys[p];
-        my_flat = static_cast<uint32_t>(flat_row(s, static_cast<int64_t>(key & tmask), T, C));
+        my_flat = RowMap(s, T, C)(key & tmask);
         my_tix = static_cast<uint32_t>(s * T + p);
         if (si == 0) {
             my_start = true;
@@ -591,216 +606,489 @@ __global__ void __launch_bounds__(SCANW_WARPS * 32) k_segscan_w(ScanArgs<typenam
     }
 }
 
-// ------------------------------------------------------------------ TMA-staged scan
-// The scan kernel for rows that are whole multiples of 16 bytes.  A CTA of 8
-// warps takes a chunk of 256 tape positions (one ticket).  Warp 0 issues one
-// TMA bulk copy (cp.async.bulk, no multicast) per row into shared memory on an
-// mbarrier; the rows then sit in shared memory, not registers, so ~7 CTAs per
-// SM keep ~200 KB of loads in flight and hide the look-back latency of their
-// neighbours.  Warp w scans positions [32w, 32w+32) with lanes over columns
-// (pass 1 stores every position from the warp's first segment start on),
-// warp 0 folds the warp sums, publishes the chunk and looks back (windowed),
-// and warps whose head continues a segment rescan it with their carry (pass 2).
-constexpr int SCANT_WARPS = 8;
-constexpr int SCANT_P = SCANT_WARPS * 32;
-constexpr uint32_t TMA_WAIT_LIMIT = 1u << 24;
+template <typename X, int EL>
+__device__ __forceinline__ void st_frag_smem(X* p, const RawWords<EL * sizeof(X)>& r) {
+    constexpr int B = EL * sizeof(X);
+    if constexpr (B == 2) *reinterpret_cast<uint16_t*>(p) = static_cast<uint16_t>(r.w[0]);
+    else if constexpr (B == 4) *reinterpret_cast<uint32_t*>(p) = r.w[0];
+    else if constexpr (B == 8) *reinterpret_cast<uint2*>(p) = make_uint2(r.w[0], r.w[1]);
+    else {
+#pragma unroll
+        for (int q = 0; q < B / 16; ++q)
+            *reinterpret_cast<uint4*>(reinterpret_cast<char*>(p) + 16 * q) =
+                make_uint4(r.w[4 * q], r.w[4 * q + 1], r.w[4 * q + 2], r.w[4 * q + 3]);
+    }
+}
 
-template <typename KeyT, int DT, int EL, bool IN_SORTED, bool OUT_SORTED>
-__global__ void __launch_bounds__(SCANT_WARPS * 32) k_segscan_t(ScanArgs<typename Elem<DT>::Acc> a) {
+// Copy staged result rows [r0, r1) of the chunk to their output rows, 16 bytes
+// per lane (rows are whole multiples of 16 bytes).
+template <typename AccT, typename X>
+__device__ __forceinline__ void store_rows(const ScanArgs<AccT>& a, const X* rows, const uint32_t* s_out, int r0,
+                                           int r1, uint32_t rb, X* out, int lane) {
+    const uint32_t vpr = rb / 16;
+    const uint32_t n = static_cast<uint32_t>(r1 > r0 ? r1 - r0 : 0) * vpr;
+    for (uint32_t e = lane; e < n; e += 32) {
+        uint32_t r, v;
+        a.fd_vpr.divmod(e, r, v);
+        const uint4 val = *reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(rows) +
+                                                          static_cast<size_t>(r0 + r) * rb + v * 16);
+        *reinterpret_cast<uint4*>(reinterpret_cast<char*>(out) + static_cast<uint64_t>(s_out[r0 + r]) * rb + v * 16) =
+            val;
+    }
+}
+
+// ------------------------------------------------------------------ lane fragments in shared memory
+// 32-bit shared-memory addressing and paired 16-bit conversions for the scan's
+// inner loop (one tape position per iteration, lanes over columns).
+template <int B>
+__device__ __forceinline__ RawWords<B> lds_words(uint32_t addr) {
+    RawWords<B> r;
+    if constexpr (B == 2) {
+        unsigned short h;
+        asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(addr));
+        r.w[0] = h;
+    } else if constexpr (B == 4) {
+        asm volatile("ld.shared.b32 %0, [%1];" : "=r"(r.w[0]) : "r"(addr));
+    } else if constexpr (B == 8) {
+        asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(r.w[0]), "=r"(r.w[1]) : "r"(addr));
+    } else {
+#pragma unroll
+        for (int q = 0; q < B / 16; ++q)
+            asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(r.w[4 * q]), "=r"(r.w[4 * q + 1]), "=r"(r.w[4 * q + 2]), "=r"(r.w[4 * q + 3])
+                         : "r"(addr + 16 * q));
+    }
+    return r;
+}
+
+template <int B>
+__device__ __forceinline__ void sts_words(uint32_t addr, const RawWords<B>& r) {
+    if constexpr (B == 2) {
+        const unsigned short h = static_cast<unsigned short>(r.w[0]);
+        asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"(h) : "memory");
+    } else if constexpr (B == 4) {
+        asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(r.w[0]) : "memory");
+    } else if constexpr (B == 8) {
+        asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(addr), "r"(r.w[0]), "r"(r.w[1]) : "memory");
+    } else {
+#pragma unroll
+        for (int q = 0; q < B / 16; ++q)
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr + 16 * q), "r"(r.w[4 * q]),
+                         "r"(r.w[4 * q + 1]), "r"(r.w[4 * q + 2]), "r"(r.w[4 * q + 3])
+                         : "memory");
+    }
+}
+
+// Unpack EL elements of X held in raw words into accumulators.
+template <typename X, typename Acc, int EL>
+__device__ __forceinline__ void unpack(const RawWords<EL * sizeof(X)>& r, Acc (&v)[EL]) {
+    if constexpr (std::is_same<X, __nv_bfloat16>::value && EL % 2 == 0) {
+#pragma unroll
+        for (int q = 0; q < EL / 2; ++q) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.w[q]));
+            v[2 * q] = f.x; v[2 * q + 1] = f.y;
+        }
+    } else if constexpr (std::is_same<X, __half>::value && EL % 2 == 0) {
+#pragma unroll
+        for (int q = 0; q < EL / 2; ++q) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&r.w[q]));
+            v[2 * q] = f.x; v[2 * q + 1] = f.y;
+        }
+    } else {
+#pragma unroll
+        for (int q = 0; q < EL; ++q) v[q] = frag_get<X, Acc, EL>(r, q);
+    }
+}
+
+// Pack EL accumulators into raw words of X (round to nearest even).
+template <typename X, typename Acc, int EL>
+__device__ __forceinline__ RawWords<EL * sizeof(X)> pack(const Acc (&v)[EL]) {
+    RawWords<EL * sizeof(X)> r;
+    if constexpr (std::is_same<X, __nv_bfloat16>::value && EL % 2 == 0) {
+#pragma unroll
+        for (int q = 0; q < EL / 2; ++q) {
+            const __nv_bfloat162 h = __float22bfloat162_rn(make_float2(v[2 * q], v[2 * q + 1]));
+            r.w[q] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+    } else if constexpr (std::is_same<X, __half>::value && EL % 2 == 0) {
+#pragma unroll
+        for (int q = 0; q < EL / 2; ++q) {
+            const __half2 h = __float22half2_rn(make_float2(v[2 * q], v[2 * q + 1]));
+            r.w[q] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+    } else {
+        X* x = reinterpret_cast<X*>(&r.w[0]);
+#pragma unroll
+        for (int q = 0; q < EL; ++q) x[q] = acc_to<X, Acc>(v[q]);
+    }
+    return r;
+}
+
+// ------------------------------------------------------------------ range scan (two kernels)
+// The scan used for rows that are whole multiples of 16 bytes.  Each stream's
+// tape (in scan order) is cut into R ranges of RL positions, and no CTA ever
+// waits on another:
+//   k_range_tail  one CTA per range: finds the range's last segment start from
+//                 the keys and sums the rows after it (its trailing segment),
+//                 i.e. the carry it hands to later ranges; has_start says
+//                 whether the range contains a segment start at all;
+//   k_range_scan  one CTA per range: folds the tails of the earlier ranges of
+//                 its stream into its carry-in, then streams its chunks of 256
+//                 positions: warp w owns 32 rows per chunk, stages them with
+//                 cp.async into a double-buffered tile (keys prefetched two
+//                 chunks ahead), scans them with lanes over columns, writes the
+//                 results in place and stores whole rows 16 bytes per lane.
+// The tails cost one extra read of the rows after each range's last segment
+// start (a few percent of the tape for Zipf addresses).
+constexpr int RS_WARPS = 8;
+constexpr int RS_CHUNK = RS_WARPS * 32;
+
+struct RangeArgs {
+    int64_t S;             // streams
+    const void* keys;      // [S][T]
+    const int* nvalid;     // [S] or null
+    int64_t T, C;
+    uint32_t D;
+    int tbits;
+    int reverse, inclusive;
+    int64_t R, RL;         // ranges per stream, positions per range (multiple of RS_CHUNK)
+    const void* in;        // dtype [N, D] gathered by flat row, or Acc [S*T, D] by tape index
+    void* out;             // dtype [N, D] scattered by flat row, or Acc [S*T, D] by tape index
+    uint8_t* out_mask;     // optional [N]
+    void* tail;            // Acc [S*R, D]
+    uint32_t* tail_hs;     // [S*R]
+    int64_t* bounds;       // [S*(R+1)] range boundaries in scan order
+    FastDiv fd_vpr;        // 16-byte vectors per input row
+};
+
+template <typename KeyT>
+__device__ __forceinline__ bool range_is_start(const KeyT* keys, int64_t si, int64_t n_s, int reverse, int tbits) {
+    if (si == 0) return true;
+    const int64_t p = reverse ? (n_s - 1 - si) : si;
+    const int64_t pp = reverse ? (n_s - si) : (si - 1);
+    return (keys[p] >> tbits) != (keys[pp] >> tbits);
+}
+
+template <typename KeyT>
+__device__ __forceinline__ uint32_t range_row(const KeyT* keys, const RowMap& rows_of, int64_t s, int64_t si,
+                                              int64_t n_s, int reverse, int tbits, int64_t T, bool sorted) {
+    const int64_t p = reverse ? (n_s - 1 - si) : si;
+    if (sorted) return static_cast<uint32_t>(s * T + p);
+    const KeyT tmask = (static_cast<KeyT>(1) << tbits) - 1;
+    return rows_of(keys[p] & tmask);
+}
+
+// First segment start in [x, end) of the scan order, or -1 (block-wide).
+template <typename KeyT>
+__device__ int64_t first_start_from(const KeyT* keys, int64_t x, int64_t end, int64_t n_s, int reverse, int tbits,
+                                    int* s_tmp) {
+    for (int64_t b0 = x; b0 < end; b0 += RS_CHUNK) {
+        if (threadIdx.x == 0) *s_tmp = RS_CHUNK;
+        __syncthreads();
+        const int64_t si = b0 + threadIdx.x;
+        if (si < end && range_is_start(keys, si, n_s, reverse, tbits)) atomicMin(s_tmp, static_cast<int>(threadIdx.x));
+        __syncthreads();
+        const int f = *s_tmp;
+        __syncthreads();
+        if (f < RS_CHUNK) return b0 + f;
+    }
+    return -1;
+}
+
+// Last segment start in [x, end) of the scan order, or -1 (block-wide).
+template <typename KeyT>
+__device__ int64_t last_start_before(const KeyT* keys, int64_t x, int64_t end, int64_t n_s, int reverse, int tbits,
+                                     int* s_tmp) {
+    for (int64_t e0 = end; e0 > x; e0 -= RS_CHUNK) {
+        if (threadIdx.x == 0) *s_tmp = -1;
+        __syncthreads();
+        const int64_t si = e0 - 1 - threadIdx.x;
+        if (si >= x && range_is_start(keys, si, n_s, reverse, tbits)) atomicMax(s_tmp, static_cast<int>(si - x));
+        __syncthreads();
+        const int f = *s_tmp;
+        __syncthreads();
+        if (f >= 0) return x + f;
+    }
+    return -1;
+}
+
+// Range boundaries: the nominal boundary r*RL moves forward to the next segment
+// start within one range length, so that the range needs no carry.  Only when
+// a segment is longer than a range does a boundary stay unsnapped; then the
+// range before it publishes its tail (sum of its rows after its last segment
+// start, or of all its rows when it has none) for the next range to fold.
+template <typename KeyT, int DT, int EL, bool IN_SORTED>
+__global__ void __launch_bounds__(RS_WARPS * 32) k_range_tail(RangeArgs a) {
+    using Acc = typename Elem<DT>::Acc;
+    using InT = typename std::conditional<IN_SORTED, Acc, typename Elem<DT>::T>::type;
+    __shared__ int s_tmp;
+    __shared__ uint32_t s_rows[RS_CHUNK];
+    __shared__ Acc s_red[RS_WARPS][32 * EL];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t s = blockIdx.x / a.R, r = blockIdx.x % a.R;
+    const int64_t n_s = a.nvalid ? a.nvalid[s] : a.T;
+    const KeyT* keys = static_cast<const KeyT*>(a.keys) + s * a.T;
+    const uint32_t D = a.D;
+    Acc* tail = static_cast<Acc*>(a.tail) + (s * a.R + r) * D;
+    auto snap = [&](int64_t x) -> int64_t {  // boundary at nominal position x
+        if (x >= n_s) return n_s;
+        if (x == 0) return 0;
+        const int64_t f = first_start_from(keys, x, x + a.RL < n_s ? x + a.RL : n_s, n_s, a.reverse, a.tbits, &s_tmp);
+        return f >= 0 ? f : x;
+    };
+    const int64_t lo = snap(r * a.RL);
+    const int64_t hi = snap((r + 1) * a.RL);
+    if (tid == 0) {
+        a.bounds[s * (a.R + 1) + r] = lo;
+        if (r == a.R - 1) a.bounds[s * (a.R + 1) + a.R] = n_s;
+    }
+    const bool hi_unsnapped = hi < n_s && !range_is_start(keys, hi, n_s, a.reverse, a.tbits);
+    if (!hi_unsnapped || lo >= hi) {
+        if (tid == 0) a.tail_hs[s * a.R + r] = 1u;  // never folded past
+        return;
+    }
+    const int64_t ls = last_start_before(keys, lo, hi, n_s, a.reverse, a.tbits, &s_tmp);
+    const RowMap rows_of(s, a.T, a.C);
+    const int64_t t0 = ls >= 0 ? ls : lo;
+    const bool active = static_cast<uint32_t>(lane * EL) < D;
+    const uint32_t col = static_cast<uint32_t>(lane * EL);
+    const InT* in = static_cast<const InT*>(a.in);
+    Acc acc[EL];
+#pragma unroll
+    for (int q = 0; q < EL; ++q) acc[q] = Acc(0);
+    for (int64_t b0 = t0; b0 < hi; b0 += RS_CHUNK) {  // 256 rows at a time, all loads in flight
+        const int64_t si = b0 + tid;
+        if (si < hi) s_rows[tid] = range_row(keys, rows_of, s, si, n_s, a.reverse, a.tbits, a.T, IN_SORTED);
+        __syncthreads();
+        const int nb = static_cast<int>(hi - b0 < RS_CHUNK ? hi - b0 : RS_CHUNK);
+#pragma unroll 8
+        for (int i = warp; i < nb; i += RS_WARPS) {
+            if (active) {
+                const RawWords<EL * sizeof(InT)> x = ld_frag<InT, EL>(in + static_cast<uint64_t>(s_rows[i]) * D + col);
+#pragma unroll
+                for (int q = 0; q < EL; ++q) acc[q] += frag_get<InT, Acc, EL>(x, q);
+            }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int q = 0; q < EL; ++q) s_red[warp][lane * EL + q] = acc[q];
+    __syncthreads();
+    if (warp == 0 && active) {
+#pragma unroll
+        for (int q = 0; q < EL; ++q) {
+            Acc v = Acc(0);
+            for (int w = 0; w < RS_WARPS; ++w) v += s_red[w][lane * EL + q];
+            tail[col + q] = v;
+        }
+    }
+    if (tid == 0) a.tail_hs[s * a.R + r] = ls >= 0 ? 1u : 0u;
+}
+
+template <typename KeyT, int DT, int EL, bool IN_SORTED, bool OUT_SORTED, bool INCL>
+__global__ void __launch_bounds__(RS_WARPS * 32) k_range_scan(RangeArgs a) {
     using E = Elem<DT>;
     using Acc = typename E::Acc;
     using V = typename E::T;
     using InT = typename std::conditional<IN_SORTED, Acc, V>::type;
     using OutT = typename std::conditional<OUT_SORTED, Acc, V>::type;
-    constexpr int NW = SCANT_WARPS;
-    constexpr int P = SCANT_P;
+    constexpr bool INPLACE = std::is_same<InT, OutT>::value;
     extern __shared__ __align__(16) unsigned char smem[];
-    const uint32_t D = static_cast<uint32_t>(a.D);
-    const uint32_t rb = D * static_cast<uint32_t>(sizeof(InT));  // input row bytes (multiple of 16)
-    InT* rows = reinterpret_cast<InT*>(smem);                     // [P][D]
-    Acc* wagg = reinterpret_cast<Acc*>(smem + static_cast<size_t>(P) * rb);  // [NW][D]
-    Acc* carry = wagg + NW * D;                                   // [D]
-    __shared__ __align__(8) uint64_t s_bar;
-    __shared__ unsigned s_ticket;
-    __shared__ unsigned s_startmask[NW];
-    __shared__ uint32_t s_in[P];
-    __shared__ uint32_t s_out[P];
-
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    if (tid == 0) {
-        s_ticket = atomicAdd(a.ticket, 1u);
-        mbar_init(&s_bar, 1);
-    }
-    __syncthreads();
-    const int64_t L = s_ticket;
-    const int64_t s = L / a.nchunks;
-    const int64_t ch = L % a.nchunks;
-    const int64_t T = a.T, C = a.C;
-    const int64_t n_s = a.nvalid ? a.nvalid[s] : T;
-    const int64_t i0 = ch * P;
-    if (i0 >= n_s) return;  // beyond this stream's tape; no later chunk waits on it
-    const int np = static_cast<int>(n_s - i0 < P ? n_s - i0 : P);
-    const KeyT* keys = static_cast<const KeyT*>(a.keys) + s * T;
-    const KeyT tmask = (static_cast<KeyT>(1) << a.tbits) - 1;
-
-    // keys -> row indices and segment starts (position i = tid)
-    bool my_start = false;
-    uint32_t my_flat = 0;
-    if (tid < np) {
-        const int64_t si = i0 + tid;
-        const int64_t p = a.reverse ? (n_s - 1 - si) : si;
-        const KeyT key = keys[p];
-        my_flat = static_cast<uint32_t>(flat_row(s, static_cast<int64_t>(key & tmask), T, C));
-        const uint32_t tix = static_cast<uint32_t>(s * T + p);
-        s_in[tid] = IN_SORTED ? tix : my_flat;
-        s_out[tid] = OUT_SORTED ? tix : my_flat;
-        if (si == 0) {
-            my_start = true;
-        } else {
-            const int64_t pp = a.reverse ? (n_s - si) : (si - 1);
-            my_start = (keys[pp] >> a.tbits) != (key >> a.tbits);
-        }
-    }
-    const unsigned startmask = __ballot_sync(0xffffffffu, my_start);
-    if (a.out_mask != nullptr && tid < np) a.out_mask[my_flat] = my_start ? 0 : 1;
-    __syncthreads();
-
-    // TMA: one bulk copy per row, all on one mbarrier
-    const InT* in = static_cast<const InT*>(a.in);
-    if (warp == 0) {
-        if (lane == 0) mbar_arrive_expect_tx(&s_bar, static_cast<uint32_t>(np) * rb);
-        __syncwarp();
-        for (int r = lane; r < np; r += 32)
-            tma_load_1d(rows + static_cast<size_t>(r) * D, in + static_cast<uint64_t>(s_in[r]) * D, rb, &s_bar);
-    }
-    bool loaded = mbar_wait_bounded(&s_bar, 0, TMA_WAIT_LIMIT);
-    if (!loaded) mbar_wait_bounded(&s_bar, 0, TMA_WAIT_LIMIT);  // let copies in flight land before exit
-
-    const int w0 = warp * 32;
-    const int nv = np - w0 < 0 ? 0 : (np - w0 < 32 ? np - w0 : 32);
-    const int first = startmask ? __ffs(startmask) - 1 : 32;
+    const uint32_t D = a.D;
+    const uint32_t rb = D * static_cast<uint32_t>(sizeof(InT));
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // each warp owns one range and a double-buffered tile of 2 x 32 rows
+    unsigned char* wbuf = smem + static_cast<size_t>(warp) * 2 * 32 * rb;
+    const int64_t gw = static_cast<int64_t>(blockIdx.x) * RS_WARPS + warp;
+    const int64_t S = a.S;
+    if (gw >= S * a.R) return;
+    const int64_t s = gw / a.R, r = gw % a.R;
+    const int64_t n_s = a.nvalid ? a.nvalid[s] : a.T;
+    const int64_t lo = a.bounds[s * (a.R + 1) + r];
+    const int64_t hi = a.bounds[s * (a.R + 1) + r + 1];
+    if (lo >= hi) return;
+    const KeyT* keys = static_cast<const KeyT*>(a.keys) + s * a.T;
     const bool active = static_cast<uint32_t>(lane * EL) < D;
     const uint32_t col = static_cast<uint32_t>(lane * EL);
+    const InT* in = static_cast<const InT*>(a.in);
     OutT* out = static_cast<OutT*>(a.out);
+    const int nch = static_cast<int>((hi - lo + 31) / 32);
+    const KeyT tmask = (static_cast<KeyT>(1) << a.tbits) - 1;
+    const RowMap rows_of(s, a.T, a.C);
 
-    // pass 1
+    // carry-in: zero when the range starts a segment (snapped boundary), else
+    // the tails of the earlier ranges back to the one holding the segment start
     Acc run[EL];
 #pragma unroll
     for (int q = 0; q < EL; ++q) run[q] = Acc(0);
-    if (loaded) {
-        for (int i = 0; i < nv; ++i) {
-            const bool st = (startmask >> i) & 1u;
-            const RawWords<EL * sizeof(InT)> x = ld_frag_smem<InT, EL>(rows + static_cast<size_t>(w0 + i) * D + col);
-            RawWords<EL * sizeof(OutT)> o;
-            OutT* ov = reinterpret_cast<OutT*>(&o.w[0]);
+    if (!range_is_start(keys, lo, n_s, a.reverse, a.tbits) && active) {
+        const Acc* tails = static_cast<const Acc*>(a.tail) + s * a.R * D;
+        for (int64_t rr = r - 1; rr >= 0; --rr) {
 #pragma unroll
-            for (int q = 0; q < EL; ++q) {
-                if (st) run[q] = Acc(0);
-                const Acc v = active ? frag_get<InT, Acc, EL>(x, q) : Acc(0);
-                if (a.inclusive) { run[q] += v; ov[q] = acc_to<OutT, Acc>(run[q]); }
-                else { ov[q] = acc_to<OutT, Acc>(run[q]); run[q] += v; }
-            }
-            if (i >= first && active) st_frag<OutT, EL>(out + static_cast<uint64_t>(s_out[w0 + i]) * D + col, o);
+            for (int q = 0; q < EL; ++q) run[q] += tails[rr * D + col + q];
+            if (a.tail_hs[s * a.R + rr] != 0u) break;
         }
     }
-    if (active) {
-#pragma unroll
-        for (int q = 0; q < EL; ++q) wagg[warp * D + col + q] = run[q];
-    }
-    if (lane == 0) s_startmask[warp] = nv > 0 ? startmask : 0u;
-    __syncthreads();
 
-    int m = NW;
-#pragma unroll
-    for (int w = NW - 1; w >= 0; --w) if (s_startmask[w] != 0u) m = w;
-    const bool head_continues = (s_startmask[0] & 1u) == 0u;
-    const int waiters = (m < NW ? m : NW - 1) + 1;
-
-    if (warp == 0) {
-        Acc cagg[EL];
-#pragma unroll
-        for (int q = 0; q < EL; ++q) cagg[q] = Acc(0);
-        for (int w = 0; w < NW; ++w) {
-            const bool hs = s_startmask[w] != 0u;
-            if (active) {
-#pragma unroll
-                for (int q = 0; q < EL; ++q) {
-                    const Acc v = wagg[w * D + col + q];
-                    cagg[q] = hs ? v : cagg[q] + v;
-                }
+    struct KeyPair { KeyT k, kp; };
+    auto load_keys = [&](int c) -> KeyPair {
+        KeyPair kk{KeyT(0), KeyT(0)};
+        const int64_t si = lo + static_cast<int64_t>(c) * 32 + lane;
+        if (c < nch && si < hi) {
+            kk.k = keys[a.reverse ? (n_s - 1 - si) : si];
+            if (si > 0) kk.kp = keys[a.reverse ? (n_s - si) : (si - 1)];
+        }
+        return kk;
+    };
+    // row indices (input, output) and segment start of this lane's position in chunk c
+    auto derive = [&](int c, const KeyPair& kk, uint32_t& my_in, uint32_t& my_out, bool& st) {
+        const int64_t si = lo + static_cast<int64_t>(c) * 32 + lane;
+        my_in = 0; my_out = 0; st = false;
+        if (c < nch && si < hi) {
+            const int64_t p = a.reverse ? (n_s - 1 - si) : si;
+            const uint32_t tix = static_cast<uint32_t>(s * a.T + p);
+            const uint32_t flat = rows_of(kk.k & tmask);
+            my_in = IN_SORTED ? tix : flat;
+            my_out = OUT_SORTED ? tix : flat;
+            st = si == 0 || (kk.k >> a.tbits) != (kk.kp >> a.tbits);
+        }
+    };
+    const uint32_t vpr = rb / 16;
+    // lane -> (row offset, 16-byte vector) once, when a row's vectors divide 32
+    const bool lane_split = vpr <= 32 && (32 % vpr) == 0;
+    uint32_t l_rr = 0, l_v = 0;
+    a.fd_vpr.divmod(static_cast<uint32_t>(lane), l_rr, l_v);
+    const uint32_t rows_per_pass = lane_split ? 32 / vpr : 0;
+    auto stage = [&](int c, uint32_t my_in) {
+        unsigned char* tile = wbuf + static_cast<size_t>(c & 1) * 32 * rb;
+        const int64_t base = lo + static_cast<int64_t>(c) * 32;
+        const int nvw = static_cast<int>(hi - base < 32 ? hi - base : 32);
+        if (lane_split) {
+            for (uint32_t rr = l_rr; rr < 32; rr += rows_per_pass) {  // uniform trip count
+                const uint32_t row = __shfl_sync(0xffffffffu, my_in, static_cast<int>(rr));
+                if (static_cast<int>(rr) < nvw)
+                    cp_async16(tile + rr * rb + l_v * 16,
+                               reinterpret_cast<const char*>(in + static_cast<uint64_t>(row) * D) + l_v * 16);
+            }
+        } else {
+            const uint32_t total = static_cast<uint32_t>(nvw) * vpr;
+            for (uint32_t e0 = 0; e0 < total; e0 += 32) {  // uniform trip count: full-warp shuffles
+                const uint32_t e = e0 + lane;
+                uint32_t rr, v;
+                a.fd_vpr.divmod(e, rr, v);
+                const uint32_t row = __shfl_sync(0xffffffffu, my_in, static_cast<int>(rr & 31u));
+                if (e < total)
+                    cp_async16(tile + rr * rb + v * 16,
+                               reinterpret_cast<const char*>(in + static_cast<uint64_t>(row) * D) + v * 16);
             }
         }
-        const bool chunk_hs = m < NW;
-        Acc* dst = chunk_hs ? a.incl : a.agg;
-        if (active) {
-#pragma unroll
-            for (int q = 0; q < EL; ++q) dst[L * D + col + q] = cagg[q];
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+
+    uint32_t in_cur, out_cur;
+    bool st_cur;
+    derive(0, load_keys(0), in_cur, out_cur, st_cur);
+    stage(0, in_cur);
+    KeyPair k_next = load_keys(1);
+
+    for (int c = 0; c < nch; ++c) {
+        uint32_t in_nx = 0, out_nx = 0;
+        bool st_nx = false;
+        if (c + 1 < nch) {
+            derive(c + 1, k_next, in_nx, out_nx, st_nx);
+            stage(c + 1, in_nx);
+            k_next = load_keys(c + 2);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
         }
-        __threadfence();
         __syncwarp();
-        if (lane == 0) st_release(a.flags + L, chunk_hs ? 2u : 1u);
-        if (head_continues) {
-            Acc cin[EL];
+        const unsigned sm = __ballot_sync(0xffffffffu, st_cur);
+        const int64_t base = lo + static_cast<int64_t>(c) * 32;
+        const int nv = static_cast<int>(hi - base < 32 ? hi - base : 32);
+        if (a.out_mask != nullptr && lane < nv) a.out_mask[out_cur] = st_cur ? 0 : 1;
+        unsigned char* tile = wbuf + static_cast<size_t>(c & 1) * 32 * rb;
+        const uint32_t tile_s = smem_u32(tile) + col * static_cast<uint32_t>(sizeof(InT));
+        // one pass with the running carry
+        if (INPLACE && nv == 32) {
 #pragma unroll
-            for (int q = 0; q < EL; ++q) cin[q] = Acc(0);
-            windowed_lookback<Acc, EL>(a.flags, a.agg, a.incl, L - 1, L - ch, D, lane, active, col, cin);
-            if (!chunk_hs) {
-                if (active) {
-#pragma unroll
-                    for (int q = 0; q < EL; ++q) a.incl[L * D + col + q] = cin[q] + cagg[q];
-                }
-                __threadfence();
-                __syncwarp();
-                if (lane == 0) st_release(a.flags + L, 2u);
-            }
-            if (active) {
-#pragma unroll
-                for (int q = 0; q < EL; ++q) carry[col + q] = cin[q];
-            }
-        }
-    }
-    if (head_continues && warp < waiters && waiters > 1) named_barrier(waiters * 32);
-
-    // pass 2: head positions [0, first) of the warp with their carry-in
-    if (first > 0 && nv > 0 && loaded) {
-        Acc cin[EL];
-#pragma unroll
-        for (int q = 0; q < EL; ++q) cin[q] = Acc(0);
-        bool any_start = false;
-        for (int w = 0; w < warp; ++w) {
-            const bool hs = s_startmask[w] != 0u;
-            any_start |= hs;
-            if (active) {
+            for (int i = 0; i < 32; ++i) {
+                const uint32_t addr = tile_s + static_cast<uint32_t>(i) * rb;
+                // lanes past the row's columns (lane*EL >= D) must not touch shared
+                // memory: their addresses run past the row and, on the last row of
+                // the last tile, past the allocation
+                RawWords<EL * sizeof(InT)> x{};
+                if (active) x = lds_words<EL * sizeof(InT)>(addr);
+                Acc v[EL];
+                unpack<InT, Acc, EL>(x, v);
+                const bool stt = (sm >> i) & 1u;
+                Acc o[EL];
 #pragma unroll
                 for (int q = 0; q < EL; ++q) {
-                    const Acc v = wagg[w * D + col + q];
-                    cin[q] = hs ? v : cin[q] + v;
+                    run[q] = stt ? Acc(0) : run[q];
+                    if (INCL) { run[q] += v[q]; o[q] = run[q]; }
+                    else { o[q] = run[q]; run[q] += v[q]; }
+                }
+                if (active) sts_words<EL * sizeof(OutT)>(addr, pack<OutT, Acc, EL>(o));
+            }
+        } else {
+            for (int i = 0; i < nv; ++i) {
+                const uint32_t addr = tile_s + static_cast<uint32_t>(i) * rb;
+                RawWords<EL * sizeof(InT)> x{};
+                if (active) x = lds_words<EL * sizeof(InT)>(addr);  // see the guard above
+                Acc v[EL];
+                unpack<InT, Acc, EL>(x, v);
+                const uint32_t orow = INPLACE ? 0u : __shfl_sync(0xffffffffu, out_cur, i);
+                const bool stt = (sm >> i) & 1u;
+                Acc o[EL];
+#pragma unroll
+                for (int q = 0; q < EL; ++q) {
+                    run[q] = stt ? Acc(0) : run[q];
+                    if (INCL) { run[q] += v[q]; o[q] = run[q]; }
+                    else { o[q] = run[q]; run[q] += v[q]; }
+                }
+                if (active) {
+                    if constexpr (INPLACE) sts_words<EL * sizeof(OutT)>(addr, pack<OutT, Acc, EL>(o));
+                    else st_frag<OutT, EL>(out + static_cast<uint64_t>(orow) * D + col, pack<OutT, Acc, EL>(o));
                 }
             }
         }
-        if (!any_start && head_continues && active) {
-#pragma unroll
-            for (int q = 0; q < EL; ++q) cin[q] += carry[col + q];
-        }
-        const int hn = first < nv ? first : nv;
-        for (int i = 0; i < hn; ++i) {
-            const RawWords<EL * sizeof(InT)> x = ld_frag_smem<InT, EL>(rows + static_cast<size_t>(w0 + i) * D + col);
-            RawWords<EL * sizeof(OutT)> o;
-            OutT* ov = reinterpret_cast<OutT*>(&o.w[0]);
-#pragma unroll
-            for (int q = 0; q < EL; ++q) {
-                const Acc v = active ? frag_get<InT, Acc, EL>(x, q) : Acc(0);
-                if (a.inclusive) { cin[q] += v; ov[q] = acc_to<OutT, Acc>(cin[q]); }
-                else { ov[q] = acc_to<OutT, Acc>(cin[q]); cin[q] += v; }
+        if constexpr (INPLACE) {
+            __syncwarp();
+            if (lane_split) {
+                for (uint32_t rr = l_rr; rr < 32; rr += rows_per_pass) {
+                    const uint32_t orow = __shfl_sync(0xffffffffu, out_cur, static_cast<int>(rr));
+                    if (static_cast<int>(rr) < nv) {
+                        const uint4 val = *reinterpret_cast<const uint4*>(tile + rr * rb + l_v * 16);
+                        *reinterpret_cast<uint4*>(reinterpret_cast<char*>(out) + static_cast<uint64_t>(orow) * rb +
+                                                  l_v * 16) = val;
+                    }
+                }
+            } else {
+                const uint32_t total = static_cast<uint32_t>(nv) * vpr;
+                for (uint32_t e0 = 0; e0 < total; e0 += 32) {
+                    const uint32_t e = e0 + lane;
+                    uint32_t rr, v;
+                    a.fd_vpr.divmod(e, rr, v);
+                    const uint32_t orow = __shfl_sync(0xffffffffu, out_cur, static_cast<int>(rr & 31u));
+                    if (e < total) {
+                        const uint4 val = *reinterpret_cast<const uint4*>(tile + rr * rb + v * 16);
+                        *reinterpret_cast<uint4*>(reinterpret_cast<char*>(out) + static_cast<uint64_t>(orow) * rb +
+                                                  v * 16) = val;
+                    }
+                }
             }
-            if (active) st_frag<OutT, EL>(out + static_cast<uint64_t>(s_out[w0 + i]) * D + col, o);
         }
+        __syncwarp();
+        in_cur = in_nx;
+        out_cur = out_nx;
+        st_cur = st_nx;
     }
 }
 
 template <typename Acc>
-inline size_t segscan_t_smem(int64_t D, size_t in_elem) {
-    return static_cast<size_t>(SCANT_P) * D * in_elem + static_cast<size_t>(SCANT_WARPS + 1) * D * sizeof(Acc);
+inline size_t range_scan_smem(int64_t D, size_t in_elem) {
+    return static_cast<size_t>(RS_WARPS) * 2 * 32 * D * in_elem;
 }
 
 // Rows a warp holds in registers: at most 64 bytes of input per lane (16 rows
@@ -834,13 +1122,16 @@ struct SsGenArgs {
     const void* grad;      // backward: grad_sums [N, D]
     void* out;             // forward: sums [N, D]
     uint8_t* out_mask;     // forward: [N]
+    FastDiv fd_C, fd_T;    // flat row -> (b, t, c)
 };
 
 template <typename KeyT>
 __device__ __forceinline__ bool ss_valid(const SsGenArgs& a, int64_t r, int64_t& tape_index) {
     const int64_t T = a.T, C = a.C;
-    const int64_t c = r % C, b = r / (C * T);
-    const int64_t s = b * C + c;
+    uint32_t bt, c32, b32, t32;
+    a.fd_C.divmod(static_cast<uint32_t>(r), bt, c32);
+    a.fd_T.divmod(bt, b32, t32);
+    const int64_t s = static_cast<int64_t>(b32) * C + c32;
     const int32_t idx = a.ridx[r];
     if (idx < 0) return false;
     const KeyT key = static_cast<const KeyT*>(a.keys)[s * T + idx];

@@ -402,6 +402,7 @@ struct SearchArgs {
     int64_t B, T, C, A;
     int tbits;
     int32_t* ridx;         // [N] local index of the latest earlier write (may be any address), -1 if none
+    FastDiv fd_C, fd_T;    // flat row -> (b, t, c)
 };
 
 // ravel_memory.py:153-159 restricted to the read's stream: the number of the
@@ -411,10 +412,11 @@ __global__ void __launch_bounds__(256) k_read_search(SearchArgs a) {
     const int64_t N = a.B * a.T * a.C;
     for (int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; r < N;
          r += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t c = r % a.C;
-        const int64_t t = (r / a.C) % a.T;
-        const int64_t b = r / (a.C * a.T);
-        const int64_t s = b * a.C + c;
+        uint32_t bt, c32, b32, t32;
+        a.fd_C.divmod(static_cast<uint32_t>(r), bt, c32);
+        a.fd_T.divmod(bt, b32, t32);
+        const int64_t t = t32;
+        const int64_t s = static_cast<int64_t>(b32) * a.C + c32;
         const uint64_t ra = fold_addr(load_addr(a.raddr, r, a.addr_i64), a.A, a.key32);
         const KeyT q = (static_cast<KeyT>(ra) << a.tbits) | static_cast<KeyT>(t);
         const KeyT* k = static_cast<const KeyT*>(a.keys) + s * a.T;
