@@ -1,0 +1,97 @@
+"""Stream sharding across ranks: partition logic and a world-size-2 gloo run.
+
+The per-rank compute in the multi-process test is the CPU oracle (this file
+checks the host-side partition, collective and reassembly, not the kernels).
+"""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from ravel_lm_b200.sharding import all_shards, assemble, shard_streams
+
+
+@pytest.mark.parametrize("B,C,world", [(4, 16, 1), (4, 16, 2), (4, 16, 4), (8, 3, 8), (4, 16, 8), (1, 8, 2),
+                                       (2, 6, 6)])
+def test_partition_covers_every_stream_once(B, C, world):
+    shards = all_shards(B, C, world)
+    seen = np.zeros((B, C), int)
+    for sh in shards:
+        seen[sh.b0:sh.b1, sh.c0:sh.c1] += 1
+    assert (seen == 1).all()
+    assert len({sh.streams for sh in shards}) == 1  # equal shards for the collective
+
+
+@pytest.mark.parametrize("B,C,world", [(3, 4, 2), (1, 3, 2), (2, 4, 3)])
+def test_partition_rejects_unequal_shapes(B, C, world):
+    with pytest.raises(ValueError):
+        all_shards(B, C, world)
+
+
+def test_assemble_round_trip():
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(2, 5, 8, 3, generator=g)
+    shards = all_shards(2, 8, 4)
+    pieces = [sh.take(x) for sh in shards]
+    assert torch.equal(assemble(pieces, shards), x)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, B, T, C, D, A, k, out_q):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        import oracle
+        from ravel_lm_b200.sharding import gather_outputs
+        g = torch.Generator().manual_seed(77)
+        w = torch.randint(0, A, (B, T, C), generator=g)
+        r = torch.randint(0, A, (B, T, C), generator=g)
+        p = torch.randn(B, T, C, D, generator=g)
+        sh = shard_streams(B, C, world, rank)
+        vals, mask, _src, tape = oracle.latestk_fwd(sh.take(w).numpy(), sh.take(p).numpy(), sh.take(r).numpy(),
+                                                    address_space=A, k=k)
+        sums, smask, _ = oracle.segsum_fwd(sh.take(w).numpy(), sh.take(p).double().numpy(), sh.take(r).numpy(),
+                                           address_space=A, tape=tape)
+        full_vals = gather_outputs(torch.from_numpy(vals), sh)
+        full_mask = gather_outputs(torch.from_numpy(mask), sh)
+        full_sums = gather_outputs(torch.from_numpy(sums), sh)
+        if rank == 0:
+            ev, em, _, et = oracle.latestk_fwd(w.numpy(), p.numpy(), r.numpy(), address_space=A, k=k)
+            es, esm, _ = oracle.segsum_fwd(w.numpy(), p.double().numpy(), r.numpy(), address_space=A, tape=et)
+            ok = (np.array_equal(full_vals.numpy(), ev) and np.array_equal(full_mask.numpy(), em)
+                  and np.allclose(full_sums.numpy(), es, rtol=0, atol=1e-12))
+            out_q.put(bool(ok))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("B,C", [(4, 3), (1, 4)])
+def test_gloo_world2_sharded_equals_unsharded(B, C):
+    """Batch-row split (B >= world) and head split (B < world) over 2 gloo ranks."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(g, 2, port, B, 60, C, 4, 9, 2, q)) for g in range(2)]
+    for pr in procs:
+        pr.start()
+    for pr in procs:
+        pr.join(timeout=120)
+    for pr in procs:
+        if pr.is_alive():
+            pr.kill()
+    assert all(pr.exitcode == 0 for pr in procs)
+    assert q.get(timeout=5) is True
