@@ -394,7 +394,7 @@ def main():
                 "unit": "GB/s", "frac": kernels[dom]["frac"], "traffic": traffic,
                 "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)" if peaks["source"] == "measured"
                 else "fallback 6.65 TB/s"}
-    step_bytes = sum(v for kname, v in kb.items() if kname != "ravel_tape_build") + 2 * kb["ravel_tape_build"]
+    step_bytes = sum(kb.values())  # one tape per step: the sum reuses the latest-k tape
     tokens = cfg.tokens * world
     value = tokens / (ms * 1e-3)
 

@@ -132,7 +132,7 @@ RangePlan range_plan(int64_t S, int64_t T, int64_t slots) {
     int64_t R = S > 0 ? slots / S : 1;
     if (R < 1) R = 1;
     int64_t RL = (T + R - 1) / R;
-    RL = (RL + 31) / 32 * 32;
+    RL = (RL + 7) / 8 * 8;
     if (RL < 64) RL = 64;
     p.RL = RL;
     p.R = T > 0 ? (T + RL - 1) / RL : 1;
@@ -153,7 +153,8 @@ int sm_count() {
 }
 
 struct ScratchLayout {
-    size_t off_sort, off_flags, off_ticket, off_agg, off_incl, off_tail, off_tail_hs, off_bounds, off_big, total;
+    size_t off_sort, off_flags, off_ticket, off_agg, off_incl, off_tail, off_tail_hs, off_bounds, off_rot, off_big,
+        total;
 };
 
 ScratchLayout scratch_layout(int64_t B, int64_t T, int64_t C, int64_t D, int64_t A, int dtype, int flags) {
@@ -173,7 +174,8 @@ ScratchLayout scratch_layout(int64_t B, int64_t T, int64_t C, int64_t D, int64_t
     l.off_tail = l.off_incl + align_up(nch * static_cast<size_t>(D) * ab);
     l.off_tail_hs = l.off_tail + align_up(nr * static_cast<size_t>(D) * ab);
     l.off_bounds = l.off_tail_hs + align_up(nr * 4);
-    l.off_big = l.off_bounds + align_up((nr + S) * 8);
+    l.off_rot = l.off_bounds + align_up((nr + S) * 4);
+    l.off_big = l.off_rot + align_up(nr * 4);
     l.total = l.off_big + (t.general ? align_up(N * static_cast<size_t>(D) * ab) : 0);
     return l;
 }
@@ -532,69 +534,76 @@ int launch_segscan(const TapeView& tv, const TapeLayout& tl, int64_t B, int64_t 
     a.agg = reinterpret_cast<Acc*>(sc + sl.off_agg);
     a.incl = reinterpret_cast<Acc*>(sc + sl.off_incl);
     a.fd_d = FastDiv(static_cast<uint32_t>(D > 0 ? D : 1));
+    using V = typename Elem<DT>::T;
+    const size_t in_es = in_sorted ? sizeof(Acc) : sizeof(V);
+    const size_t out_es = out_sorted ? sizeof(Acc) : sizeof(V);
+    // group scan: rows of 16-byte vectors, 1..32 lanes per row (2 vectors per lane up to 1 KB rows)
+    const int64_t nvec = (D * static_cast<int64_t>(in_es)) % 16 == 0 ? D * static_cast<int64_t>(in_es) / 16 : 0;
+    int vpl = 0, lshift = 0;
+    if (nvec > 0 && (nvec & (nvec - 1)) == 0 && nvec <= 64) {
+        vpl = nvec == 64 ? 2 : 1;
+        const int64_t L = nvec / vpl;
+        while ((int64_t{1} << lshift) < L) ++lshift;
+    }
+    const size_t ovec = (16 / in_es) * out_es;  // output bytes per 16-byte input vector
+    if (vpl && addr_bits(in) % 16 == 0 && addr_bits(out) % ovec == 0) {
+        GsArgs ga;
+        ga.S = B * C;
+        ga.keys = tv.keys;
+        ga.nvalid = tv.nvalid;
+        ga.T = T; ga.C = C;
+        ga.D = static_cast<uint32_t>(D);
+        ga.tbits = tl.kl.tbits;
+        ga.reverse = reverse;
+        ga.lshift = lshift;
+        ga.snap = GS_SNAP;
+        ga.in = in; ga.out = out; ga.out_mask = out_mask;
+        ga.piece = sc + sl.off_tail;
+        ga.rflags = reinterpret_cast<uint32_t*>(sc + sl.off_tail_hs);
+        ga.bounds = reinterpret_cast<int32_t*>(sc + sl.off_bounds);
+        ga.rot = reinterpret_cast<int32_t*>(sc + sl.off_rot);
+        auto go = [&](auto vplc, auto inc, auto outc) -> int {
+            constexpr int VPL = decltype(vplc)::value;
+            constexpr bool IS = decltype(inc)::value != 0;
+            constexpr bool OS = decltype(outc)::value != 0;
+            auto kern = inclusive ? k_group_scan<KeyT, DT, IS, OS, true, VPL>
+                                  : k_group_scan<KeyT, DT, IS, OS, false, VPL>;
+            const size_t smem = group_scan_smem<VPL>();
+            if (int e = set_smem(kern, smem)) return e;
+            int occ = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, GS_WARPS * 32, smem) != cudaSuccess ||
+                occ < 1)
+                occ = 1;
+            // one range per lane group, one wave of groups
+            const int64_t groups_per_warp = int64_t{32} >> lshift;
+            const RangePlan rp =
+                range_plan(B * C, T, static_cast<int64_t>(occ) * GS_WARPS * groups_per_warp * sm_count());
+            ga.R = rp.R;
+            ga.RL = rp.RL;
+            const int64_t nranges = B * C * rp.R;
+            k_group_prep<KeyT, DT, IS, VPL>
+                <<<static_cast<unsigned>((nranges + GS_WARPS - 1) / GS_WARPS), GS_WARPS * 32, 0, st>>>(ga);
+            if (int e = check_launch()) return e;
+            const int64_t per_block = GS_WARPS * groups_per_warp;
+            kern<<<static_cast<unsigned>((nranges + per_block - 1) / per_block), GS_WARPS * 32, smem, st>>>(ga);
+            return check_launch();
+        };
+        auto by_mode = [&](auto vplc) -> int {
+            if (in_sorted) return go(vplc, IC<1>{}, IC<0>{});
+            if (out_sorted) return go(vplc, IC<0>{}, IC<1>{});
+            return go(vplc, IC<0>{}, IC<0>{});
+        };
+        return vpl == 2 ? by_mode(IC<2>{}) : by_mode(IC<1>{});
+    }
+    // fallbacks: chunked scans with decoupled look-back (flags start at zero)
     const int64_t nch = B * C * sp.nchunks;
     if (cudaMemsetAsync(a.flags, 0, sl.off_agg - sl.off_flags, st) != cudaSuccess) return RAVEL_ERR_CUDA;
     // warp-register kernel when one warp access covers a row
-    using V = typename Elem<DT>::T;
     int el = 0;
     for (int cand = 1; cand <= 8; cand *= 2) {
         if (D > 0 && D % cand == 0 && D / cand <= 32) { el = cand; break; }
     }
     if (el) {
-        const size_t in_es = in_sorted ? sizeof(Acc) : sizeof(V);
-        const size_t out_es = out_sorted ? sizeof(Acc) : sizeof(V);
-        const bool range_ok = (D * in_es) % 16 == 0 && addr_bits(in) % 16 == 0 &&
-                              addr_bits(out) % (el * out_es) == 0 &&
-                              range_scan_smem<Acc>(D, in_es) <= 200 * 1024;
-        if (range_ok) {
-            RangeArgs ra;
-            ra.keys = tv.keys;
-            ra.nvalid = tv.nvalid;
-            ra.T = T; ra.C = C;
-            ra.D = static_cast<uint32_t>(D);
-            ra.tbits = tl.kl.tbits;
-            ra.reverse = reverse;
-            ra.inclusive = inclusive;
-            ra.in = in; ra.out = out; ra.out_mask = out_mask;
-            ra.tail = sc + sl.off_tail;
-            ra.tail_hs = reinterpret_cast<uint32_t*>(sc + sl.off_tail_hs);
-            ra.bounds = reinterpret_cast<int64_t*>(sc + sl.off_bounds);
-            ra.fd_vpr = FastDiv(static_cast<uint32_t>(D * in_es / 16));
-            const size_t smem = range_scan_smem<Acc>(D, in_es);
-            auto go = [&](auto elc, auto inc, auto outc) -> int {
-                constexpr int EL = decltype(elc)::value;
-                constexpr bool IS = decltype(inc)::value != 0;
-                constexpr bool OS = decltype(outc)::value != 0;
-                auto kern = inclusive ? k_range_scan<KeyT, DT, EL, IS, OS, true>
-                                      : k_range_scan<KeyT, DT, EL, IS, OS, false>;
-                if (int e = set_smem(kern, smem)) return e;
-                int occ = 0;
-                if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, RS_WARPS * 32, smem) != cudaSuccess ||
-                    occ < 1)
-                    occ = 1;
-                // one range per warp, one wave of warps
-                const RangePlan rp = range_plan(B * C, T, static_cast<int64_t>(occ) * RS_WARPS * sm_count());
-                ra.R = rp.R;
-                ra.RL = rp.RL;
-                ra.S = B * C;
-                const int64_t nranges = B * C * rp.R;
-                k_range_tail<KeyT, DT, EL, IS><<<static_cast<unsigned>(nranges), RS_WARPS * 32, 0, st>>>(ra);
-                if (int e = check_launch()) return e;
-                kern<<<static_cast<unsigned>((nranges + RS_WARPS - 1) / RS_WARPS), RS_WARPS * 32, smem, st>>>(ra);
-                return check_launch();
-            };
-            auto by_mode = [&](auto elc) -> int {
-                if (in_sorted) return go(elc, IC<1>{}, IC<0>{});
-                if (out_sorted) return go(elc, IC<0>{}, IC<1>{});
-                return go(elc, IC<0>{}, IC<0>{});
-            };
-            switch (el) {
-                case 1: return by_mode(IC<1>{});
-                case 2: return by_mode(IC<2>{});
-                case 4: return by_mode(IC<4>{});
-                default: return by_mode(IC<8>{});
-            }
-        }
         const bool aligned = addr_bits(in) % (el * in_es) == 0 && addr_bits(out) % (el * out_es) == 0;
         const int P = scanw_positions(D, static_cast<int>(in_es));
         if (aligned && P >= sp.min_P) {

@@ -724,371 +724,354 @@ __device__ __forceinline__ RawWords<EL * sizeof(X)> pack(const Acc (&v)[EL]) {
     return r;
 }
 
-// ------------------------------------------------------------------ range scan (two kernels)
-// The scan used for rows that are whole multiples of 16 bytes.  Each stream's
-// tape (in scan order) is cut into R ranges of RL positions, and no CTA ever
-// waits on another:
-//   k_range_tail  one CTA per range: finds the range's last segment start from
-//                 the keys and sums the rows after it (its trailing segment),
-//                 i.e. the carry it hands to later ranges; has_start says
-//                 whether the range contains a segment start at all;
-//   k_range_scan  one CTA per range: folds the tails of the earlier ranges of
-//                 its stream into its carry-in, then streams its chunks of 256
-//                 positions: warp w owns 32 rows per chunk, stages them with
-//                 cp.async into a double-buffered tile (keys prefetched two
-//                 chunks ahead), scans them with lanes over columns, writes the
-//                 results in place and stores whole rows 16 bytes per lane.
-// The tails cost one extra read of the rows after each range's last segment
-// start (a few percent of the tape for Zipf addresses).
-constexpr int RS_WARPS = 8;
-constexpr int RS_CHUNK = RS_WARPS * 32;
+// ------------------------------------------------------------------ group scan (two kernels)
+// The scan used for rows that are whole multiples of 16 bytes, up to 1 KB.
+// Each stream's tape (in scan order) is cut into R ranges of about RL
+// positions; a nominal boundary r*RL moves forward to a segment start when one
+// lies within `snap` positions, so every range stays within RL + snap.
+//   k_group_prep  one warp per range: writes its lower boundary lo, its last
+//                 segment start ls, and -- when its upper boundary hi falls
+//                 inside a segment -- its piece: the sum of its rows from ls
+//                 (from lo when it holds no start) to hi, which is the carry it
+//                 hands to the next range.  Pieces never overlap.
+//   k_group_scan  a group of L = row_bytes / (16 VPL) lanes per range (32/L
+//                 ranges per warp); each lane owns VPL 16-byte column slices of
+//                 every row.  A lane stages its own slices with cp.async into a
+//                 lane-private ring of shared memory GS_Q blocks of GS_U rows
+//                 deep, so no lane ever waits on another.  The group visits
+//                 ls .. hi-1 first -- the rows the prep kernel has just read,
+//                 so likely still in L2 -- then lo .. ls-1; the carry (the pieces of the
+//                 ranges before, back to one that holds a segment start)
+//                 enters at lo.  The running sum is reset at segment starts.
+// No block waits on another.  Rows are read and written in tape order, i.e. at
+// random row addresses, so the scan kernel is bounded by random 16-byte-sliced
+// row traffic rather than by streaming bandwidth.
+// Tuning constants (overridable at build time for sweeps).
+#ifndef RAVEL_GS_WARPS
+#define RAVEL_GS_WARPS 4
+#endif
+#ifndef RAVEL_GS_U
+#define RAVEL_GS_U 4
+#endif
+#ifndef RAVEL_GS_Q
+#define RAVEL_GS_Q 3
+#endif
+#ifndef RAVEL_GS_SNAP
+#define RAVEL_GS_SNAP 32
+#endif
+constexpr int GS_WARPS = RAVEL_GS_WARPS;  // warps per block
+constexpr int GS_U = RAVEL_GS_U;          // rows per ring block
+constexpr int GS_Q = RAVEL_GS_Q;          // ring blocks (GS_Q - 1 blocks in flight)
+constexpr int GS_SNAP = RAVEL_GS_SNAP;    // boundary snap window, <= 32
+static_assert(GS_SNAP >= 0 && GS_SNAP <= 32, "snap window is one warp ballot");
 
-struct RangeArgs {
+struct GsArgs {
     int64_t S;             // streams
     const void* keys;      // [S][T]
     const int* nvalid;     // [S] or null
     int64_t T, C;
     uint32_t D;
     int tbits;
-    int reverse, inclusive;
-    int64_t R, RL;         // ranges per stream, positions per range (multiple of RS_CHUNK)
-    const void* in;        // dtype [N, D] gathered by flat row, or Acc [S*T, D] by tape index
-    void* out;             // dtype [N, D] scattered by flat row, or Acc [S*T, D] by tape index
-    uint8_t* out_mask;     // optional [N]
-    void* tail;            // Acc [S*R, D]
-    uint32_t* tail_hs;     // [S*R]
-    int64_t* bounds;       // [S*(R+1)] range boundaries in scan order
-    FastDiv fd_vpr;        // 16-byte vectors per input row
+    int reverse;
+    int lshift;            // log2 of lanes per row group (L)
+    int snap;              // boundary snap window, <= 32
+    int64_t R, RL;         // ranges per stream, nominal positions per range
+    const void* in;        // dtype [N, D] by flat row, or Acc [S*T, D] by tape index
+    void* out;             // dtype [N, D] by flat row, or Acc [S*T, D] by tape index
+    uint8_t* out_mask;     // optional [N]: 1 where an earlier write of the segment exists
+    void* piece;           // Acc [S*R, D]
+    int32_t* bounds;       // [S*(R+1)] lower boundaries in scan order, then n_s
+    int32_t* rot;          // [S*R] last segment start in the range, else lo
+    uint32_t* rflags;      // [S*R] bit 0: range holds a segment start; bit 1: piece written
 };
 
+// Keys of one stream addressed in scan order.
 template <typename KeyT>
-__device__ __forceinline__ bool range_is_start(const KeyT* keys, int64_t si, int64_t n_s, int reverse, int tbits) {
-    if (si == 0) return true;
-    const int64_t p = reverse ? (n_s - 1 - si) : si;
-    const int64_t pp = reverse ? (n_s - si) : (si - 1);
-    return (keys[p] >> tbits) != (keys[pp] >> tbits);
-}
-
-template <typename KeyT>
-__device__ __forceinline__ uint32_t range_row(const KeyT* keys, const RowMap& rows_of, int64_t s, int64_t si,
-                                              int64_t n_s, int reverse, int tbits, int64_t T, bool sorted) {
-    const int64_t p = reverse ? (n_s - 1 - si) : si;
-    if (sorted) return static_cast<uint32_t>(s * T + p);
-    const KeyT tmask = (static_cast<KeyT>(1) << tbits) - 1;
-    return rows_of(keys[p] & tmask);
-}
-
-// First segment start in [x, end) of the scan order, or -1 (block-wide).
-template <typename KeyT>
-__device__ int64_t first_start_from(const KeyT* keys, int64_t x, int64_t end, int64_t n_s, int reverse, int tbits,
-                                    int* s_tmp) {
-    for (int64_t b0 = x; b0 < end; b0 += RS_CHUNK) {
-        if (threadIdx.x == 0) *s_tmp = RS_CHUNK;
-        __syncthreads();
-        const int64_t si = b0 + threadIdx.x;
-        if (si < end && range_is_start(keys, si, n_s, reverse, tbits)) atomicMin(s_tmp, static_cast<int>(threadIdx.x));
-        __syncthreads();
-        const int f = *s_tmp;
-        __syncthreads();
-        if (f < RS_CHUNK) return b0 + f;
+struct ScanKeys {
+    const KeyT* k;
+    int64_t n;
+    int reverse, tbits;
+    __device__ __forceinline__ int64_t pos(int64_t si) const { return reverse ? n - 1 - si : si; }
+    __device__ __forceinline__ KeyT at(int64_t si) const { return k[pos(si)]; }
+    __device__ __forceinline__ bool start(int64_t si) const {
+        return si == 0 || ((at(si) ^ at(si - 1)) >> tbits) != 0;
     }
-    return -1;
-}
+};
 
-// Last segment start in [x, end) of the scan order, or -1 (block-wide).
-template <typename KeyT>
-__device__ int64_t last_start_before(const KeyT* keys, int64_t x, int64_t end, int64_t n_s, int reverse, int tbits,
-                                     int* s_tmp) {
-    for (int64_t e0 = end; e0 > x; e0 -= RS_CHUNK) {
-        if (threadIdx.x == 0) *s_tmp = -1;
-        __syncthreads();
-        const int64_t si = e0 - 1 - threadIdx.x;
-        if (si >= x && range_is_start(keys, si, n_s, reverse, tbits)) atomicMax(s_tmp, static_cast<int>(si - x));
-        __syncthreads();
-        const int f = *s_tmp;
-        __syncthreads();
-        if (f >= 0) return x + f;
-    }
-    return -1;
-}
-
-// Range boundaries: the nominal boundary r*RL moves forward to the next segment
-// start within one range length, so that the range needs no carry.  Only when
-// a segment is longer than a range does a boundary stay unsnapped; then the
-// range before it publishes its tail (sum of its rows after its last segment
-// start, or of all its rows when it has none) for the next range to fold.
-template <typename KeyT, int DT, int EL, bool IN_SORTED>
-__global__ void __launch_bounds__(RS_WARPS * 32) k_range_tail(RangeArgs a) {
-    using Acc = typename Elem<DT>::Acc;
-    using InT = typename std::conditional<IN_SORTED, Acc, typename Elem<DT>::T>::type;
-    __shared__ int s_tmp;
-    __shared__ uint32_t s_rows[RS_CHUNK];
-    __shared__ Acc s_red[RS_WARPS][32 * EL];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int64_t s = blockIdx.x / a.R, r = blockIdx.x % a.R;
+template <typename KeyT, int DT, bool IN_SORTED, int VPL>
+__global__ void __launch_bounds__(GS_WARPS * 32) k_group_prep(GsArgs a) {
+    using E = Elem<DT>;
+    using Acc = typename E::Acc;
+    using InT = typename std::conditional<IN_SORTED, Acc, typename E::T>::type;
+    constexpr int EL = 16 / static_cast<int>(sizeof(InT));
+    constexpr int NE = VPL * EL;
+    const int lane = threadIdx.x & 31;
+    const int64_t g = static_cast<int64_t>(blockIdx.x) * GS_WARPS + (threadIdx.x >> 5);
+    if (g >= a.S * a.R) return;  // whole warp
+    const int64_t s = g / a.R, r = g - s * a.R;
     const int64_t n_s = a.nvalid ? a.nvalid[s] : a.T;
-    const KeyT* keys = static_cast<const KeyT*>(a.keys) + s * a.T;
-    const uint32_t D = a.D;
-    Acc* tail = static_cast<Acc*>(a.tail) + (s * a.R + r) * D;
-    auto snap = [&](int64_t x) -> int64_t {  // boundary at nominal position x
+    const ScanKeys<KeyT> kk{static_cast<const KeyT*>(a.keys) + s * a.T, n_s, a.reverse, a.tbits};
+    // boundary at nominal scan index x: the first segment start in [x, x + snap), else x
+    auto snap = [&](int64_t x) -> int64_t {
         if (x >= n_s) return n_s;
         if (x == 0) return 0;
-        const int64_t f = first_start_from(keys, x, x + a.RL < n_s ? x + a.RL : n_s, n_s, a.reverse, a.tbits, &s_tmp);
-        return f >= 0 ? f : x;
+        const int64_t si = x + lane;
+        const unsigned m = __ballot_sync(0xffffffffu, lane < a.snap && si < n_s && kk.start(si));
+        return m ? x + __ffs(m) - 1 : x;
     };
     const int64_t lo = snap(r * a.RL);
     const int64_t hi = snap((r + 1) * a.RL);
-    if (tid == 0) {
-        a.bounds[s * (a.R + 1) + r] = lo;
-        if (r == a.R - 1) a.bounds[s * (a.R + 1) + a.R] = n_s;
+    int64_t ls = -1;
+    for (int64_t e0 = hi; e0 > lo && ls < 0; e0 -= 128) {  // last segment start in [lo, hi), 128 keys a round
+        unsigned m[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int64_t si = e0 - 1 - 32 * q - lane;
+            m[q] = __ballot_sync(0xffffffffu, si >= lo && kk.start(si));
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            if (ls < 0 && m[q] != 0u) ls = e0 - 32 * q - __ffs(m[q]);
     }
-    const bool hi_unsnapped = hi < n_s && !range_is_start(keys, hi, n_s, a.reverse, a.tbits);
-    if (!hi_unsnapped || lo >= hi) {
-        if (tid == 0) a.tail_hs[s * a.R + r] = 1u;  // never folded past
-        return;
+    const bool hi_open = hi < n_s && lo < hi && !kk.start(hi);
+    const int64_t rot = ls >= 0 ? ls : lo;
+    if (lane == 0) {
+        int32_t* bounds = a.bounds + s * (a.R + 1);
+        bounds[r] = static_cast<int32_t>(lo);
+        if (r == a.R - 1) bounds[a.R] = static_cast<int32_t>(n_s);
+        a.rot[g] = static_cast<int32_t>(rot);
+        a.rflags[g] = (ls >= 0 ? 1u : 0u) | (hi_open ? 2u : 0u);
     }
-    const int64_t ls = last_start_before(keys, lo, hi, n_s, a.reverse, a.tbits, &s_tmp);
+    if (!hi_open) return;
+    // piece = sum of rows [rot, hi): lane l fetches the row of piece index 32q + l for
+    // 8 chunks q at once; groups of L lanes then read each chunk's rows, L rows a group
+    const uint32_t L = 1u << a.lshift, G = 32u >> a.lshift;
+    const uint32_t grp = static_cast<uint32_t>(lane) >> a.lshift, lig = static_cast<uint32_t>(lane) & (L - 1);
     const RowMap rows_of(s, a.T, a.C);
-    const int64_t t0 = ls >= 0 ? ls : lo;
-    const bool active = static_cast<uint32_t>(lane * EL) < D;
-    const uint32_t col = static_cast<uint32_t>(lane * EL);
-    const InT* in = static_cast<const InT*>(a.in);
-    Acc acc[EL];
+    const KeyT tmask = (static_cast<KeyT>(1) << a.tbits) - 1;
+    const char* in = static_cast<const char*>(a.in) + lig * 16u;
+    const uint64_t rb = static_cast<uint64_t>(a.D) * sizeof(InT);
+    Acc acc[NE];
 #pragma unroll
-    for (int q = 0; q < EL; ++q) acc[q] = Acc(0);
-    for (int64_t b0 = t0; b0 < hi; b0 += RS_CHUNK) {  // 256 rows at a time, all loads in flight
-        const int64_t si = b0 + tid;
-        if (si < hi) s_rows[tid] = range_row(keys, rows_of, s, si, n_s, a.reverse, a.tbits, a.T, IN_SORTED);
-        __syncthreads();
-        const int nb = static_cast<int>(hi - b0 < RS_CHUNK ? hi - b0 : RS_CHUNK);
+    for (int q = 0; q < NE; ++q) acc[q] = Acc(0);
+    const int64_t n = hi - rot;
+    auto row_of = [&](int64_t i) -> uint32_t {
+        if (i >= n) return 0u;
+        const int64_t p = kk.pos(rot + i);
+        return IN_SORTED ? static_cast<uint32_t>(s * a.T + p) : rows_of(kk.k[p] & tmask);
+    };
+    for (int64_t c0 = 0; c0 < n; c0 += 256) {
+        uint32_t rw[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) rw[q] = row_of(c0 + 32 * q + lane);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const int64_t cnt = n - c0 - 32 * q;  // rows left from this chunk on
+            if (cnt <= 0) break;
 #pragma unroll 8
-        for (int i = warp; i < nb; i += RS_WARPS) {
-            if (active) {
-                const RawWords<EL * sizeof(InT)> x = ld_frag<InT, EL>(in + static_cast<uint64_t>(s_rows[i]) * D + col);
+            for (uint32_t u = 0; u < L; ++u) {
+                const uint32_t j = u * G + grp;
+                const uint32_t row = __shfl_sync(0xffffffffu, rw[q], static_cast<int>(j));
+                if (static_cast<int64_t>(j) < cnt) {
 #pragma unroll
-                for (int q = 0; q < EL; ++q) acc[q] += frag_get<InT, Acc, EL>(x, q);
+                    for (int v = 0; v < VPL; ++v) {
+                        const uint4 w = ld_nc_v4(in + row * rb + v * L * 16u);
+                        RawWords<16> x;
+                        x.w[0] = w.x; x.w[1] = w.y; x.w[2] = w.z; x.w[3] = w.w;
+                        Acc f[EL];
+                        unpack<InT, Acc, EL>(x, f);
+#pragma unroll
+                        for (int e = 0; e < EL; ++e) acc[v * EL + e] += f[e];
+                    }
+                }
             }
         }
-        __syncthreads();
     }
+    for (uint32_t off = L; off < 32u; off <<= 1)
 #pragma unroll
-    for (int q = 0; q < EL; ++q) s_red[warp][lane * EL + q] = acc[q];
-    __syncthreads();
-    if (warp == 0 && active) {
+        for (int q = 0; q < NE; ++q) acc[q] += __shfl_xor_sync(0xffffffffu, acc[q], static_cast<int>(off));
+    if (grp == 0) {
+        Acc* pc = static_cast<Acc*>(a.piece) + g * a.D;
 #pragma unroll
-        for (int q = 0; q < EL; ++q) {
-            Acc v = Acc(0);
-            for (int w = 0; w < RS_WARPS; ++w) v += s_red[w][lane * EL + q];
-            tail[col + q] = v;
-        }
+        for (int v = 0; v < VPL; ++v)
+#pragma unroll
+            for (int e = 0; e < EL; ++e) pc[(lig + v * L) * EL + e] = acc[v * EL + e];
     }
-    if (tid == 0) a.tail_hs[s * a.R + r] = ls >= 0 ? 1u : 0u;
 }
 
-template <typename KeyT, int DT, int EL, bool IN_SORTED, bool OUT_SORTED, bool INCL>
-__global__ void __launch_bounds__(RS_WARPS * 32) k_range_scan(RangeArgs a) {
+template <int VPL>
+constexpr size_t group_scan_smem() {
+    return static_cast<size_t>(GS_WARPS) * GS_Q * GS_U * 32 * (16 * VPL + 4);
+}
+
+template <typename KeyT, int DT, bool IN_SORTED, bool OUT_SORTED, bool INCL, int VPL>
+__global__ void __launch_bounds__(GS_WARPS * 32) k_group_scan(GsArgs a) {
     using E = Elem<DT>;
     using Acc = typename E::Acc;
     using V = typename E::T;
     using InT = typename std::conditional<IN_SORTED, Acc, V>::type;
     using OutT = typename std::conditional<OUT_SORTED, Acc, V>::type;
-    constexpr bool INPLACE = std::is_same<InT, OutT>::value;
+    constexpr int EL = 16 / static_cast<int>(sizeof(InT));
+    constexpr int NE = VPL * EL;
+    constexpr int SLOTS = GS_Q * GS_U;
     extern __shared__ __align__(16) unsigned char smem[];
-    const uint32_t D = a.D;
-    const uint32_t rb = D * static_cast<uint32_t>(sizeof(InT));
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    // each warp owns one range and a double-buffered tile of 2 x 32 rows
-    unsigned char* wbuf = smem + static_cast<size_t>(warp) * 2 * 32 * rb;
-    const int64_t gw = static_cast<int64_t>(blockIdx.x) * RS_WARPS + warp;
-    const int64_t S = a.S;
-    if (gw >= S * a.R) return;
-    const int64_t s = gw / a.R, r = gw % a.R;
-    const int64_t n_s = a.nvalid ? a.nvalid[s] : a.T;
-    const int64_t lo = a.bounds[s * (a.R + 1) + r];
-    const int64_t hi = a.bounds[s * (a.R + 1) + r + 1];
+    // lane-private ring: slot j of this lane's data at ring + (j*32 + lane)*16*VPL,
+    // its row word (output row | start bit 31) at meta + (j*32 + lane)*4
+    const uint32_t ring = smem_u32(smem) + static_cast<uint32_t>(warp) * SLOTS * 32 * (16 * VPL + 4);
+    const uint32_t meta = ring + SLOTS * 32 * 16 * VPL;
+    const uint32_t L = 1u << a.lshift;
+    const uint32_t grp = static_cast<uint32_t>(lane) >> a.lshift, lig = static_cast<uint32_t>(lane) & (L - 1);
+    const int64_t g = (static_cast<int64_t>(blockIdx.x) * GS_WARPS + warp) * (32 >> a.lshift) + grp;
+    if (g >= a.S * a.R) return;  // this group only: nothing below synchronises lanes
+    const int64_t s = g / a.R, r = g - s * a.R;
+    const int32_t* bounds = a.bounds + s * (a.R + 1);
+    const int32_t lo = bounds[r], hi = bounds[r + 1];
     if (lo >= hi) return;
-    const KeyT* keys = static_cast<const KeyT*>(a.keys) + s * a.T;
-    const bool active = static_cast<uint32_t>(lane * EL) < D;
-    const uint32_t col = static_cast<uint32_t>(lane * EL);
-    const InT* in = static_cast<const InT*>(a.in);
-    OutT* out = static_cast<OutT*>(a.out);
-    const int nch = static_cast<int>((hi - lo + 31) / 32);
-    const KeyT tmask = (static_cast<KeyT>(1) << a.tbits) - 1;
-    const RowMap rows_of(s, a.T, a.C);
+    const int32_t n_s = a.nvalid ? a.nvalid[s] : static_cast<int32_t>(a.T);
+    const ScanKeys<KeyT> kk{static_cast<const KeyT*>(a.keys) + s * a.T, n_s, a.reverse, a.tbits};
+    // key of scan position si at kbase[dir * si]; tape index tix0 + dir * si
+    const int32_t dir = a.reverse ? -1 : 1;
+    const KeyT* kbase = static_cast<const KeyT*>(a.keys) + s * a.T + (a.reverse ? n_s - 1 : 0);
+    const uint32_t tix0 = static_cast<uint32_t>(s * a.T) + static_cast<uint32_t>(a.reverse ? n_s - 1 : 0);
+    const int32_t rot = a.rot[g];
+    const int32_t len = hi - lo, nA = hi - rot;
+    const int32_t offA = rot, offB = lo - nA;  // si = i + (i < nA ? offA : offB)
+    const int32_t inj = nA == len ? 0 : nA;    // sequence index of position lo
+    const uint32_t D = a.D;
+    const int tb = a.tbits;
 
-    // carry-in: zero when the range starts a segment (snapped boundary), else
-    // the tails of the earlier ranges back to the one holding the segment start
-    Acc run[EL];
+    // carry entering at lo: pieces of the ranges before, back to one with a segment start
+    Acc carry[NE];
 #pragma unroll
-    for (int q = 0; q < EL; ++q) run[q] = Acc(0);
-    if (!range_is_start(keys, lo, n_s, a.reverse, a.tbits) && active) {
-        const Acc* tails = static_cast<const Acc*>(a.tail) + s * a.R * D;
+    for (int q = 0; q < NE; ++q) carry[q] = Acc(0);
+    if (!kk.start(lo)) {
+        const Acc* pc = static_cast<const Acc*>(a.piece) + s * a.R * D;
         for (int64_t rr = r - 1; rr >= 0; --rr) {
 #pragma unroll
-            for (int q = 0; q < EL; ++q) run[q] += tails[rr * D + col + q];
-            if (a.tail_hs[s * a.R + rr] != 0u) break;
+            for (int v = 0; v < VPL; ++v)
+#pragma unroll
+                for (int e = 0; e < EL; ++e) carry[v * EL + e] += pc[rr * D + (lig + v * L) * EL + e];
+            if (a.rflags[s * a.R + rr] & 1u) break;
         }
     }
+    // keys before the two sequence breaks (i = 0 at rot, i = nA at lo); ~key marks a stream start
+    const KeyT kbr0 = rot > 0 ? kbase[dir * (rot - 1)] : ~kbase[dir * rot];
+    const KeyT kbrA = (nA < len && lo > 0) ? kbase[dir * (lo - 1)] : ~kbase[dir * lo];
 
-    struct KeyPair { KeyT k, kp; };
-    auto load_keys = [&](int c) -> KeyPair {
-        KeyPair kk{KeyT(0), KeyT(0)};
-        const int64_t si = lo + static_cast<int64_t>(c) * 32 + lane;
-        if (c < nch && si < hi) {
-            kk.k = keys[a.reverse ? (n_s - 1 - si) : si];
-            if (si > 0) kk.kp = keys[a.reverse ? (n_s - si) : (si - 1)];
-        }
-        return kk;
-    };
-    // row indices (input, output) and segment start of this lane's position in chunk c
-    auto derive = [&](int c, const KeyPair& kk, uint32_t& my_in, uint32_t& my_out, bool& st) {
-        const int64_t si = lo + static_cast<int64_t>(c) * 32 + lane;
-        my_in = 0; my_out = 0; st = false;
-        if (c < nch && si < hi) {
-            const int64_t p = a.reverse ? (n_s - 1 - si) : si;
-            const uint32_t tix = static_cast<uint32_t>(s * a.T + p);
-            const uint32_t flat = rows_of(kk.k & tmask);
-            my_in = IN_SORTED ? tix : flat;
-            my_out = OUT_SORTED ? tix : flat;
-            st = si == 0 || (kk.k >> a.tbits) != (kk.kp >> a.tbits);
+    const RowMap rows_of(s, a.T, a.C);
+    const KeyT tmask = (static_cast<KeyT>(1) << tb) - 1;
+    const char* in = static_cast<const char*>(a.in) + lig * 16u;
+    char* out = static_cast<char*>(a.out) + lig * static_cast<uint32_t>(EL * sizeof(OutT));
+    uint8_t* omask = (a.out_mask != nullptr && lig == 0) ? a.out_mask : nullptr;
+    const uint32_t rbi = D * static_cast<uint32_t>(sizeof(InT));
+    const uint32_t rbo = D * static_cast<uint32_t>(sizeof(OutT));
+    const int32_t nb = (len + GS_U - 1) / GS_U;
+    const uint32_t lane_slot = static_cast<uint32_t>(lane);
+
+    auto load_keys = [&](int32_t b, KeyT (&k)[GS_U]) {
+#pragma unroll
+        for (int u = 0; u < GS_U; ++u) {
+            const int32_t i = b * GS_U + u;
+            if (i < len) k[u] = kbase[dir * (i + (i < nA ? offA : offB))];
         }
     };
-    const uint32_t vpr = rb / 16;
-    // lane -> (row offset, 16-byte vector) once, when a row's vectors divide 32
-    const bool lane_split = vpr <= 32 && (32 % vpr) == 0;
-    uint32_t l_rr = 0, l_v = 0;
-    a.fd_vpr.divmod(static_cast<uint32_t>(lane), l_rr, l_v);
-    const uint32_t rows_per_pass = lane_split ? 32 / vpr : 0;
-    auto stage = [&](int c, uint32_t my_in) {
-        unsigned char* tile = wbuf + static_cast<size_t>(c & 1) * 32 * rb;
-        const int64_t base = lo + static_cast<int64_t>(c) * 32;
-        const int nvw = static_cast<int>(hi - base < 32 ? hi - base : 32);
-        if (lane_split) {
-            for (uint32_t rr = l_rr; rr < 32; rr += rows_per_pass) {  // uniform trip count
-                const uint32_t row = __shfl_sync(0xffffffffu, my_in, static_cast<int>(rr));
-                if (static_cast<int>(rr) < nvw)
-                    cp_async16(tile + rr * rb + l_v * 16,
-                               reinterpret_cast<const char*>(in + static_cast<uint64_t>(row) * D) + l_v * 16);
+    KeyT klast = KeyT(0);  // key of the row staged last
+    // stage block b into ring block b % GS_Q from its keys (always commits one group)
+    auto stage = [&](int32_t b, const KeyT (&kb)[GS_U]) {
+        if (b < nb) {
+            const uint32_t slot0 = static_cast<uint32_t>(b % GS_Q) * GS_U;
+#pragma unroll
+            for (int u = 0; u < GS_U; ++u) {
+                const int32_t i = b * GS_U + u;
+                if (i < len) {
+                    const KeyT k = kb[u];
+                    const KeyT kp = i == 0 ? kbr0 : (i == nA ? kbrA : (u > 0 ? kb[u - 1] : klast));
+                    const bool st = ((k ^ kp) >> tb) != 0;
+                    uint32_t rin, rout;
+                    if (IN_SORTED || OUT_SORTED) {
+                        const uint32_t tix = tix0 + static_cast<uint32_t>(dir * (i + (i < nA ? offA : offB)));
+                        const uint32_t flat = rows_of(k & tmask);
+                        rin = IN_SORTED ? tix : flat;
+                        rout = OUT_SORTED ? tix : flat;
+                    } else {
+                        rin = rout = rows_of(k & tmask);
+                    }
+                    const uint32_t slot = (slot0 + u) * 32 + lane_slot;
+#pragma unroll
+                    for (int v = 0; v < VPL; ++v)
+                        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(ring + (slot * VPL + v) * 16),
+                                     "l"(in + static_cast<uint64_t>(rin) * rbi + v * L * 16u)
+                                     : "memory");
+                    asm volatile("st.shared.u32 [%0], %1;" ::"r"(meta + slot * 4), "r"(rout | (st ? 0x80000000u : 0u))
+                                 : "memory");
+                }
             }
-        } else {
-            const uint32_t total = static_cast<uint32_t>(nvw) * vpr;
-            for (uint32_t e0 = 0; e0 < total; e0 += 32) {  // uniform trip count: full-warp shuffles
-                const uint32_t e = e0 + lane;
-                uint32_t rr, v;
-                a.fd_vpr.divmod(e, rr, v);
-                const uint32_t row = __shfl_sync(0xffffffffu, my_in, static_cast<int>(rr & 31u));
-                if (e < total)
-                    cp_async16(tile + rr * rb + v * 16,
-                               reinterpret_cast<const char*>(in + static_cast<uint64_t>(row) * D) + v * 16);
-            }
+            klast = kb[GS_U - 1];
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
 
-    uint32_t in_cur, out_cur;
-    bool st_cur;
-    derive(0, load_keys(0), in_cur, out_cur, st_cur);
-    stage(0, in_cur);
-    KeyPair k_next = load_keys(1);
-
-    for (int c = 0; c < nch; ++c) {
-        uint32_t in_nx = 0, out_nx = 0;
-        bool st_nx = false;
-        if (c + 1 < nch) {
-            derive(c + 1, k_next, in_nx, out_nx, st_nx);
-            stage(c + 1, in_nx);
-            k_next = load_keys(c + 2);
-            asm volatile("cp.async.wait_group 1;" ::: "memory");
-        } else {
-            asm volatile("cp.async.wait_group 0;" ::: "memory");
-        }
-        __syncwarp();
-        const unsigned sm = __ballot_sync(0xffffffffu, st_cur);
-        const int64_t base = lo + static_cast<int64_t>(c) * 32;
-        const int nv = static_cast<int>(hi - base < 32 ? hi - base : 32);
-        if (a.out_mask != nullptr && lane < nv) a.out_mask[out_cur] = st_cur ? 0 : 1;
-        unsigned char* tile = wbuf + static_cast<size_t>(c & 1) * 32 * rb;
-        const uint32_t tile_s = smem_u32(tile) + col * static_cast<uint32_t>(sizeof(InT));
-        // one pass with the running carry
-        if (INPLACE && nv == 32) {
+    Acc acc[NE];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                const uint32_t addr = tile_s + static_cast<uint32_t>(i) * rb;
-                // lanes past the row's columns (lane*EL >= D) must not touch shared
-                // memory: their addresses run past the row and, on the last row of
-                // the last tile, past the allocation
-                RawWords<EL * sizeof(InT)> x{};
-                if (active) x = lds_words<EL * sizeof(InT)>(addr);
-                Acc v[EL];
-                unpack<InT, Acc, EL>(x, v);
-                const bool stt = (sm >> i) & 1u;
-                Acc o[EL];
+    for (int q = 0; q < NE; ++q) acc[q] = Acc(0);
+    // process block b (staged GS_Q - 1 blocks earlier)
+    auto process = [&](int32_t b) {
+        asm volatile("cp.async.wait_group %0;" ::"n"(GS_Q - 1) : "memory");
+        const uint32_t slot0 = static_cast<uint32_t>(b % GS_Q) * GS_U;
 #pragma unroll
-                for (int q = 0; q < EL; ++q) {
-                    run[q] = stt ? Acc(0) : run[q];
-                    if (INCL) { run[q] += v[q]; o[q] = run[q]; }
-                    else { o[q] = run[q]; run[q] += v[q]; }
-                }
-                if (active) sts_words<EL * sizeof(OutT)>(addr, pack<OutT, Acc, EL>(o));
-            }
-        } else {
-            for (int i = 0; i < nv; ++i) {
-                const uint32_t addr = tile_s + static_cast<uint32_t>(i) * rb;
-                RawWords<EL * sizeof(InT)> x{};
-                if (active) x = lds_words<EL * sizeof(InT)>(addr);  // see the guard above
-                Acc v[EL];
-                unpack<InT, Acc, EL>(x, v);
-                const uint32_t orow = INPLACE ? 0u : __shfl_sync(0xffffffffu, out_cur, i);
-                const bool stt = (sm >> i) & 1u;
-                Acc o[EL];
+        for (int u = 0; u < GS_U; ++u) {
+            const int32_t i = b * GS_U + u;
+            if (i < len) {
+                if (i == inj) {
 #pragma unroll
-                for (int q = 0; q < EL; ++q) {
-                    run[q] = stt ? Acc(0) : run[q];
-                    if (INCL) { run[q] += v[q]; o[q] = run[q]; }
-                    else { o[q] = run[q]; run[q] += v[q]; }
+                    for (int q = 0; q < NE; ++q) acc[q] = carry[q];
                 }
-                if (active) {
-                    if constexpr (INPLACE) sts_words<EL * sizeof(OutT)>(addr, pack<OutT, Acc, EL>(o));
-                    else st_frag<OutT, EL>(out + static_cast<uint64_t>(orow) * D + col, pack<OutT, Acc, EL>(o));
-                }
-            }
-        }
-        if constexpr (INPLACE) {
-            __syncwarp();
-            if (lane_split) {
-                for (uint32_t rr = l_rr; rr < 32; rr += rows_per_pass) {
-                    const uint32_t orow = __shfl_sync(0xffffffffu, out_cur, static_cast<int>(rr));
-                    if (static_cast<int>(rr) < nv) {
-                        const uint4 val = *reinterpret_cast<const uint4*>(tile + rr * rb + l_v * 16);
-                        *reinterpret_cast<uint4*>(reinterpret_cast<char*>(out) + static_cast<uint64_t>(orow) * rb +
-                                                  l_v * 16) = val;
+                const uint32_t slot = (slot0 + u) * 32 + lane_slot;
+                uint32_t mw;
+                asm volatile("ld.shared.u32 %0, [%1];" : "=r"(mw) : "r"(meta + slot * 4));
+                const bool st = static_cast<int32_t>(mw) < 0;
+                const uint32_t orow = mw & 0x7fffffffu;
+#pragma unroll
+                for (int v = 0; v < VPL; ++v) {
+                    const RawWords<16> x = lds_words<16>(ring + (slot * VPL + v) * 16);
+                    Acc f[EL], o[EL];
+                    unpack<InT, Acc, EL>(x, f);
+#pragma unroll
+                    for (int e = 0; e < EL; ++e) {
+                        Acc& c = acc[v * EL + e];
+                        c = st ? Acc(0) : c;
+                        if (INCL) { c += f[e]; o[e] = c; }
+                        else { o[e] = c; c += f[e]; }
                     }
+                    st_frag<OutT, EL>(reinterpret_cast<OutT*>(out + static_cast<uint64_t>(orow) * rbo +
+                                                              v * L * static_cast<uint32_t>(EL * sizeof(OutT))),
+                                      pack<OutT, Acc, EL>(o));
                 }
-            } else {
-                const uint32_t total = static_cast<uint32_t>(nv) * vpr;
-                for (uint32_t e0 = 0; e0 < total; e0 += 32) {
-                    const uint32_t e = e0 + lane;
-                    uint32_t rr, v;
-                    a.fd_vpr.divmod(e, rr, v);
-                    const uint32_t orow = __shfl_sync(0xffffffffu, out_cur, static_cast<int>(rr & 31u));
-                    if (e < total) {
-                        const uint4 val = *reinterpret_cast<const uint4*>(tile + rr * rb + v * 16);
-                        *reinterpret_cast<uint4*>(reinterpret_cast<char*>(out) + static_cast<uint64_t>(orow) * rb +
-                                                  v * 16) = val;
-                    }
-                }
+                if (omask != nullptr) omask[orow] = st ? 0 : 1;
             }
         }
-        __syncwarp();
-        in_cur = in_nx;
-        out_cur = out_nx;
-        st_cur = st_nx;
+    };
+    // keys run two blocks ahead of staging, staging GS_Q - 1 blocks ahead of processing
+    KeyT k0[GS_U], k1[GS_U];
+#pragma unroll
+    for (int b = 0; b < GS_Q - 1; ++b) {
+        load_keys(b, k0);
+        stage(b, k0);
     }
-}
-
-template <typename Acc>
-inline size_t range_scan_smem(int64_t D, size_t in_elem) {
-    return static_cast<size_t>(RS_WARPS) * 2 * 32 * D * in_elem;
+    load_keys(GS_Q - 1, k0);
+    load_keys(GS_Q, k1);
+    for (int32_t b = 0; b < nb; b += 2) {
+        stage(b + GS_Q - 1, k0);
+        load_keys(b + GS_Q + 1, k0);
+        process(b);
+        if (b + 1 < nb) {
+            stage(b + GS_Q, k1);
+            load_keys(b + GS_Q + 2, k1);
+            process(b + 1);
+        }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
 // Rows a warp holds in registers: at most 64 bytes of input per lane (16 rows
