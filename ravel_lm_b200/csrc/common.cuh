@@ -127,6 +127,9 @@ __device__ __forceinline__ int64_t load_addr(const void* base, int64_t i, int ad
 
 __device__ __forceinline__ uint64_t fold_addr(int64_t a, int64_t A, int key32) {
     if (key32) a = static_cast<int64_t>(static_cast<int32_t>(static_cast<uint32_t>(a)));
+    // in-range addresses (the usual case) and power-of-two spaces need no division
+    if (a >= 0 && a < A) return static_cast<uint64_t>(a);
+    if ((A & (A - 1)) == 0) return static_cast<uint64_t>(a & (A - 1));
     int64_t r = a % A;
     if (r < 0) r += A;
     return static_cast<uint64_t>(r);
@@ -185,6 +188,23 @@ template <> __device__ __forceinline__ uint32_t zero_word<RAVEL_F16>(uint32_t w)
 __device__ __forceinline__ void zero_f64_pair(uint32_t& lo, uint32_t& hi) {
     if ((hi & 0x7ff00000u) == 0x7ff00000u) { hi = 0x7ff80000u; lo = 0u; }
     else { hi &= 0x80000000u; lo = 0u; }
+}
+
+// candidate * 0 on a whole 32-bit word at once (two 16-bit elements, or one
+// float): a half's exponent field is all ones exactly when adding one unit to
+// it carries into bit 15, so the non-finite halves are found without branches.
+template <int DT> __device__ __forceinline__ uint32_t zero_word_packed(uint32_t w) {
+    if constexpr (DT == RAVEL_F32) {
+        const uint32_t nf = ((w & 0x7f800000u) + 0x00800000u) & 0x80000000u;
+        return nf ? 0x7fc00000u : (w & 0x80000000u);
+    } else {
+        constexpr uint32_t EXP = DT == RAVEL_BF16 ? 0x7f807f80u : 0x7c007c00u;
+        constexpr uint32_t ONE = DT == RAVEL_BF16 ? 0x00800080u : 0x04000400u;
+        constexpr uint32_t QNAN = DT == RAVEL_BF16 ? 0x7fc07fc0u : 0x7e007e00u;
+        const uint32_t nf = ((w & EXP) + ONE) & 0x80008000u;
+        const uint32_t mm = (nf >> 15) * 0xffffu;  // all ones over each non-finite half
+        return (mm & QNAN) | (w & 0x80008000u & ~mm);
+    }
 }
 
 // Zero a vector of VB bytes (VB in {2, 4, 8, 16}) held as 32-bit words.

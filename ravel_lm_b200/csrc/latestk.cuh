@@ -150,6 +150,36 @@ __global__ void __launch_bounds__(256) k_lk_fwd_fast(LkArgs a) {
             st_vec_stream<VB>(outv + blk * a.row_bytes + o * VB, x);
             if (o == 0) a.out_mask[blk] = valid ? 1 : 0;
         }
+    } else if (32 % rv == 0 && DT != RAVEL_F64) {
+        // one position per warp; lane = (slot offset j0, vector o) fixed for the
+        // kernel, slots j0, j0 + 32/rv, ... in successive passes
+        const uint32_t jstep = 32 / rv;
+        const uint32_t o = static_cast<uint32_t>(lane) % rv, j0 = static_cast<uint32_t>(lane) / rv;
+        const uint32_t rows_s = smem_u32(rows) + o * VB;
+        const uint32_t rb32 = static_cast<uint32_t>(a.row_bytes);
+        const uint64_t blk_bytes = static_cast<uint64_t>(a.row_bytes) * static_cast<uint64_t>(k);
+        for (int i = warp; i < np; i += 8) {
+            const int wi = i + k;
+            const uint32_t my = static_cast<uint32_t>(wadr[wi]);
+            const uint32_t orow = static_cast<uint32_t>(wrow[wi]);
+            char* ob = outv + orow * blk_bytes + o * VB;
+            uint8_t* mb = a.out_mask + static_cast<uint64_t>(orow) * static_cast<uint64_t>(k);
+            for (uint32_t j = j0; j < static_cast<uint32_t>(k); j += jstep) {
+                const int src = wi - 1 - static_cast<int>(j);
+                const bool valid = static_cast<uint32_t>(wadr[src]) == my;
+                uint4 x;
+                asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                             : "=r"(x.x), "=r"(x.y), "=r"(x.z), "=r"(x.w)
+                             : "r"(rows_s + static_cast<uint32_t>(src) * rb32));
+                if (!valid) {
+                    x.x = zero_word_packed<DT>(x.x);
+                    if constexpr (VB >= 8) x.y = zero_word_packed<DT>(x.y);
+                    if constexpr (VB == 16) { x.z = zero_word_packed<DT>(x.z); x.w = zero_word_packed<DT>(x.w); }
+                }
+                st_vec_stream<VB>(ob + j * rb32, x);
+                if (o == 0) mb[j] = valid ? 1 : 0;
+            }
+        }
     } else {
         // one position per warp, ceil(bv/32) passes
         for (int i = warp; i < np; i += 8) {

@@ -247,3 +247,53 @@ def test_tape_cache_reuse_and_invalidation():
     s_ref, _ = causal_sum_lookup(w, p, address_space=A)
     assert torch.equal(s_new, s_ref)
     assert not torch.equal(s_new, s_fresh)
+
+
+SPECIAL_BITS = {
+    # +Inf, -Inf, quiet NaN, NaN with payload and sign, -0, +0, smallest subnormal, -subnormal, max finite
+    torch.bfloat16: [0x7F80, 0xFF80, 0x7FC0, 0xFFA1, 0x8000, 0x0000, 0x0001, 0x8001, 0x7F7F],
+    torch.float16: [0x7C00, 0xFC00, 0x7E00, 0xFE01, 0x8000, 0x0000, 0x0001, 0x8001, 0x7BFF],
+    torch.float32: [0x7F800000, 0xFF800000, 0x7FC00000, 0xFFC12345, 0x80000000, 0x0, 0x1, 0x80000001, 0x7F7FFFFF],
+    torch.float64: [0x7FF0000000000000, 0xFFF0000000000000, 0x7FF8000000000000, 0xFFF8000000000ABC,
+                    0x8000000000000000, 0x0, 0x1, 0x8000000000000001, 0x7FEFFFFFFFFFFFFF],
+}
+
+NONFINITE_CASES = [
+    # name, B, T, C, D, k, dtype, reads (each case lands on a different output loop of the fast kernel)
+    ("bf16_d64_k8", 2, 600, 3, 64, 8, torch.bfloat16, False),
+    ("f16_d16_k4", 2, 500, 3, 16, 4, torch.float16, False),
+    ("f32_d64_k4", 2, 400, 2, 64, 4, torch.float32, False),
+    ("f32_d32_k4", 2, 400, 2, 32, 4, torch.float32, False),
+    ("f64_d32_k4", 1, 300, 2, 32, 4, torch.float64, False),
+    ("bf16_d24_k16", 1, 700, 2, 24, 16, torch.bfloat16, False),
+    ("bf16_d64_k8_general", 2, 500, 3, 64, 8, torch.bfloat16, True),
+]
+
+
+@pytest.mark.parametrize("case", NONFINITE_CASES, ids=[c[0] for c in NONFINITE_CASES])
+def test_latestk_nonfinite_payload_bits(oracle_mod, case):
+    """Invalid slots hold candidate * 0: +-0 for finite candidates (sign kept) and the canonical
+    quiet NaN for Inf/NaN; valid slots copy the candidate's bits, NaN payloads included."""
+    from ravel_lm_b200 import causal_last_k_lookup
+    name, B, T, C, D, k, dt, reads = case
+    gen = torch.Generator().manual_seed(zlib.crc32(name.encode()))
+    A = 37
+    w = torch.randint(0, A, (B, T, C), generator=gen)
+    r = torch.randint(0, A, (B, T, C), generator=gen) if reads else None
+    p = torch.randn(B, T, C, D, generator=gen).to(dt)
+    ibits = {2: torch.int16, 4: torch.int32, 8: torch.int64}[p.element_size()]
+    bits = p.view(ibits)
+    width = 8 * p.element_size()
+    signed = [v - 2 ** width if v >= 2 ** (width - 1) else v for v in SPECIAL_BITS[dt]]
+    special = torch.tensor(signed, dtype=ibits)
+    pick = torch.rand(bits.shape, generator=gen) < 0.15
+    choice = special[torch.randint(0, len(special), bits.shape, generator=gen)]
+    bits[pick] = choice[pick]
+    vals, mask = causal_last_k_lookup(w.cuda(), p.cuda(), None if r is None else r.cuda(), address_space=A, k=k)
+    torch.cuda.synchronize()
+    code = {torch.bfloat16: "bf16", torch.float16: "f16"}.get(dt)
+    ov, om, _, _ = oracle_mod.latestk_fwd(w.numpy(), payload_np(p), None if r is None else r.numpy(),
+                                          address_space=A, k=k, dtype=code)
+    assert np.array_equal(mask.cpu().numpy(), om), "latest-k mask"
+    assert_bits_equal(vals, ov.view({2: np.uint16, 4: np.uint32, 8: np.uint64}[ov.dtype.itemsize]), name)
+    assert (~om).any() and om.any(), "the case must hold both valid and invalid slots"
