@@ -811,29 +811,71 @@ __global__ void __launch_bounds__(GS_WARPS * 32) k_group_prep(GsArgs a) {
     const int64_t s = g / a.R, r = g - s * a.R;
     const int64_t n_s = a.nvalid ? a.nvalid[s] : a.T;
     const ScanKeys<KeyT> kk{static_cast<const KeyT*>(a.keys) + s * a.T, n_s, a.reverse, a.tbits};
+    // One round of key loads for the whole geometry: window 0 at the nominal lower
+    // boundary xl, window 1 at the nominal upper boundary xh, windows 2..9 the 256
+    // scan indices below the largest possible hi.  Lane l of window w holds the key
+    // of scan index base[w] + l; the key before it comes from lane l-1 (lane 0
+    // loads its own).  All loads are issued before the first ballot.
+    constexpr int NWIN = 10;
+    const int64_t xl = r * a.RL, xh = (r + 1) * a.RL;
+    const int64_t emax = xh + 32 < n_s ? xh + 32 : n_s;
+    int64_t base[NWIN];
+    base[0] = xl;
+    base[1] = xh;
+#pragma unroll
+    for (int w = 2; w < NWIN; ++w) base[w] = emax - 32 * (w - 1);
+    KeyT kv[NWIN], kb[NWIN];
+#pragma unroll
+    for (int w = 0; w < NWIN; ++w) {
+        const int64_t si = base[w] + lane;
+        kv[w] = (si >= 0 && si < n_s) ? kk.at(si) : KeyT(0);
+        kb[w] = (lane == 0 && si > 0 && si - 1 < n_s) ? kk.at(si - 1) : KeyT(0);
+    }
+    unsigned bits[NWIN];  // bit l: scan index base[w] + l (< n_s) begins a segment
+#pragma unroll
+    for (int w = 0; w < NWIN; ++w) {
+        const int64_t si = base[w] + lane;
+        KeyT kp = __shfl_up_sync(0xffffffffu, kv[w], 1);
+        if (lane == 0) kp = kb[w];
+        bits[w] = __ballot_sync(0xffffffffu, si >= 0 && si < n_s && (si == 0 || ((kv[w] ^ kp) >> a.tbits) != 0));
+    }
     // boundary at nominal scan index x: the first segment start in [x, x + snap), else x
-    auto snap = [&](int64_t x) -> int64_t {
+    const unsigned smask = a.snap >= 32 ? 0xffffffffu : ((1u << a.snap) - 1u);
+    auto snap = [&](int64_t x, unsigned win) -> int64_t {
         if (x >= n_s) return n_s;
         if (x == 0) return 0;
-        const int64_t si = x + lane;
-        const unsigned m = __ballot_sync(0xffffffffu, lane < a.snap && si < n_s && kk.start(si));
+        const unsigned m = win & smask;
         return m ? x + __ffs(m) - 1 : x;
     };
-    const int64_t lo = snap(r * a.RL);
-    const int64_t hi = snap((r + 1) * a.RL);
+    const int64_t lo = snap(xl, bits[0]);
+    const int64_t hi = snap(xh, bits[1]);
+    const bool hi_start = hi < n_s && hi - xh < 32 && ((bits[1] >> (hi - xh)) & 1u);
+    const bool hi_open = hi < n_s && lo < hi && !hi_start;
+    // last segment start in [lo, hi): the search windows first, further down only
+    // when the range reaches below them
+    auto keep = [&](unsigned v, int64_t x) -> unsigned {  // bits of [lo, hi) within [x, x + 32)
+        const int64_t b0 = lo - x, b1 = hi - x;
+        if (b0 > 0) v = b0 >= 32 ? 0u : v & ~((1u << b0) - 1u);
+        if (b1 < 32) v = b1 <= 0 ? 0u : v & ((1u << b1) - 1u);
+        return v;
+    };
     int64_t ls = -1;
-    for (int64_t e0 = hi; e0 > lo && ls < 0; e0 -= 128) {  // last segment start in [lo, hi), 128 keys a round
+#pragma unroll
+    for (int w = 2; w < NWIN; ++w) {
+        const unsigned v = keep(bits[w], base[w]);
+        if (ls < 0 && v != 0u) ls = base[w] + 31 - __clz(v);
+    }
+    for (int64_t e0 = emax - 32 * (NWIN - 2); e0 > lo && ls < 0; e0 -= 128) {
         unsigned m[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             const int64_t si = e0 - 1 - 32 * q - lane;
-            m[q] = __ballot_sync(0xffffffffu, si >= lo && kk.start(si));
+            m[q] = __ballot_sync(0xffffffffu, si >= lo && si < hi && kk.start(si));
         }
 #pragma unroll
         for (int q = 0; q < 4; ++q)
             if (ls < 0 && m[q] != 0u) ls = e0 - 32 * q - __ffs(m[q]);
     }
-    const bool hi_open = hi < n_s && lo < hi && !kk.start(hi);
     const int64_t rot = ls >= 0 ? ls : lo;
     if (lane == 0) {
         int32_t* bounds = a.bounds + s * (a.R + 1);
@@ -865,24 +907,33 @@ __global__ void __launch_bounds__(GS_WARPS * 32) k_group_prep(GsArgs a) {
 #pragma unroll
         for (int q = 0; q < 8; ++q) rw[q] = row_of(c0 + 32 * q + lane);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const int64_t cnt = n - c0 - 32 * q;  // rows left from this chunk on
-            if (cnt <= 0) break;
+        for (int q = 0; q < 8; q += 2) {  // two chunks of row loads in flight
+            const int64_t cnt0 = n - c0 - 32 * q;  // rows left from chunk q on
+            if (cnt0 <= 0) break;
+            const int64_t cnt1 = cnt0 - 32;
 #pragma unroll 8
             for (uint32_t u = 0; u < L; ++u) {
                 const uint32_t j = u * G + grp;
-                const uint32_t row = __shfl_sync(0xffffffffu, rw[q], static_cast<int>(j));
-                if (static_cast<int64_t>(j) < cnt) {
+                const uint32_t row0 = __shfl_sync(0xffffffffu, rw[q], static_cast<int>(j));
+                const uint32_t row1 = __shfl_sync(0xffffffffu, rw[q + 1], static_cast<int>(j));
+                uint4 w0[VPL], w1[VPL];
 #pragma unroll
-                    for (int v = 0; v < VPL; ++v) {
-                        const uint4 w = ld_nc_v4(in + row * rb + v * L * 16u);
-                        RawWords<16> x;
-                        x.w[0] = w.x; x.w[1] = w.y; x.w[2] = w.z; x.w[3] = w.w;
-                        Acc f[EL];
-                        unpack<InT, Acc, EL>(x, f);
+                for (int v = 0; v < VPL; ++v) {
+                    w0[v] = static_cast<int64_t>(j) < cnt0 ? ld_nc_v4(in + row0 * rb + v * L * 16u)
+                                                           : make_uint4(0u, 0u, 0u, 0u);
+                    w1[v] = static_cast<int64_t>(j) < cnt1 ? ld_nc_v4(in + row1 * rb + v * L * 16u)
+                                                           : make_uint4(0u, 0u, 0u, 0u);
+                }
 #pragma unroll
-                        for (int e = 0; e < EL; ++e) acc[v * EL + e] += f[e];
-                    }
+                for (int v = 0; v < VPL; ++v) {
+                    RawWords<16> x0, x1;
+                    x0.w[0] = w0[v].x; x0.w[1] = w0[v].y; x0.w[2] = w0[v].z; x0.w[3] = w0[v].w;
+                    x1.w[0] = w1[v].x; x1.w[1] = w1[v].y; x1.w[2] = w1[v].z; x1.w[3] = w1[v].w;
+                    Acc f0[EL], f1[EL];
+                    unpack<InT, Acc, EL>(x0, f0);
+                    unpack<InT, Acc, EL>(x1, f1);
+#pragma unroll
+                    for (int e = 0; e < EL; ++e) acc[v * EL + e] += f0[e] + f1[e];
                 }
             }
         }
