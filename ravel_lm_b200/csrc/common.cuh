@@ -166,6 +166,15 @@ template <> struct Elem<RAVEL_F64> {
 
 inline int elem_bytes(int dt) { return dt == RAVEL_F32 ? 4 : (dt == RAVEL_F64 ? 8 : 2); }
 
+// Two packed 16-bit elements (low half first) to floats.
+template <typename V> __device__ __forceinline__ float2 pair_to_float2(uint32_t w);
+template <> __device__ __forceinline__ float2 pair_to_float2<__nv_bfloat16>(uint32_t w) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+}
+template <> __device__ __forceinline__ float2 pair_to_float2<__half>(uint32_t w) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+
 // candidate * 0 on raw bits (ravel_memory.py:175, :280): a finite value keeps only
 // its sign bit (+-0); Inf/NaN become the dtype's canonical quiet NaN.
 template <int DT> __device__ __forceinline__ uint32_t zero_word(uint32_t w);

@@ -338,7 +338,7 @@ __global__ void __launch_bounds__(256) k_lk_fwd_general(LkArgs a, int64_t reads_
 // atomicAdd of grad_vals into an accumulator [N, D] (float, or double for
 // float64); the accumulator is the output itself for float32 / float64.
 template <typename KeyT, int DT>
-__global__ void __launch_bounds__(256) k_lk_bwd_general(LkArgs a, int64_t reads_per_cta) {
+__global__ void __launch_bounds__(256) k_lk_bwd_general(LkArgs a, int64_t reads_per_cta, int vshift) {
     using E = Elem<DT>;
     using Acc = typename E::Acc;
     using V = typename E::T;
@@ -358,6 +358,24 @@ __global__ void __launch_bounds__(256) k_lk_bwd_general(LkArgs a, int64_t reads_
     const V* g = static_cast<const V*>(a.grad) + r0 * k * D;
     Acc* acc = static_cast<Acc*>(a.out);
     const bool vec4 = (DT == RAVEL_F32) && (D % 4 == 0);
+    if constexpr (sizeof(V) == 2) {
+        if (vshift >= 0) {
+            // 16-bit payloads: one 16-byte gradient load and two float4 atomics per 8 elements
+            const uint32_t cmask = (1u << vshift) - 1u;
+            for (uint32_t e = threadIdx.x; e < (static_cast<uint32_t>(ns) << vshift); e += 256) {
+                const uint32_t sl = e >> vshift, c = e & cmask;
+                const int64_t row = srow[sl];
+                if (row < 0) continue;
+                const uint4 w = ld_nc_v4(g + static_cast<int64_t>(sl) * D + c * 8);
+                const float2 p0 = pair_to_float2<V>(w.x), p1 = pair_to_float2<V>(w.y);
+                const float2 p2 = pair_to_float2<V>(w.z), p3 = pair_to_float2<V>(w.w);
+                float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(acc) + row * D + c * 8);
+                atomicAdd(dst, make_float4(p0.x, p0.y, p1.x, p1.y));
+                atomicAdd(dst + 1, make_float4(p2.x, p2.y, p3.x, p3.y));
+            }
+            return;
+        }
+    }
     if (vec4) {
         const uint32_t d4 = static_cast<uint32_t>(D / 4);
         for (uint32_t e = threadIdx.x; e < static_cast<uint32_t>(ns) * d4; e += 256) {

@@ -80,6 +80,18 @@ SortPlan sort_plan(int64_t T) {
 
 int acc_bytes(int dtype) { return dtype == RAVEL_F64 ? 8 : 4; }
 
+// 16-bit payload rows taken as 2^v chunks of 8 elements (16 bytes): v when D/8 is a
+// power of two up to 32 and every pointer involved is 16-byte aligned, else -1.
+int vshift16(int dtype, int64_t D, uintptr_t align_bits) {
+    if (dtype != RAVEL_BF16 && dtype != RAVEL_F16) return -1;
+    if (D <= 0 || D % 8 != 0 || align_bits % 16 != 0) return -1;
+    const int64_t c = D / 8;
+    if (c > 32 || (c & (c - 1)) != 0) return -1;
+    int v = 0;
+    while ((int64_t{1} << v) < c) ++v;
+    return v;
+}
+
 struct ScanPlan {
     int P, parts, min_P;
     int64_t nchunks;      // chunks per stream of the fallback kernel
@@ -495,11 +507,12 @@ int lk_bwd(const void* tape, int flags, const void* raddr, int addr_dtype, const
     if (cudaMemsetAsync(acc, 0, acc_sz, st) != cudaSuccess) return RAVEL_ERR_CUDA;
     a.out = acc;
     const int64_t rpc = 512 / k;
+    const int vsh = vshift16(dtype, D, addr_bits(grad_vals) | addr_bits(acc));
     return with_key(tl.kl.key64, [&](auto kt) -> int {
         using KeyT = decltype(kt);
         return with_dtype(dtype, [&](auto dtc) -> int {
             constexpr int DT = decltype(dtc)::value;
-            k_lk_bwd_general<KeyT, DT><<<static_cast<unsigned>((N + rpc - 1) / rpc), 256, 0, st>>>(a, rpc);
+            k_lk_bwd_general<KeyT, DT><<<static_cast<unsigned>((N + rpc - 1) / rpc), 256, 0, st>>>(a, rpc, vsh);
             if (int e = check_launch()) return e;
             if constexpr (DT == RAVEL_BF16 || DT == RAVEL_F16) {
                 const int64_t n = N * D;
@@ -689,6 +702,7 @@ int ss_fwd_tape(const void* tape, int flags, const void* raddr, int addr_dtype, 
             g.tapebuf = tapebuf;
             g.out = out_sums;
             g.out_mask = out_mask;
+            g.vshift = vshift16(DT, D, addr_bits(out_sums) | addr_bits(tapebuf));
             k_ss_gather<KeyT, DT><<<grid_cap((N * 32 + 255) / 256), 256, 0, st>>>(g);
             return check_launch();
         });
@@ -734,6 +748,7 @@ int ss_bwd(const void* tape, int flags, const void* raddr, int addr_dtype, const
             g.fd_T = FastDiv(static_cast<uint32_t>(T));
             g.accbuf = accbuf;
             g.grad = grad_sums;
+            g.vshift = vshift16(DT, D, addr_bits(grad_sums) | addr_bits(accbuf));
             k_ss_scatter<KeyT, DT><<<grid_cap((N * 32 + 255) / 256), 256, 0, st>>>(g);
             if (int e = check_launch()) return e;
             return launch_segscan<KeyT, DT>(tv, tl, B, T, C, D, accbuf, 1, grad_payload, 0, nullptr, 1, 1,

@@ -1157,7 +1157,22 @@ struct SsGenArgs {
     void* out;             // forward: sums [N, D]
     uint8_t* out_mask;     // forward: [N]
     FastDiv fd_C, fd_T;    // flat row -> (b, t, c)
+    int vshift;            // 16-bit payloads: log2(D/8) when rows split into 2^vshift 8-element
+                           // chunks (D/8 a power of two <= 32, 16-byte aligned), else -1
 };
+
+// 8 floats <-> 8 elements of a 16-bit payload type packed in a uint4.
+template <typename V>
+__device__ __forceinline__ void unpack8(const uint4& w, float (&f)[8]) {
+    RawWords<16> x;
+    x.w[0] = w.x; x.w[1] = w.y; x.w[2] = w.z; x.w[3] = w.w;
+    unpack<V, float, 8>(x, f);
+}
+template <typename V>
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+    const RawWords<16> x = pack<V, float, 8>(f);
+    return make_uint4(x.w[0], x.w[1], x.w[2], x.w[3]);
+}
 
 template <typename KeyT>
 __device__ __forceinline__ bool ss_valid(const SsGenArgs& a, int64_t r, int64_t& tape_index) {
@@ -1184,6 +1199,31 @@ __global__ void __launch_bounds__(256) k_ss_gather(SsGenArgs a) {
     const int lane = threadIdx.x & 31;
     const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+    if constexpr (sizeof(V) == 2) {
+        if (a.vshift >= 0) {  // 2^vshift lanes per read, 8 elements (16 bytes out) per lane
+            const int sh = a.vshift;
+            const int sub = lane >> sh, c = lane & ((1 << sh) - 1);
+            const int64_t per = 32 >> sh;
+            for (int64_t r0 = warp0 * per; r0 < N; r0 += nwarps * per) {
+                const int64_t r = r0 + sub;
+                if (r >= N) continue;
+                int64_t ti = 0;
+                const bool valid = ss_valid<KeyT>(a, r, ti);
+                float f[8];
+                if (valid) {
+                    const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(a.tapebuf) + ti * D + c * 8);
+                    const float4 u0 = src[0], u1 = src[1];
+                    f[0] = u0.x; f[1] = u0.y; f[2] = u0.z; f[3] = u0.w; f[4] = u1.x; f[5] = u1.y; f[6] = u1.z; f[7] = u1.w;
+                } else {
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) f[q] = 0.f;
+                }
+                *reinterpret_cast<uint4*>(static_cast<V*>(a.out) + r * D + c * 8) = pack8<V>(f);
+                if (c == 0) a.out_mask[r] = valid ? 1 : 0;
+            }
+            return;
+        }
+    }
     for (int64_t r = warp0; r < N; r += nwarps) {
         int64_t ti = 0;
         const bool valid = ss_valid<KeyT>(a, r, ti);
@@ -1204,6 +1244,25 @@ __global__ void __launch_bounds__(256) k_ss_scatter(SsGenArgs a) {
     const int lane = threadIdx.x & 31;
     const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+    if constexpr (sizeof(V) == 2) {
+        if (a.vshift >= 0) {  // 2^vshift lanes per read: a 16-byte gradient load, two float4 atomics
+            const int sh = a.vshift;
+            const int sub = lane >> sh, c = lane & ((1 << sh) - 1);
+            const int64_t per = 32 >> sh;
+            for (int64_t r0 = warp0 * per; r0 < N; r0 += nwarps * per) {
+                const int64_t r = r0 + sub;
+                if (r >= N) continue;
+                int64_t ti = 0;
+                if (!ss_valid<KeyT>(a, r, ti)) continue;
+                float f[8];
+                unpack8<V>(ld_nc_v4(static_cast<const V*>(a.grad) + r * D + c * 8), f);
+                float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.accbuf) + ti * D + c * 8);
+                atomicAdd(dst, make_float4(f[0], f[1], f[2], f[3]));
+                atomicAdd(dst + 1, make_float4(f[4], f[5], f[6], f[7]));
+            }
+            return;
+        }
+    }
     for (int64_t r = warp0; r < N; r += nwarps) {
         int64_t ti = 0;
         if (!ss_valid<KeyT>(a, r, ti)) continue;

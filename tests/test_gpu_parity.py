@@ -120,6 +120,8 @@ CASES = [
     ("d256_bf16_el8", 1, 3000, 2, 256, 90, 2, torch.bfloat16, False, False, "uniform"),
     ("d128_f32_el4", 1, 2500, 2, 128, 40, 2, torch.float32, True, False, "uniform"),
     ("d48_f64_el2", 1, 1700, 2, 48, 30, 2, torch.float64, False, True, "uniform"),
+    ("general_bf16_d64_vec", 2, 3000, 4, 64, 500, 4, torch.bfloat16, True, True, "zipf1.05"),
+    ("general_f16_d32_vec", 2, 2000, 3, 32, 300, 3, torch.float16, True, False, "uniform"),
 ]
 
 
