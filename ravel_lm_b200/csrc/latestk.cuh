@@ -395,6 +395,91 @@ __global__ void __launch_bounds__(256) k_lk_bwd_general(LkArgs a, int64_t reads_
     }
 }
 
+// General latest-k backward as a gather (no atomics, deterministic): the gradient
+// of the write at sorted position q of stream s is the sum, over slots j < k whose
+// write q+j lies in q's segment, of grad_vals[r, j] over the reads r whose latest
+// valid write is q+j (bucket q+j of the read tape).  Every write row is stored
+// once, zeros for masked writes.  A group of 2^lshift lanes takes one write, a
+// lane one VB-byte vector of the row (row_bytes / VB = 2^lshift).
+template <typename KeyT, typename RKeyT, int DT, int VB>
+__global__ void __launch_bounds__(256) k_lk_bwd_gather(LkArgs a, const RKeyT* rkeys, const int32_t* bstart,
+                                                       int lshift) {
+    using E = Elem<DT>;
+    using Acc = typename E::Acc;
+    using V = typename E::T;
+    constexpr int EPV = VB / static_cast<int>(sizeof(V));
+    const int lane = threadIdx.x & 31;
+    const uint32_t L = 1u << lshift;
+    const uint32_t grp = static_cast<uint32_t>(lane) >> lshift, lig = static_cast<uint32_t>(lane) & (L - 1);
+    const int64_t gpw = 32 >> lshift;
+    const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+    const int64_t T = a.T, S = a.B * a.C, D = a.D;
+    const int k = static_cast<int>(a.k);
+    const KeyT tmask = (static_cast<KeyT>(1) << a.tbits) - 1;
+    const RKeyT rtmask = (static_cast<RKeyT>(1) << a.tbits) - 1;
+    const V* grad = static_cast<const V*>(a.grad);
+    V* out = static_cast<V*>(a.out);
+    for (int64_t gi = warp0 * gpw + grp; gi < S * T; gi += nwarps * gpw) {
+        const int64_t s = gi / T, q = gi - s * T;
+        const int64_t n_s = a.nvalid ? a.nvalid[s] : T;
+        const KeyT* wk = static_cast<const KeyT*>(a.keys) + s * T;
+        const KeyT kq = wk[q];
+        const RowMap rows_of(s, T, a.C);
+        Acc acc[EPV];
+#pragma unroll
+        for (int e = 0; e < EPV; ++e) acc[e] = Acc(0);
+        if (q < n_s) {
+            // slots j < jmax keep write q+j in q's segment: k write keys loaded 8 at a
+            // time, independently
+            const KeyT aq = kq >> a.tbits;
+            int jmax = 0;
+            for (int j0 = 0; j0 < k && jmax == j0; j0 += 8) {
+                bool m[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int64_t qq = q + j0 + u;
+                    m[u] = j0 + u < k && qq < n_s && (wk[qq < n_s ? qq : q] >> a.tbits) == aq;
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    if (jmax == j0 + u && m[u]) ++jmax;
+            }
+            // the reads of buckets q .. q+jmax-1 are one contiguous run of the read
+            // tape; a read's slot is its latest valid write minus q
+            const int32_t* bs = bstart + s * (T + 2);
+            const RKeyT* rk = rkeys + s * T;
+            const int32_t i0 = bs[q + 1], i1 = bs[q + 1 + jmax];
+            for (int32_t i = i0; i < i1; i += 4) {
+                uint32_t rrow[4];
+                int jj[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const RKeyT key = i + u < i1 ? rk[i + u] : RKeyT(0);
+                    rrow[u] = rows_of(key & rtmask);
+                    jj[u] = static_cast<int>(static_cast<int64_t>(key >> a.tbits) - 1 - q);
+                }
+                uint4 x[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    x[u] = i + u < i1 ? ldg_vec<VB>(grad + (static_cast<uint64_t>(rrow[u]) * k + jj[u]) * D + lig * EPV)
+                                      : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const V* xv = reinterpret_cast<const V*>(&x[u]);
+#pragma unroll
+                    for (int e = 0; e < EPV; ++e) acc[e] += E::to_acc(xv[e]);
+                }
+            }
+        }
+        uint4 o = make_uint4(0u, 0u, 0u, 0u);
+        V* ov = reinterpret_cast<V*>(&o);
+#pragma unroll
+        for (int e = 0; e < EPV; ++e) ov[e] = E::from_acc(acc[e]);
+        st_vec<VB>(out + static_cast<uint64_t>(rows_of(kq & tmask)) * D + lig * EPV, o);
+    }
+}
+
 // Convert a float accumulator [n] to the payload dtype.
 template <int DT>
 __global__ void k_acc_to_dtype(const float* __restrict__ acc, typename Elem<DT>::T* __restrict__ out, int64_t n) {

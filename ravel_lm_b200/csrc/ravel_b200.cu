@@ -23,7 +23,10 @@ struct TapeLayout {
     int general;            // reads use the search path
     int has_mask;
     size_t key_bytes;
-    size_t off_keys, off_nvalid, off_soff, off_ridx, total;
+    int rbits;              // read tape: bits of (latest valid write + 1), 0..T
+    int rkey64;             // read-tape keys are 64-bit
+    size_t rkey_bytes;
+    size_t off_keys, off_nvalid, off_soff, off_ridx, off_rkeys, off_bstart, total;
 };
 
 TapeLayout tape_layout(int64_t B, int64_t T, int64_t C, int64_t A, int flags) {
@@ -37,7 +40,13 @@ TapeLayout tape_layout(int64_t B, int64_t T, int64_t C, int64_t A, int flags) {
     t.off_nvalid = align_up(S * static_cast<size_t>(T) * t.key_bytes);
     t.off_soff = t.off_nvalid + align_up(S * 4);
     t.off_ridx = t.off_soff + align_up((S + 1) * 8);
-    t.total = t.off_ridx + (t.general ? align_up(N * 4) : 0);
+    t.rbits = 0;
+    while ((int64_t{1} << t.rbits) <= T) ++t.rbits;
+    t.rkey64 = (t.kl.tbits + t.rbits > 32) ? 1 : 0;
+    t.rkey_bytes = t.rkey64 ? 8 : 4;
+    t.off_rkeys = t.off_ridx + (t.general ? align_up(N * 4) : 0);
+    t.off_bstart = t.off_rkeys + (t.general ? align_up(S * static_cast<size_t>(T) * t.rkey_bytes) : 0);
+    t.total = t.off_bstart + (t.general ? align_up(S * static_cast<size_t>(T + 2) * 4) : 0);
     return t;
 }
 
@@ -46,6 +55,8 @@ struct TapeView {
     int* nvalid;       // null unless a mask is present
     int64_t* soff;
     int32_t* ridx;
+    void* rkeys;       // general tapes: [S][T] reads sorted by (latest valid write + 1, t)
+    int32_t* bstart;   // general tapes: [S][T+2] start of each value of that field in rkeys
 };
 
 TapeView tape_view(const void* tape, const TapeLayout& t) {
@@ -55,6 +66,8 @@ TapeView tape_view(const void* tape, const TapeLayout& t) {
     v.nvalid = t.has_mask ? reinterpret_cast<int*>(base + t.off_nvalid) : nullptr;
     v.soff = reinterpret_cast<int64_t*>(base + t.off_soff);
     v.ridx = t.general ? reinterpret_cast<int32_t*>(base + t.off_ridx) : nullptr;
+    v.rkeys = t.general ? static_cast<void*>(base + t.off_rkeys) : nullptr;
+    v.bstart = t.general ? reinterpret_cast<int32_t*>(base + t.off_bstart) : nullptr;
     return v;
 }
 
@@ -178,7 +191,8 @@ ScratchLayout scratch_layout(int64_t B, int64_t T, int64_t C, int64_t D, int64_t
     const size_t nch = S * static_cast<size_t>(sc.max_nchunks);
     const size_t ab = static_cast<size_t>(acc_bytes(dtype));
     l.off_sort = 0;
-    l.off_flags = align_up(sp.tiles > 1 ? S * static_cast<size_t>(T) * t.key_bytes : 0);
+    const size_t sort_key_bytes = (t.general && t.rkey_bytes > t.key_bytes) ? t.rkey_bytes : t.key_bytes;
+    l.off_flags = align_up(sp.tiles > 1 ? S * static_cast<size_t>(T) * sort_key_bytes : 0);
     l.off_ticket = l.off_flags + align_up(nch * 4);
     l.off_agg = l.off_ticket + 256;
     l.off_incl = l.off_agg + align_up(nch * static_cast<size_t>(D) * ab);
@@ -269,6 +283,69 @@ int key32_of(int64_t B, int64_t T, int64_t C, int64_t A) {
 }
 
 // ------------------------------------------------------------------ tape build
+// Sort every stream's events (the keys sort_key builds) into `out`: one cluster
+// per stream for 2-8 tiles, else tiles sorted in shared memory and merged
+// through `other` (ping-pong, S*T keys).
+template <typename KeyT>
+int sort_streams(const SortArgs& a0, void* out, void* other, int64_t S, int64_t T, cudaStream_t st) {
+    const SortPlan sp = sort_plan(T);
+    SortArgs a = a0;
+    a.tiles = sp.tiles;
+    if (sp.tiles > 1 && sp.tiles <= 8) {
+        // one cluster of `tiles` CTAs per stream, straight into `out`
+        const size_t smem = cluster_sort_smem<1024, 8, KeyT>();
+        if (set_smem(k_cluster_sort<KeyT, 1024, 8>, smem) == RAVEL_OK) {
+            SortArgs ca = a;
+            ca.keys_out = out;
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(static_cast<unsigned>(S * sp.tiles));
+            cfg.blockDim = dim3(1024);
+            cfg.dynamicSmemBytes = smem;
+            cfg.stream = st;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = static_cast<unsigned>(sp.tiles);
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            if (cudaLaunchKernelEx(&cfg, k_cluster_sort<KeyT, 1024, 8>, ca) == cudaSuccess) return check_launch();
+            (void)cudaGetLastError();  // not schedulable here: use tiles + merges
+        }
+    }
+    void* first = (sp.merge_passes % 2 == 0) ? out : other;
+    a.keys_out = first;
+    const int64_t grid = S * sp.tiles;
+    auto launch = [&](auto th) -> int {
+        constexpr int TH = decltype(th)::value;
+        const size_t smem = tile_sort_smem<TH, 8, KeyT>();
+        if (int e = set_smem(k_tile_sort<KeyT, TH, 8>, smem)) return e;
+        k_tile_sort<KeyT, TH, 8><<<static_cast<unsigned>(grid), TH, smem, st>>>(a);
+        return check_launch();
+    };
+    int e = RAVEL_OK;
+    switch (sp.threads) {
+        case 32: e = launch(IC<32>{}); break;
+        case 64: e = launch(IC<64>{}); break;
+        case 128: e = launch(IC<128>{}); break;
+        case 256: e = launch(IC<256>{}); break;
+        case 512: e = launch(IC<512>{}); break;
+        default: e = launch(IC<1024>{}); break;
+    }
+    if (e) return e;
+    const KeyT* src = static_cast<const KeyT*>(first);
+    int64_t run = static_cast<int64_t>(sp.threads) * 8;
+    const int64_t cps = (T + MERGE_OUT - 1) / MERGE_OUT;
+    for (int pass = 0; pass < sp.merge_passes; ++pass) {
+        KeyT* dst = (src == static_cast<const KeyT*>(out)) ? static_cast<KeyT*>(other) : static_cast<KeyT*>(out);
+        k_merge<KeyT><<<static_cast<unsigned>(S * cps), MERGE_THREADS, 0, st>>>(src, dst, T, run, cps);
+        if (int e2 = check_launch()) return e2;
+        src = dst;
+        run *= 2;
+    }
+    return RAVEL_OK;
+}
+
 int tape_build(const void* waddr, const void* raddr, int addr_dtype, const uint8_t* wmask, int64_t B,
                int64_t T, int64_t C, int64_t A, int flags, void* tape, size_t tape_bytes, void* scratch,
                size_t scratch_bytes, cudaStream_t st) {
@@ -296,70 +373,13 @@ int tape_build(const void* waddr, const void* raddr, int addr_dtype, const uint8
     a.tbits = tl.kl.tbits; a.abits = tl.kl.abits; a.mbit = tl.kl.mbit;
     a.tiles = sp.tiles;
     a.nvalid = tv.nvalid;
+    a.ridx = nullptr;
+    a.wkeys = nullptr;
+    a.wkey64 = 0;
     void* other = static_cast<char*>(scratch) + sl.off_sort;
-    void* first = (sp.merge_passes % 2 == 0) ? tv.keys : other;
-    a.keys_out = first;
-    const int64_t grid = B * sp.tiles * C;
-
     int rc = with_key(tl.kl.key64, [&](auto kt) -> int {
         using KeyT = decltype(kt);
-        bool sorted = false;
-        if (sp.tiles > 1 && sp.tiles <= 8) {
-            // one cluster of `tiles` CTAs per stream, straight into the tape
-            const size_t smem = cluster_sort_smem<1024, 8, KeyT>();
-            if (set_smem(k_cluster_sort<KeyT, 1024, 8>, smem) == RAVEL_OK) {
-                SortArgs ca = a;
-                ca.keys_out = tv.keys;
-                cudaLaunchConfig_t cfg = {};
-                cfg.gridDim = dim3(static_cast<unsigned>(S * sp.tiles));
-                cfg.blockDim = dim3(1024);
-                cfg.dynamicSmemBytes = smem;
-                cfg.stream = st;
-                cudaLaunchAttribute attr[1];
-                attr[0].id = cudaLaunchAttributeClusterDimension;
-                attr[0].val.clusterDim.x = static_cast<unsigned>(sp.tiles);
-                attr[0].val.clusterDim.y = 1;
-                attr[0].val.clusterDim.z = 1;
-                cfg.attrs = attr;
-                cfg.numAttrs = 1;
-                if (cudaLaunchKernelEx(&cfg, k_cluster_sort<KeyT, 1024, 8>, ca) == cudaSuccess) {
-                    if (int e = check_launch()) return e;
-                    sorted = true;
-                } else {
-                    (void)cudaGetLastError();  // not schedulable here: use tiles + merges
-                }
-            }
-        }
-        auto launch = [&](auto th) -> int {
-            constexpr int TH = decltype(th)::value;
-            const size_t smem = tile_sort_smem<TH, 8, KeyT>();
-            if (int e = set_smem(k_tile_sort<KeyT, TH, 8>, smem)) return e;
-            k_tile_sort<KeyT, TH, 8><<<static_cast<unsigned>(grid), TH, smem, st>>>(a);
-            return check_launch();
-        };
-        int e = RAVEL_OK;
-        if (!sorted) {
-            switch (sp.threads) {
-                case 32: e = launch(IC<32>{}); break;
-                case 64: e = launch(IC<64>{}); break;
-                case 128: e = launch(IC<128>{}); break;
-                case 256: e = launch(IC<256>{}); break;
-                case 512: e = launch(IC<512>{}); break;
-                default: e = launch(IC<1024>{}); break;
-            }
-        }
-        if (e) return e;
-        const KeyT* src = static_cast<const KeyT*>(first);
-        int64_t run = static_cast<int64_t>(sp.threads) * 8;
-        const int64_t cps = (T + MERGE_OUT - 1) / MERGE_OUT;
-        for (int pass = 0; pass < (sorted ? 0 : sp.merge_passes); ++pass) {
-            KeyT* dst = (src == static_cast<const KeyT*>(tv.keys)) ? static_cast<KeyT*>(other)
-                                                                  : static_cast<KeyT*>(tv.keys);
-            k_merge<KeyT><<<static_cast<unsigned>(S * cps), MERGE_THREADS, 0, st>>>(src, dst, T, run, cps);
-            if (int e2 = check_launch()) return e2;
-            src = dst;
-            run *= 2;
-        }
+        if (int e = sort_streams<KeyT>(a, tv.keys, other, S, T, st)) return e;
         if (tl.general) {
             k_stream_offsets<<<1, 1024, 0, st>>>(tv.nvalid, tv.soff, S, T);
             if (int e2 = check_launch()) return e2;
@@ -376,6 +396,24 @@ int tape_build(const void* waddr, const void* raddr, int addr_dtype, const uint8
             q.fd_T = FastDiv(static_cast<uint32_t>(T));
             k_read_search<KeyT><<<grid_cap((N + 255) / 256), 256, 0, st>>>(q);
             if (int e2 = check_launch()) return e2;
+            // read tape: every stream's reads by (latest valid write + 1, t), and where
+            // each value of that field starts
+            SortArgs ra = a;
+            ra.waddr = q.raddr;
+            ra.wmask = nullptr;
+            ra.nvalid = nullptr;
+            ra.abits = tl.rbits;
+            ra.mbit = 0;
+            ra.ridx = tv.ridx;
+            ra.wkeys = tv.keys;
+            ra.wkey64 = tl.kl.key64;
+            return with_key(tl.rkey64, [&](auto rkt) -> int {
+                using RKeyT = decltype(rkt);
+                if (int e3 = sort_streams<RKeyT>(ra, tv.rkeys, other, S, T, st)) return e3;
+                k_bucket_starts<RKeyT><<<grid_cap((S * (T + 1) + 255) / 256), 256, 0, st>>>(
+                    static_cast<const RKeyT*>(tv.rkeys), S, T, tl.kl.tbits, tv.bstart);
+                return check_launch();
+            });
         }
         return RAVEL_OK;
     });
@@ -495,7 +533,38 @@ int lk_bwd(const void* tape, int flags, const void* raddr, int addr_dtype, const
             });
         });
     }
-    // general: atomics into an accumulator
+    // general: a gather over the read tape when a row splits into 2^m <= 32
+    // vectors, one lane each; otherwise atomics into an accumulator
+    {
+        const int gvb = pick_vec_bytes(a.row_bytes, addr_bits(grad_vals) | addr_bits(grad_payload));
+        const int64_t grv = a.row_bytes / gvb;
+        if (grv >= 1 && grv <= 32 && (grv & (grv - 1)) == 0) {
+            int lsh = 0;
+            while ((int64_t{1} << lsh) < grv) ++lsh;
+            a.out = grad_payload;
+            const int64_t groups = B * C * T;
+            const int64_t warps = (groups + (32 >> lsh) - 1) / (32 >> lsh);
+            return with_key(tl.kl.key64, [&](auto kt) -> int {
+                using KeyT = decltype(kt);
+                return with_key(tl.rkey64, [&](auto rkt) -> int {
+                    using RKeyT = decltype(rkt);
+                    return with_dtype(dtype, [&](auto dtc) -> int {
+                        constexpr int DT = decltype(dtc)::value;
+                        return with_vb(gvb, [&](auto vbc) -> int {
+                            constexpr int VB = decltype(vbc)::value;
+                            if constexpr (!vb_ok<DT, VB>()) {
+                                return RAVEL_ERR_INVALID_ARG;
+                            } else {
+                                k_lk_bwd_gather<KeyT, RKeyT, DT, VB><<<grid_cap((warps * 32 + 255) / 256), 256, 0, st>>>(
+                                    a, static_cast<const RKeyT*>(tv.rkeys), tv.bstart, lsh);
+                                return check_launch();
+                            }
+                        });
+                    });
+                });
+            });
+        }
+    }
     const ScratchLayout sl = scratch_layout(B, T, C, D, A, dtype, flags);
     const bool direct = dtype == RAVEL_F32 || dtype == RAVEL_F64;
     void* acc = grad_payload;
@@ -732,10 +801,36 @@ int ss_bwd(const void* tape, int flags, const void* raddr, int addr_dtype, const
             }
             void* accbuf = static_cast<char*>(scratch) + sl.off_big;
             const size_t acc_sz = static_cast<size_t>(B * C * T) * D * acc_bytes(DT);
-            if (cudaMemsetAsync(accbuf, 0, acc_sz, st) != cudaSuccess) return RAVEL_ERR_CUDA;
             if (tl.has_mask &&
                 cudaMemsetAsync(grad_payload, 0, static_cast<size_t>(N) * D * elem_bytes(DT), st) != cudaSuccess)
                 return RAVEL_ERR_CUDA;
+            // read gradients gathered at their latest write over the read tape when a
+            // row splits into 2^m <= 32 vectors; otherwise atomics
+            const int gvb = pick_vec_bytes(D * elem_bytes(DT), addr_bits(grad_sums));
+            const int64_t grv = D * elem_bytes(DT) / gvb;
+            if (grv >= 1 && grv <= 32 && (grv & (grv - 1)) == 0) {
+                int lsh = 0;
+                while ((int64_t{1} << lsh) < grv) ++lsh;
+                const int64_t warps = (B * C * T + (32 >> lsh) - 1) / (32 >> lsh);
+                int e = with_key(tl.rkey64, [&](auto rkt) -> int {
+                    using RKeyT = decltype(rkt);
+                    return with_vb(gvb, [&](auto vbc) -> int {
+                        constexpr int VB = decltype(vbc)::value;
+                        if constexpr (!vb_ok<DT, VB>()) {
+                            return RAVEL_ERR_INVALID_ARG;
+                        } else {
+                            k_ss_bwd_gather<RKeyT, DT, VB><<<grid_cap((warps * 32 + 255) / 256), 256, 0, st>>>(
+                                static_cast<const RKeyT*>(tv.rkeys), tv.bstart, tv.nvalid, grad_sums, accbuf, B * C, T,
+                                C, D, tl.kl.tbits, lsh);
+                            return check_launch();
+                        }
+                    });
+                });
+                if (e) return e;
+                return launch_segscan<KeyT, DT>(tv, tl, B, T, C, D, accbuf, 1, grad_payload, 0, nullptr, 1, 1,
+                                                scratch, sl, st);
+            }
+            if (cudaMemsetAsync(accbuf, 0, acc_sz, st) != cudaSuccess) return RAVEL_ERR_CUDA;
             SsGenArgs g;
             std::memset(&g, 0, sizeof(g));
             g.keys = tv.keys; g.soff = tv.soff; g.ridx = tv.ridx;

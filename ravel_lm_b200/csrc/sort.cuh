@@ -35,7 +35,42 @@ struct SortArgs {
     int64_t tiles;         // tiles per stream
     void* keys_out;        // [S][T]
     int* nvalid;           // [S], pre-zeroed, or null when there is no mask
+    // read tape: when ridx is set, the sort orders each stream's READS by
+    // (latest valid earlier write + 1, t) instead of its writes by (address, t);
+    // waddr then holds the read addresses and wkeys the sorted write keys
+    const int32_t* ridx;   // [N] latest earlier write of every read (any address), -1 if none
+    const void* wkeys;     // [S][T] sorted write keys
+    int wkey64;            // write keys are 64-bit
 };
+
+// Sort key of event (b, c, t) (stream s = b*C + c).  Writes: (invalid bit | folded
+// address) above t; a masked write sorts after every valid one.  Reads (read
+// tape): 1 + the index of the latest earlier write when that write has the
+// read's address, else 0 (the read sees no write), above t.
+template <typename KeyT>
+__device__ __forceinline__ KeyT sort_key(const SortArgs& a, int64_t b, int64_t c, int64_t s, int64_t t,
+                                         int& nvalid_local) {
+    const int64_t row = (b * a.T + t) * a.C + c;
+    if (a.ridx != nullptr) {
+        const int32_t q = a.ridx[row];
+        uint64_t v = 0;
+        if (q >= 0) {
+            const uint64_t ra = fold_addr(load_addr(a.waddr, row, a.addr_i64), a.A, a.key32);
+            const uint64_t wa = a.wkey64 ? (static_cast<const uint64_t*>(a.wkeys)[s * a.T + q] >> a.tbits)
+                                         : (static_cast<const uint32_t*>(a.wkeys)[s * a.T + q] >> a.tbits);
+            if (wa == ra) v = static_cast<uint64_t>(q) + 1;
+        }
+        return (static_cast<KeyT>(v) << a.tbits) | static_cast<KeyT>(t);
+    }
+    const uint64_t ad = fold_addr(load_addr(a.waddr, row, a.addr_i64), a.A, a.key32);
+    const bool valid = a.wmask == nullptr || a.wmask[b * a.T + t] != 0;
+    if (valid) {
+        ++nvalid_local;
+        return (static_cast<KeyT>(ad) << a.tbits) | static_cast<KeyT>(t);
+    }
+    // masked write: invalid bit above the address field, sorts last
+    return (static_cast<KeyT>(1) << (a.tbits + a.abits)) | static_cast<KeyT>(t);
+}
 
 template <typename KeyT, int THREADS, int ITEMS>
 __global__ void __launch_bounds__(THREADS) k_tile_sort(SortArgs a) {
@@ -62,20 +97,8 @@ __global__ void __launch_bounds__(THREADS) k_tile_sort(SortArgs a) {
     int nvalid_local = 0;
     for (int i = tid; i < TILE; i += THREADS) {
         const int64_t t = t0 + i;
-        KeyT key;
-        if (t < T) {
-            const uint64_t ad = fold_addr(load_addr(a.waddr, (b * T + t) * C + c, a.addr_i64), a.A, a.key32);
-            const bool valid = a.wmask == nullptr || a.wmask[b * T + t] != 0;
-            if (valid) {
-                key = (static_cast<KeyT>(ad) << a.tbits) | static_cast<KeyT>(t);
-                ++nvalid_local;
-            } else {
-                // masked write: invalid bit above the address field, sorts last
-                key = (static_cast<KeyT>(1) << (a.tbits + a.abits)) | static_cast<KeyT>(t);
-            }
-        } else {
-            key = ~static_cast<KeyT>(0);  // tile padding: sorts after everything
-        }
+        // tile padding sorts after everything
+        const KeyT key = t < T ? sort_key<KeyT>(a, b, c, s, t, nvalid_local) : ~static_cast<KeyT>(0);
         ka[i] = key;
     }
     if (a.nvalid != nullptr) {
@@ -183,19 +206,7 @@ __global__ void __launch_bounds__(THREADS) k_cluster_sort(SortArgs a) {
     int nvalid_local = 0;
     for (int i = tid; i < TILE; i += THREADS) {
         const int64_t t = t0 + i;
-        KeyT key;
-        if (t < T) {
-            const uint64_t ad = fold_addr(load_addr(a.waddr, (b * T + t) * C + c, a.addr_i64), a.A, a.key32);
-            const bool valid = a.wmask == nullptr || a.wmask[b * T + t] != 0;
-            if (valid) {
-                key = (static_cast<KeyT>(ad) << a.tbits) | static_cast<KeyT>(t);
-                ++nvalid_local;
-            } else {
-                key = (static_cast<KeyT>(1) << (a.tbits + a.abits)) | static_cast<KeyT>(t);
-            }
-        } else {
-            key = ~static_cast<KeyT>(0);
-        }
+        const KeyT key = t < T ? sort_key<KeyT>(a, b, c, s, t, nvalid_local) : ~static_cast<KeyT>(0);
         ka[i] = key;
     }
     if (a.nvalid != nullptr) {
@@ -426,6 +437,24 @@ __global__ void __launch_bounds__(256) k_read_search(SearchArgs a) {
             if (k[mid] < q) lo = mid + 1; else hi = mid;
         }
         a.ridx[r] = static_cast<int32_t>(lo - 1);
+    }
+}
+
+// Read tape bucket starts: bstart[s][j] = the number of stream s's sorted reads
+// whose field (key >> tbits, = latest valid write + 1) is below j, j = 0..T+1.
+// The reads whose latest valid write is q are rkeys[s][bstart[q+1] .. bstart[q+2]).
+// Thread (s, i) fills the starts between sorted reads i-1 and i (i = T: the end),
+// so every entry is written once.
+template <typename KeyT>
+__global__ void __launch_bounds__(256) k_bucket_starts(const KeyT* rkeys, int64_t S, int64_t T, int tbits,
+                                                      int32_t* bstart) {
+    for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < S * (T + 1);
+         e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t s = e / (T + 1), i = e - s * (T + 1);
+        const KeyT* k = rkeys + s * T;
+        const int64_t lo = i > 0 ? static_cast<int64_t>(k[i - 1] >> tbits) + 1 : 0;
+        const int64_t hi = i < T ? static_cast<int64_t>(k[i] >> tbits) : T + 1;
+        for (int64_t j = lo; j <= hi; ++j) bstart[s * (T + 2) + j] = static_cast<int32_t>(i);
     }
 }
 
