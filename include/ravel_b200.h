@@ -168,6 +168,22 @@ int ravel_cache_step(void* values, uint8_t* filled, const void* raddr, const voi
                      int64_t A, int64_t D, void* out_vals, uint8_t* out_mask, void* stream);
 
 /*
+ * Bulk prefill of the decode cache.  Replaces the token-by-token prefill of
+ * ravel_lm/model.py:600-602, whose memory layers write the cache once per
+ * position (RavelMemoryLayer.step, :424, i.e. RavelLayerCache.write,
+ * ravel_lm/ravel_memory.py:283-292).  The result equals ravel_cache_write of
+ * (addr[:, t], payload[:, t]) for t = 0 .. T-1 in order: for every (b, c) and
+ * clamped address, the latest t that writes it wins and its filled flag is set;
+ * entries no position writes keep their contents.  addr [B, T, C], payload
+ * [B, T, C, D] in the cache's dtype.  One per-stream sort plus one copy kernel;
+ * scratch of ravel_cache_prefill_scratch_bytes(B, T, C, A) bytes holds the sort.
+ */
+size_t ravel_cache_prefill_scratch_bytes(int64_t B, int64_t T, int64_t C, int64_t A);
+int ravel_cache_prefill(void* values, uint8_t* filled, const void* addr, int addr_dtype,
+                        const void* payload, int dtype, int64_t B, int64_t T, int64_t C, int64_t A,
+                        int64_t D, void* scratch, size_t scratch_bytes, void* stream);
+
+/*
  * causal_sum_lookup forward for callers that cannot allocate device memory.
  * No counterpart in the reference: it exists for hosts that may not call
  * cudaMalloc or a caching allocator on this path -- plugin interfaces whose

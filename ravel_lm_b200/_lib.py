@@ -57,6 +57,9 @@ SIGNATURES = {
     "ravel_cache_write": (_c_int, [_c_vp, _c_vp, _c_vp, _c_int, _c_vp, _c_int] + [_c_i64] * 4 + [_c_vp]),
     "ravel_cache_step": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_vp, _c_int] + [_c_i64] * 4 +
                          [_c_vp, _c_vp, _c_vp]),
+    "ravel_cache_prefill_scratch_bytes": (ctypes.c_size_t, [_c_i64] * 4),
+    "ravel_cache_prefill": (_c_int, [_c_vp, _c_vp, _c_vp, _c_int, _c_vp, _c_int] + [_c_i64] * 5 +
+                            [_c_vp, ctypes.c_size_t, _c_vp]),
     "ravel_device_error": (_c_int, [ctypes.POINTER(_c_int), _c_vp]),
     "ravel_clear_device_error": (_c_int, [_c_vp]),
     "ravel_kernel_launches": (ctypes.c_uint64, []),

@@ -69,4 +69,29 @@ __global__ void __launch_bounds__(256) k_cache_step(CacheArgs a) {
     }
 }
 
+// Bulk prefill: every stream's writes are sorted by (clamped address, t); the
+// last write of each address segment is the one a token-by-token prefill leaves
+// in the cache.  One thread per sorted position copies that write's payload row
+// into values[b, c, address] (VB bytes at a time) and sets filled.  Each cache
+// entry has at most one writer, so there are no races.
+template <typename KeyT, int VB>
+__global__ void __launch_bounds__(256) k_cache_prefill(const KeyT* keys, int64_t S, int64_t T, int64_t C, int64_t A,
+                                                       int tbits, const void* payload, int64_t row_bytes,
+                                                       void* values, uint8_t* filled) {
+    const KeyT tmask = (static_cast<KeyT>(1) << tbits) - 1;
+    for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < S * T;
+         e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t s = e / T, p = e - s * T;
+        const KeyT key = keys[e];
+        if (p + 1 < T && (keys[e + 1] >> tbits) == (key >> tbits)) continue;  // a later write of this address
+        const int64_t b = s / C, c = s - b * C;
+        const int64_t t = static_cast<int64_t>(key & tmask);
+        const int64_t addr = static_cast<int64_t>(key >> tbits);
+        const char* src = static_cast<const char*>(payload) + ((b * T + t) * C + c) * row_bytes;
+        char* dst = static_cast<char*>(values) + (s * A + addr) * row_bytes;
+        for (int64_t o = 0; o < row_bytes; o += VB) st_vec<VB>(dst + o, ldg_vec<VB>(src + o));
+        filled[s * A + addr] = 1;
+    }
+}
+
 }  // namespace ravel

@@ -376,6 +376,7 @@ int tape_build(const void* waddr, const void* raddr, int addr_dtype, const uint8
     a.ridx = nullptr;
     a.wkeys = nullptr;
     a.wkey64 = 0;
+    a.clamp = 0;
     void* other = static_cast<char*>(scratch) + sl.off_sort;
     int rc = with_key(tl.kl.key64, [&](auto kt) -> int {
         using KeyT = decltype(kt);
@@ -853,6 +854,59 @@ int ss_bwd(const void* tape, int flags, const void* raddr, int addr_dtype, const
 }
 
 // ------------------------------------------------------------------ decode cache
+// ------------------------------------------------------------------ decode cache bulk prefill
+struct PrefillLayout {
+    KeyLayout kl;
+    size_t key_bytes, off_keys, off_other, total;
+};
+
+PrefillLayout prefill_layout(int64_t B, int64_t T, int64_t C, int64_t A) {
+    PrefillLayout l;
+    l.kl = key_layout(T, A, 0);
+    l.key_bytes = l.kl.key64 ? 8 : 4;
+    const size_t n = static_cast<size_t>(B * C) * static_cast<size_t>(T) * l.key_bytes;
+    l.off_keys = 0;
+    l.off_other = align_up(n);
+    l.total = l.off_other + (sort_plan(T).tiles > 1 ? align_up(n) : 0);
+    return l;
+}
+
+int cache_prefill(void* values, uint8_t* filled, const void* addr, int addr_dtype, const void* payload, int dtype,
+                  int64_t B, int64_t T, int64_t C, int64_t A, int64_t D, void* scratch, size_t scratch_bytes,
+                  cudaStream_t st) {
+    if (int e = check_sizes(B, T, C, D, A)) return e;
+    if (addr_dtype != RAVEL_I32 && addr_dtype != RAVEL_I64) return RAVEL_ERR_INVALID_ARG;
+    if (dtype < 0 || dtype > 3) return RAVEL_ERR_INVALID_ARG;
+    const int64_t S = B * C;
+    if (S * T == 0) return RAVEL_OK;
+    if (values == nullptr || filled == nullptr || addr == nullptr || (D > 0 && payload == nullptr))
+        return RAVEL_ERR_INVALID_ARG;
+    const PrefillLayout pl = prefill_layout(B, T, C, A);
+    if (scratch == nullptr || scratch_bytes < pl.total) return RAVEL_ERR_WORKSPACE;
+    char* sc = static_cast<char*>(scratch);
+    SortArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.waddr = addr;
+    a.addr_i64 = addr_dtype == RAVEL_I64;
+    a.key32 = 0;
+    a.B = B; a.T = T; a.C = C; a.A = A;
+    a.tbits = pl.kl.tbits; a.abits = pl.kl.abits; a.mbit = 0;
+    a.clamp = 1;
+    const int64_t row_bytes = D * elem_bytes(dtype);
+    const int vb = row_bytes > 0 ? pick_vec_bytes(row_bytes, addr_bits(values) | addr_bits(payload)) : 2;
+    return with_key(pl.kl.key64, [&](auto kt) -> int {
+        using KeyT = decltype(kt);
+        if (int e = sort_streams<KeyT>(a, sc + pl.off_keys, sc + pl.off_other, S, T, st)) return e;
+        return with_vb(vb, [&](auto vbc) -> int {
+            constexpr int VB = decltype(vbc)::value;
+            k_cache_prefill<KeyT, VB><<<grid_cap((S * T + 255) / 256), 256, 0, st>>>(
+                reinterpret_cast<const KeyT*>(sc + pl.off_keys), S, T, C, A, pl.kl.tbits, payload, row_bytes, values,
+                filled);
+            return check_launch();
+        });
+    });
+}
+
 int cache_op(void* values, uint8_t* filled, const void* raddr, const void* waddr, int addr_dtype,
              const void* payload, int dtype, int64_t B, int64_t C, int64_t A, int64_t D, void* out_vals,
              uint8_t* out_mask, cudaStream_t st) {
@@ -1042,6 +1096,18 @@ int ravel_cache_step(void* values, uint8_t* filled, const void* raddr, const voi
     if (raddr == nullptr || waddr == nullptr) return RAVEL_ERR_INVALID_ARG;
     return cache_op(values, filled, raddr, waddr, addr_dtype, payload, dtype, B, C, A, D, out_vals, out_mask,
                     static_cast<cudaStream_t>(stream));
+}
+
+size_t ravel_cache_prefill_scratch_bytes(int64_t B, int64_t T, int64_t C, int64_t A) {
+    if (B < 0 || T < 0 || C < 0 || A <= 0) return 0;
+    return prefill_layout(B, T, C, A).total;
+}
+
+int ravel_cache_prefill(void* values, uint8_t* filled, const void* addr, int addr_dtype, const void* payload,
+                        int dtype, int64_t B, int64_t T, int64_t C, int64_t A, int64_t D, void* scratch,
+                        size_t scratch_bytes, void* stream) {
+    return cache_prefill(values, filled, addr, addr_dtype, payload, dtype, B, T, C, A, D, scratch, scratch_bytes,
+                         static_cast<cudaStream_t>(stream));
 }
 
 int ravel_device_error(int* out, void* stream) {

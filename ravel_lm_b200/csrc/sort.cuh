@@ -41,6 +41,7 @@ struct SortArgs {
     const int32_t* ridx;   // [N] latest earlier write of every read (any address), -1 if none
     const void* wkeys;     // [S][T] sorted write keys
     int wkey64;            // write keys are 64-bit
+    int clamp;             // addresses clamped to [0, A-1] (decode cache) instead of wrapped
 };
 
 // Sort key of event (b, c, t) (stream s = b*C + c).  Writes: (invalid bit | folded
@@ -62,7 +63,8 @@ __device__ __forceinline__ KeyT sort_key(const SortArgs& a, int64_t b, int64_t c
         }
         return (static_cast<KeyT>(v) << a.tbits) | static_cast<KeyT>(t);
     }
-    const uint64_t ad = fold_addr(load_addr(a.waddr, row, a.addr_i64), a.A, a.key32);
+    const int64_t raw = load_addr(a.waddr, row, a.addr_i64);
+    const uint64_t ad = a.clamp ? static_cast<uint64_t>(clamp_addr(raw, a.A)) : fold_addr(raw, a.A, a.key32);
     const bool valid = a.wmask == nullptr || a.wmask[b * a.T + t] != 0;
     if (valid) {
         ++nvalid_local;

@@ -485,6 +485,35 @@ class RavelLayerCache:
         _lib.call("ravel_cache_write", self.values.data_ptr(), self.filled.data_ptr(), a.data_ptr(), code,
                   p.data_ptr(), _payload_code(self.values), B, C, self.values.shape[2], D, _stream(device))
 
+    def prefill(self, write_addresses: Tensor, payloads: Tensor) -> None:
+        """All writes of a prefill at once: the cache state left by ``write(write_addresses[:, t],
+        payloads[:, t])`` for t = 0 .. T-1 in order.  addresses [B, T, C], payloads [B, T, C, D].
+
+        The reference prefills token by token (ravel_lm/model.py:600-602), one ``write`` per position
+        and layer; this sorts each stream's writes once and copies the last write of every address.
+        """
+        if write_addresses.dim() != 3:
+            raise ValueError("write_addresses must have shape [B, T, C]")
+        B, T, C = write_addresses.shape
+        D = payloads.shape[-1]
+        if self.values.shape[:2] != (B, C) or self.values.shape[-1] != D:
+            raise ValueError("cache and payload shapes do not match")
+        if payloads.shape[:3] != (B, T, C):
+            raise ValueError("cache and payload shapes do not match")
+        device = _require_cuda(self.values, self.filled, write_addresses, payloads)
+        self._check_storage()
+        if B * T * C == 0:
+            return
+        A = self.values.shape[2]
+        a, code = _addr(write_addresses)
+        p = payloads.to(self.values.dtype).contiguous()
+        lib = _lib.load()
+        scratch = torch.empty(int(lib.ravel_cache_prefill_scratch_bytes(B, T, C, A)), dtype=torch.uint8,
+                              device=device)
+        _lib.call("ravel_cache_prefill", self.values.data_ptr(), self.filled.data_ptr(), a.data_ptr(), code,
+                  p.data_ptr(), _payload_code(self.values), B, T, C, A, D, scratch.data_ptr(), scratch.numel(),
+                  _stream(device))
+
     def step(self, read_addresses: Tensor, write_addresses: Tensor, payloads: Tensor) -> Tuple[Tensor, Tensor]:
         """``read(read_addresses)`` then ``write(write_addresses, payloads)`` in one launch."""
         B, C = read_addresses.shape

@@ -117,3 +117,58 @@ def test_decode_cuda_graph_replay():
         assert torch.equal(v1, v2) and torch.equal(m1, m2)
     assert torch.equal(eager.values, graphed.values)
     del graph
+
+
+PREFILL_CASES = [
+    # name, B, T, C, A, D, dtype, address dtype, address range (lo, hi)
+    ("bf16_clamped", 3, 500, 4, 64, 16, torch.bfloat16, torch.int64, (-8, 72)),
+    ("f32_one_tile", 2, 4096, 3, 4096, 8, torch.float32, torch.int32, (0, 4096)),
+    ("f16_cluster", 1, 20000, 2, 300, 24, torch.float16, torch.int64, (-5, 310)),
+    ("f64_merge", 1, 70000, 2, 1000, 4, torch.float64, torch.int64, (0, 1000)),
+    ("bf16_hot", 2, 9000, 2, 5, 64, torch.bfloat16, torch.int64, (0, 5)),
+]
+
+
+@pytest.mark.parametrize("case", PREFILL_CASES, ids=[c[0] for c in PREFILL_CASES])
+def test_bulk_prefill_equals_token_by_token_writes(oracle_mod, case):
+    """RavelLayerCache.prefill leaves the state of T sequential writes (ravel_lm/model.py:600-602 prefill),
+    bit for bit, on a cache that already holds data; checked against the oracle on the smallest case."""
+    from ravel_lm_b200 import RavelLayerCache
+    name, B, T, C, A, D, dtype, adt, (lo, hi) = case
+    g = torch.Generator().manual_seed(len(name) * 1009 + T)
+    addr = torch.randint(lo, hi, (B, T, C), generator=g).to(adt)
+    pay = torch.randn(B, T, C, D, generator=g).to(dtype)
+    prior_v = torch.randn(B, C, A, D, generator=g).to(dtype)
+    prior_f = torch.rand(B, C, A, generator=g) < 0.3
+    bulk = RavelLayerCache(prior_v.clone().cuda(), prior_f.clone().cuda())
+    bulk.prefill(addr.cuda(), pay.cuda())
+    seq = RavelLayerCache(prior_v.clone().cuda(), prior_f.clone().cuda())
+    ad, pd = addr.cuda(), pay.cuda()
+    for t in range(T):
+        seq.write(ad[:, t], pd[:, t])
+    torch.cuda.synchronize()
+    assert torch.equal(bulk.filled, seq.filled), name
+    assert torch.equal(bulk.values.view(torch.uint8), seq.values.view(torch.uint8)), name
+    if B * T * C <= 6000:
+        vals_np = prior_v.double().numpy().copy()
+        filled_np = prior_f.numpy().copy()
+        for t in range(T):
+            oracle_mod.cache_write(vals_np, filled_np, addr[:, t].numpy(), pay[:, t].double().numpy())
+        assert np.array_equal(bulk.filled.cpu().numpy(), filled_np)
+        assert np.array_equal(bulk.values.double().cpu().numpy(), vals_np)
+
+
+def test_bulk_prefill_then_decode_matches_latest1():
+    """Prefill in bulk, then decode step by step: every read equals latest-1 over the whole tape."""
+    from ravel_lm_b200 import RavelLayerCache, causal_last_k_lookup
+    g = torch.Generator().manual_seed(21)
+    B, T0, T1, C, A, D = 4, 700, 60, 3, 40, 32
+    addr = torch.randint(0, A, (B, T0 + T1, C), generator=g).cuda()
+    pay = torch.randn(B, T0 + T1, C, D, generator=g).to(torch.bfloat16).cuda()
+    vals, mask = causal_last_k_lookup(addr, pay, address_space=A, k=1)
+    cache = RavelLayerCache.empty(B, C, A, D, device="cuda", dtype=torch.bfloat16)
+    cache.prefill(addr[:, :T0], pay[:, :T0])
+    for t in range(T0, T0 + T1):
+        v, m = cache.step(addr[:, t], addr[:, t], pay[:, t])
+        assert torch.equal(m, mask[:, t, :, 0])
+        assert torch.equal(v, vals[:, t, :, 0])

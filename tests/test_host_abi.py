@@ -96,6 +96,12 @@ def test_cache_validation_and_no_cpu_path():
         c.write(torch.zeros(2, 3, dtype=torch.long), torch.zeros(2, 3, 5))
     with pytest.raises(RuntimeError, match="CUDA tensors only"):
         c.read(torch.zeros(2, 3, dtype=torch.long))
+    with pytest.raises(ValueError, match="shape"):
+        c.prefill(torch.zeros(2, 3, dtype=torch.long), torch.zeros(2, 3, 4))
+    with pytest.raises(ValueError, match="do not match"):
+        c.prefill(torch.zeros(2, 5, 3, dtype=torch.long), torch.zeros(2, 4, 3, 4))
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        c.prefill(torch.zeros(2, 5, 3, dtype=torch.long), torch.zeros(2, 5, 3, 4))
 
 
 def test_composite_key_dtype_matches_reference_golden():
