@@ -299,3 +299,55 @@ def test_latestk_nonfinite_payload_bits(oracle_mod, case):
     assert np.array_equal(mask.cpu().numpy(), om), "latest-k mask"
     assert_bits_equal(vals, ov.view({2: np.uint16, 4: np.uint32, 8: np.uint64}[ov.dtype.itemsize]), name)
     assert (~om).any() and om.any(), "the case must hold both valid and invalid slots"
+
+
+@pytest.mark.parametrize("general", [False, True], ids=["aliased", "general_mask"])
+def test_training_step_captured_in_cuda_graph(general):
+    """Forward and backward of both lookups captured once in a CUDA graph, then replayed on new
+    inputs copied into the captured buffers: bit-identical to the eager step on those inputs."""
+    from ravel_lm_b200 import causal_last_k_lookup, causal_sum_lookup
+    g = torch.Generator().manual_seed(33 + int(general))
+    B, T, C, D, A, k = 2, 2048, 4, 32, 300, 3
+
+    def fresh():
+        w = torch.randint(0, A, (B, T, C), generator=g)
+        r = torch.randint(0, A, (B, T, C), generator=g) if general else None
+        m = (torch.rand(B, T, generator=g) < 0.8) if general else None
+        p = torch.randn(B, T, C, D, generator=g).to(torch.bfloat16)
+        gv = torch.randn(B, T, C, k, D, generator=g).to(torch.bfloat16)
+        gs = torch.randn(B, T, C, D, generator=g).to(torch.bfloat16)
+        return [w, r, m, p, gv, gs]
+
+    def step(w, r, m, p, gv, gs):
+        vals, vm = causal_last_k_lookup(w, p, r, address_space=A, k=k, write_mask=m)
+        sums, sm = causal_sum_lookup(w, p, r, address_space=A, write_mask=m)
+        (gp,) = torch.autograd.grad([vals, sums], [p], [gv, gs])
+        return vals, vm, sums, sm, gp
+
+    static = [None if t is None else t.cuda() for t in fresh()]
+    static[3].requires_grad_(True)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            step(*static)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        captured = step(*static)
+    for _ in range(2):
+        new = fresh()
+        with torch.no_grad():
+            for dst, src in zip(static, new):
+                if dst is not None:
+                    dst.copy_(src.cuda())
+        graph.replay()
+        torch.cuda.synchronize()
+        eager_in = [None if t is None else t.cuda() for t in new]
+        eager_in[3].requires_grad_(True)
+        eager = step(*eager_in)
+        torch.cuda.synchronize()
+        for name, a, b in zip(("values", "mask", "sums", "sum mask", "payload grad"), captured, eager):
+            assert torch.equal(a.view(torch.uint8) if a.dtype != torch.bool else a,
+                               b.view(torch.uint8) if b.dtype != torch.bool else b), name
+    del graph
