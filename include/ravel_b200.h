@@ -86,7 +86,9 @@ int ravel_tape_build(const void* waddr, const void* raddr, int addr_dtype, const
  * Latest-k gather from a built tape: values[b,t,c,j] = payload of the j-th
  * latest write with the same (b, c, address) strictly before t, else
  * candidate*0; mask = validity.  Replaces ravel_lm/ravel_memory.py:160-176.
- * raddr is needed only for general reads (NULL otherwise).
+ * raddr is needed whenever tape_flags is nonzero (reads that differ from the
+ * writes, or a write mask): the read addresses, or the write addresses when
+ * reads alias writes.  With tape_flags == 0 it may be NULL.
  */
 int ravel_latestk_fwd_tape(const void* tape, int tape_flags, const void* raddr, int addr_dtype,
                            const void* payload, int dtype, int64_t B, int64_t T, int64_t C,

@@ -313,22 +313,6 @@ __device__ __forceinline__ RawWords<EL * sizeof(X)> ld_frag(const X* p) {
     return r;
 }
 
-template <typename X, int EL>
-__device__ __forceinline__ RawWords<EL * sizeof(X)> ld_frag_smem(const X* p) {
-    RawWords<EL * sizeof(X)> r;
-    constexpr int B = EL * sizeof(X);
-    if constexpr (B == 2) r.w[0] = *reinterpret_cast<const uint16_t*>(p);
-    else if constexpr (B == 4) r.w[0] = *reinterpret_cast<const uint32_t*>(p);
-    else if constexpr (B == 8) { const uint2 v = *reinterpret_cast<const uint2*>(p); r.w[0] = v.x; r.w[1] = v.y; }
-    else {
-#pragma unroll
-        for (int q = 0; q < B / 16; ++q) {
-            const uint4 v = *reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(p) + 16 * q);
-            r.w[4 * q] = v.x; r.w[4 * q + 1] = v.y; r.w[4 * q + 2] = v.z; r.w[4 * q + 3] = v.w;
-        }
-    }
-    return r;
-}
 
 template <typename X, int EL>
 __device__ __forceinline__ void st_frag(X* p, const RawWords<EL * sizeof(X)>& r) {
@@ -606,36 +590,9 @@ __global__ void __launch_bounds__(SCANW_WARPS * 32) k_segscan_w(ScanArgs<typenam
     }
 }
 
-template <typename X, int EL>
-__device__ __forceinline__ void st_frag_smem(X* p, const RawWords<EL * sizeof(X)>& r) {
-    constexpr int B = EL * sizeof(X);
-    if constexpr (B == 2) *reinterpret_cast<uint16_t*>(p) = static_cast<uint16_t>(r.w[0]);
-    else if constexpr (B == 4) *reinterpret_cast<uint32_t*>(p) = r.w[0];
-    else if constexpr (B == 8) *reinterpret_cast<uint2*>(p) = make_uint2(r.w[0], r.w[1]);
-    else {
-#pragma unroll
-        for (int q = 0; q < B / 16; ++q)
-            *reinterpret_cast<uint4*>(reinterpret_cast<char*>(p) + 16 * q) =
-                make_uint4(r.w[4 * q], r.w[4 * q + 1], r.w[4 * q + 2], r.w[4 * q + 3]);
-    }
-}
 
 // Copy staged result rows [r0, r1) of the chunk to their output rows, 16 bytes
 // per lane (rows are whole multiples of 16 bytes).
-template <typename AccT, typename X>
-__device__ __forceinline__ void store_rows(const ScanArgs<AccT>& a, const X* rows, const uint32_t* s_out, int r0,
-                                           int r1, uint32_t rb, X* out, int lane) {
-    const uint32_t vpr = rb / 16;
-    const uint32_t n = static_cast<uint32_t>(r1 > r0 ? r1 - r0 : 0) * vpr;
-    for (uint32_t e = lane; e < n; e += 32) {
-        uint32_t r, v;
-        a.fd_vpr.divmod(e, r, v);
-        const uint4 val = *reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(rows) +
-                                                          static_cast<size_t>(r0 + r) * rb + v * 16);
-        *reinterpret_cast<uint4*>(reinterpret_cast<char*>(out) + static_cast<uint64_t>(s_out[r0 + r]) * rb + v * 16) =
-            val;
-    }
-}
 
 // ------------------------------------------------------------------ lane fragments in shared memory
 // 32-bit shared-memory addressing and paired 16-bit conversions for the scan's
@@ -661,23 +618,6 @@ __device__ __forceinline__ RawWords<B> lds_words(uint32_t addr) {
     return r;
 }
 
-template <int B>
-__device__ __forceinline__ void sts_words(uint32_t addr, const RawWords<B>& r) {
-    if constexpr (B == 2) {
-        const unsigned short h = static_cast<unsigned short>(r.w[0]);
-        asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"(h) : "memory");
-    } else if constexpr (B == 4) {
-        asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(r.w[0]) : "memory");
-    } else if constexpr (B == 8) {
-        asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(addr), "r"(r.w[0]), "r"(r.w[1]) : "memory");
-    } else {
-#pragma unroll
-        for (int q = 0; q < B / 16; ++q)
-            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr + 16 * q), "r"(r.w[4 * q]),
-                         "r"(r.w[4 * q + 1]), "r"(r.w[4 * q + 2]), "r"(r.w[4 * q + 3])
-                         : "memory");
-    }
-}
 
 // Unpack EL elements of X held in raw words into accumulators.
 template <typename X, typename Acc, int EL>
