@@ -619,7 +619,7 @@ int launch_segscan(const TapeView& tv, const TapeLayout& tl, int64_t B, int64_t 
     a.fd_d = FastDiv(static_cast<uint32_t>(D > 0 ? D : 1));
     using V = typename Elem<DT>::T;
     const size_t in_es = in_sorted ? sizeof(Acc) : sizeof(V);
-    const size_t out_es = out_sorted ? sizeof(Acc) : sizeof(V);
+    const size_t out_es = sizeof(V);  // sorted outputs are stored in the payload dtype too
     // group scan: rows of 16-byte vectors, 1..32 lanes per row (2 vectors per lane up to 1 KB rows)
     const int64_t nvec = (D * static_cast<int64_t>(in_es)) % 16 == 0 ? D * static_cast<int64_t>(in_es) / 16 : 0;
     int vpl = 0, lshift = 0;

@@ -41,7 +41,7 @@ struct ScanArgs {
     int64_t B, T, C, D;
     int tbits;
     const void* in;          // in_sorted ? Acc [S*T, D] : dtype [N, D]
-    void* out;               // out_sorted ? Acc [S*T, D] : dtype [N, D]
+    void* out;               // dtype: [S*T, D] by tape index when out_sorted, else [N, D] by flat row
     uint8_t* out_mask;       // optional [N]: 1 unless the position starts its segment
     int in_sorted, out_sorted, inclusive, reverse;
     int P;                   // positions per chunk
@@ -241,11 +241,11 @@ __global__ void __launch_bounds__(SCAN_THREADS) k_segscan(ScanArgs<typename Elem
 
     // write out
     if (a.out_sorted) {
-        Acc* out = static_cast<Acc*>(a.out) + s * T * D;
+        V* out = static_cast<V*>(a.out) + s * T * D;
         for (uint32_t e = tid; e < static_cast<uint32_t>(np * D); e += SCAN_THREADS) {
             uint32_t i, d;
             a.fd_d.divmod(e, i, d);
-            out[(srow[i] & 0xffffffffll) * D + d] = rows[e];
+            out[(srow[i] & 0xffffffffll) * D + d] = E::from_acc(rows[e]);
         }
     } else {
         V* out = static_cast<V*>(a.out);
@@ -407,7 +407,7 @@ __global__ void __launch_bounds__(SCANW_WARPS * 32) k_segscan_w(ScanArgs<typenam
     using Acc = typename E::Acc;
     using V = typename E::T;
     using InT = typename std::conditional<IN_SORTED, Acc, V>::type;
-    using OutT = typename std::conditional<OUT_SORTED, Acc, V>::type;
+    using OutT = V;  // sorted outputs too are stored in the payload dtype
     constexpr int NW = SCANW_WARPS;
     constexpr int P = NW * R;
     extern __shared__ __align__(16) unsigned char smem[];
@@ -901,7 +901,7 @@ __global__ void __launch_bounds__(GS_WARPS * 32) k_group_scan(GsArgs a) {
     using Acc = typename E::Acc;
     using V = typename E::T;
     using InT = typename std::conditional<IN_SORTED, Acc, V>::type;
-    using OutT = typename std::conditional<OUT_SORTED, Acc, V>::type;
+    using OutT = V;  // sorted outputs too are stored in the payload dtype
     constexpr int EL = 16 / static_cast<int>(sizeof(InT));
     constexpr int NE = VPL * EL;
     constexpr int SLOTS = GS_Q * GS_U;
@@ -1091,7 +1091,7 @@ struct SsGenArgs {
     int addr_i64, key32;
     int64_t B, T, C, D, A;
     int tbits;
-    const void* tapebuf;   // Acc [S*T, D] (forward: inclusive segmented sums)
+    const void* tapebuf;   // dtype [S*T, D] (forward: inclusive segmented sums, rounded once)
     void* accbuf;          // Acc [S*T, D] (backward: read gradients added at their latest write)
     const void* grad;      // backward: grad_sums [N, D]
     void* out;             // forward: sums [N, D]
@@ -1101,17 +1101,12 @@ struct SsGenArgs {
                            // chunks (D/8 a power of two <= 32, 16-byte aligned), else -1
 };
 
-// 8 floats <-> 8 elements of a 16-bit payload type packed in a uint4.
+// 8 elements of a 16-bit payload type packed in a uint4, as floats.
 template <typename V>
 __device__ __forceinline__ void unpack8(const uint4& w, float (&f)[8]) {
     RawWords<16> x;
     x.w[0] = w.x; x.w[1] = w.y; x.w[2] = w.z; x.w[3] = w.w;
     unpack<V, float, 8>(x, f);
-}
-template <typename V>
-__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
-    const RawWords<16> x = pack<V, float, 8>(f);
-    return make_uint4(x.w[0], x.w[1], x.w[2], x.w[3]);
 }
 
 template <typename KeyT>
@@ -1149,16 +1144,9 @@ __global__ void __launch_bounds__(256) k_ss_gather(SsGenArgs a) {
                 if (r >= N) continue;
                 int64_t ti = 0;
                 const bool valid = ss_valid<KeyT>(a, r, ti);
-                float f[8];
-                if (valid) {
-                    const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(a.tapebuf) + ti * D + c * 8);
-                    const float4 u0 = src[0], u1 = src[1];
-                    f[0] = u0.x; f[1] = u0.y; f[2] = u0.z; f[3] = u0.w; f[4] = u1.x; f[5] = u1.y; f[6] = u1.z; f[7] = u1.w;
-                } else {
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) f[q] = 0.f;
-                }
-                *reinterpret_cast<uint4*>(static_cast<V*>(a.out) + r * D + c * 8) = pack8<V>(f);
+                const uint4 w = valid ? ld_nc_v4(static_cast<const V*>(a.tapebuf) + ti * D + c * 8)
+                                      : make_uint4(0u, 0u, 0u, 0u);
+                *reinterpret_cast<uint4*>(static_cast<V*>(a.out) + r * D + c * 8) = w;
                 if (c == 0) a.out_mask[r] = valid ? 1 : 0;
             }
             return;
@@ -1167,9 +1155,9 @@ __global__ void __launch_bounds__(256) k_ss_gather(SsGenArgs a) {
     for (int64_t r = warp0; r < N; r += nwarps) {
         int64_t ti = 0;
         const bool valid = ss_valid<KeyT>(a, r, ti);
-        const Acc* src = static_cast<const Acc*>(a.tapebuf) + ti * D;
+        const V* src = static_cast<const V*>(a.tapebuf) + ti * D;
         V* dst = static_cast<V*>(a.out) + r * D;
-        for (int64_t d = lane; d < D; d += 32) dst[d] = E::from_acc(valid ? src[d] : Acc(0));
+        for (int64_t d = lane; d < D; d += 32) dst[d] = valid ? src[d] : E::from_acc(Acc(0));
         if (lane == 0) a.out_mask[r] = valid ? 1 : 0;
     }
 }
