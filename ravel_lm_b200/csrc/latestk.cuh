@@ -16,8 +16,9 @@
 // elements is one contiguous streaming store.
 //
 // General reads or a write mask: each read's latest index comes from
-// k_read_search; reads are processed in their original order so the output is
-// written sequentially, and candidate rows are gathered directly.
+// k_read_ranks; the forward takes reads in their original order so the output
+// is written sequentially, and gathers the candidate rows directly; the backward
+// gathers over the read tape (k_lk_bwd_gather).
 #pragma once
 
 #include "common.cuh"
@@ -397,13 +398,13 @@ __global__ void __launch_bounds__(256) k_lk_bwd_general(LkArgs a, int64_t reads_
 
 // General latest-k backward as a gather (no atomics, deterministic): the gradient
 // of the write at sorted position q of stream s is the sum, over slots j < k whose
-// write q+j lies in q's segment, of grad_vals[r, j] over the reads r whose latest
-// valid write is q+j (bucket q+j of the read tape).  Every write row is stored
+// write q+j lies in q's segment, of grad_vals[r, j] over the reads r of q's address
+// whose latest earlier write is q+j (bucket q+j of the read tape).  Every write row is stored
 // once, zeros for masked writes.  A group of 2^lshift lanes takes one write, a
 // lane one VB-byte vector of the row (row_bytes / VB = 2^lshift).
-template <typename KeyT, typename RKeyT, int DT, int VB>
-__global__ void __launch_bounds__(256) k_lk_bwd_gather(LkArgs a, const RKeyT* rkeys, const int32_t* bstart,
-                                                       int lshift) {
+template <typename KeyT, int DT, int VB>
+__global__ void __launch_bounds__(256) k_lk_bwd_gather(LkArgs a, const KeyT* rkeys, const int32_t* rridx,
+                                                       const int32_t* bstart, int lshift) {
     using E = Elem<DT>;
     using Acc = typename E::Acc;
     using V = typename E::T;
@@ -417,7 +418,6 @@ __global__ void __launch_bounds__(256) k_lk_bwd_gather(LkArgs a, const RKeyT* rk
     const int64_t T = a.T, S = a.B * a.C, D = a.D;
     const int k = static_cast<int>(a.k);
     const KeyT tmask = (static_cast<KeyT>(1) << a.tbits) - 1;
-    const RKeyT rtmask = (static_cast<RKeyT>(1) << a.tbits) - 1;
     const V* grad = static_cast<const V*>(a.grad);
     V* out = static_cast<V*>(a.out);
     for (int64_t gi = warp0 * gpw + grp; gi < S * T; gi += nwarps * gpw) {
@@ -445,25 +445,29 @@ __global__ void __launch_bounds__(256) k_lk_bwd_gather(LkArgs a, const RKeyT* rk
                 for (int u = 0; u < 8; ++u)
                     if (jmax == j0 + u && m[u]) ++jmax;
             }
-            // the reads of buckets q .. q+jmax-1 are one contiguous run of the read
-            // tape; a read's slot is its latest valid write minus q
+            // the reads whose latest write is q .. q+jmax-1 are one contiguous run of
+            // the read tape; a read of q's address takes slot (its latest write - q),
+            // reads of other addresses in the run see no write of their own address
             const int32_t* bs = bstart + s * (T + 2);
-            const RKeyT* rk = rkeys + s * T;
+            const KeyT* rk = rkeys + s * T;
+            const int32_t* rr = rridx + s * T;
             const int32_t i0 = bs[q + 1], i1 = bs[q + 1 + jmax];
             for (int32_t i = i0; i < i1; i += 4) {
                 uint32_t rrow[4];
                 int jj[4];
+                bool use[4];
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
-                    const RKeyT key = i + u < i1 ? rk[i + u] : RKeyT(0);
-                    rrow[u] = rows_of(key & rtmask);
-                    jj[u] = static_cast<int>(static_cast<int64_t>(key >> a.tbits) - 1 - q);
+                    const KeyT key = i + u < i1 ? rk[i + u] : KeyT(0);
+                    rrow[u] = rows_of(key & tmask);
+                    jj[u] = static_cast<int>((i + u < i1 ? rr[i + u] : 0) - q);
+                    use[u] = i + u < i1 && (key >> a.tbits) == aq;
                 }
                 uint4 x[4];
 #pragma unroll
                 for (int u = 0; u < 4; ++u)
-                    x[u] = i + u < i1 ? ldg_vec<VB>(grad + (static_cast<uint64_t>(rrow[u]) * k + jj[u]) * D + lig * EPV)
-                                      : make_uint4(0u, 0u, 0u, 0u);
+                    x[u] = use[u] ? ldg_vec<VB>(grad + (static_cast<uint64_t>(rrow[u]) * k + jj[u]) * D + lig * EPV)
+                                  : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const V* xv = reinterpret_cast<const V*>(&x[u]);

@@ -23,10 +23,7 @@ struct TapeLayout {
     int general;            // reads use the search path
     int has_mask;
     size_t key_bytes;
-    int rbits;              // read tape: bits of (latest valid write + 1), 0..T
-    int rkey64;             // read-tape keys are 64-bit
-    size_t rkey_bytes;
-    size_t off_keys, off_nvalid, off_soff, off_ridx, off_rkeys, off_bstart, total;
+    size_t off_keys, off_nvalid, off_soff, off_ridx, off_rkeys, off_rridx, off_bstart, total;
 };
 
 TapeLayout tape_layout(int64_t B, int64_t T, int64_t C, int64_t A, int flags) {
@@ -40,12 +37,9 @@ TapeLayout tape_layout(int64_t B, int64_t T, int64_t C, int64_t A, int flags) {
     t.off_nvalid = align_up(S * static_cast<size_t>(T) * t.key_bytes);
     t.off_soff = t.off_nvalid + align_up(S * 4);
     t.off_ridx = t.off_soff + align_up((S + 1) * 8);
-    t.rbits = 0;
-    while ((int64_t{1} << t.rbits) <= T) ++t.rbits;
-    t.rkey64 = (t.kl.tbits + t.rbits > 32) ? 1 : 0;
-    t.rkey_bytes = t.rkey64 ? 8 : 4;
     t.off_rkeys = t.off_ridx + (t.general ? align_up(N * 4) : 0);
-    t.off_bstart = t.off_rkeys + (t.general ? align_up(S * static_cast<size_t>(T) * t.rkey_bytes) : 0);
+    t.off_rridx = t.off_rkeys + (t.general ? align_up(S * static_cast<size_t>(T) * t.key_bytes) : 0);
+    t.off_bstart = t.off_rridx + (t.general ? align_up(S * static_cast<size_t>(T) * 4) : 0);
     t.total = t.off_bstart + (t.general ? align_up(S * static_cast<size_t>(T + 2) * 4) : 0);
     return t;
 }
@@ -55,8 +49,9 @@ struct TapeView {
     int* nvalid;       // null unless a mask is present
     int64_t* soff;
     int32_t* ridx;
-    void* rkeys;       // general tapes: [S][T] reads sorted by (latest valid write + 1, t)
-    int32_t* bstart;   // general tapes: [S][T+2] start of each value of that field in rkeys
+    void* rkeys;       // general tapes: [S][T] read keys sorted by (address, t), write key width
+    int32_t* rridx;    // general tapes: [S][T] latest valid write below each sorted read, -1 if none
+    int32_t* bstart;   // general tapes: [S][T+2] first sorted read of each rridx value + 1
 };
 
 TapeView tape_view(const void* tape, const TapeLayout& t) {
@@ -67,6 +62,7 @@ TapeView tape_view(const void* tape, const TapeLayout& t) {
     v.soff = reinterpret_cast<int64_t*>(base + t.off_soff);
     v.ridx = t.general ? reinterpret_cast<int32_t*>(base + t.off_ridx) : nullptr;
     v.rkeys = t.general ? static_cast<void*>(base + t.off_rkeys) : nullptr;
+    v.rridx = t.general ? reinterpret_cast<int32_t*>(base + t.off_rridx) : nullptr;
     v.bstart = t.general ? reinterpret_cast<int32_t*>(base + t.off_bstart) : nullptr;
     return v;
 }
@@ -191,8 +187,7 @@ ScratchLayout scratch_layout(int64_t B, int64_t T, int64_t C, int64_t D, int64_t
     const size_t nch = S * static_cast<size_t>(sc.max_nchunks);
     const size_t ab = static_cast<size_t>(acc_bytes(dtype));
     l.off_sort = 0;
-    const size_t sort_key_bytes = (t.general && t.rkey_bytes > t.key_bytes) ? t.rkey_bytes : t.key_bytes;
-    l.off_flags = align_up(sp.tiles > 1 ? S * static_cast<size_t>(T) * sort_key_bytes : 0);
+    l.off_flags = align_up(sp.tiles > 1 ? S * static_cast<size_t>(T) * t.key_bytes : 0);
     l.off_ticket = l.off_flags + align_up(nch * 4);
     l.off_agg = l.off_ticket + 256;
     l.off_incl = l.off_agg + align_up(nch * static_cast<size_t>(D) * ab);
@@ -373,9 +368,6 @@ int tape_build(const void* waddr, const void* raddr, int addr_dtype, const uint8
     a.tbits = tl.kl.tbits; a.abits = tl.kl.abits; a.mbit = tl.kl.mbit;
     a.tiles = sp.tiles;
     a.nvalid = tv.nvalid;
-    a.ridx = nullptr;
-    a.wkeys = nullptr;
-    a.wkey64 = 0;
     a.clamp = 0;
     void* other = static_cast<char*>(scratch) + sl.off_sort;
     int rc = with_key(tl.kl.key64, [&](auto kt) -> int {
@@ -384,37 +376,20 @@ int tape_build(const void* waddr, const void* raddr, int addr_dtype, const uint8
         if (tl.general) {
             k_stream_offsets<<<1, 1024, 0, st>>>(tv.nvalid, tv.soff, S, T);
             if (int e2 = check_launch()) return e2;
-            SearchArgs q;
-            q.keys = tv.keys;
-            q.nvalid = tv.nvalid;
-            q.raddr = (raddr != nullptr) ? raddr : waddr;
-            q.addr_i64 = a.addr_i64;
-            q.key32 = a.key32;
-            q.B = B; q.T = T; q.C = C; q.A = A;
-            q.tbits = tl.kl.tbits;
-            q.ridx = tv.ridx;
-            q.fd_C = FastDiv(static_cast<uint32_t>(C));
-            q.fd_T = FastDiv(static_cast<uint32_t>(T));
-            k_read_search<KeyT><<<grid_cap((N + 255) / 256), 256, 0, st>>>(q);
-            if (int e2 = check_launch()) return e2;
-            // read tape: every stream's reads by (latest valid write + 1, t), and where
-            // each value of that field starts
+            // read tape: the reads sorted like the writes (by address, t), then ranked
+            // against the sorted writes; the rank is each read's latest earlier write
             SortArgs ra = a;
-            ra.waddr = q.raddr;
+            ra.waddr = (raddr != nullptr) ? raddr : waddr;
             ra.wmask = nullptr;
             ra.nvalid = nullptr;
-            ra.abits = tl.rbits;
             ra.mbit = 0;
-            ra.ridx = tv.ridx;
-            ra.wkeys = tv.keys;
-            ra.wkey64 = tl.kl.key64;
-            return with_key(tl.rkey64, [&](auto rkt) -> int {
-                using RKeyT = decltype(rkt);
-                if (int e3 = sort_streams<RKeyT>(ra, tv.rkeys, other, S, T, st)) return e3;
-                k_bucket_starts<RKeyT><<<grid_cap((S * (T + 1) + 255) / 256), 256, 0, st>>>(
-                    static_cast<const RKeyT*>(tv.rkeys), S, T, tl.kl.tbits, tv.bstart);
-                return check_launch();
-            });
+            if (int e3 = sort_streams<KeyT>(ra, tv.rkeys, other, S, T, st)) return e3;
+            k_read_ranks<KeyT><<<grid_cap((S * ((T + 7) / 8) + 255) / 256), 256, 0, st>>>(
+                static_cast<const KeyT*>(tv.keys), tv.nvalid, static_cast<const KeyT*>(tv.rkeys), S, T, C,
+                tl.kl.tbits, tv.rridx, tv.ridx);
+            if (int e3 = check_launch()) return e3;
+            k_bucket_starts<<<grid_cap((S * (T + 1) + 255) / 256), 256, 0, st>>>(tv.rridx, S, T, tv.bstart);
+            if (int e3 = check_launch()) return e3;
         }
         return RAVEL_OK;
     });
@@ -547,20 +522,17 @@ int lk_bwd(const void* tape, int flags, const void* raddr, int addr_dtype, const
             const int64_t warps = (groups + (32 >> lsh) - 1) / (32 >> lsh);
             return with_key(tl.kl.key64, [&](auto kt) -> int {
                 using KeyT = decltype(kt);
-                return with_key(tl.rkey64, [&](auto rkt) -> int {
-                    using RKeyT = decltype(rkt);
-                    return with_dtype(dtype, [&](auto dtc) -> int {
-                        constexpr int DT = decltype(dtc)::value;
-                        return with_vb(gvb, [&](auto vbc) -> int {
-                            constexpr int VB = decltype(vbc)::value;
-                            if constexpr (!vb_ok<DT, VB>()) {
-                                return RAVEL_ERR_INVALID_ARG;
-                            } else {
-                                k_lk_bwd_gather<KeyT, RKeyT, DT, VB><<<grid_cap((warps * 32 + 255) / 256), 256, 0, st>>>(
-                                    a, static_cast<const RKeyT*>(tv.rkeys), tv.bstart, lsh);
-                                return check_launch();
-                            }
-                        });
+                return with_dtype(dtype, [&](auto dtc) -> int {
+                    constexpr int DT = decltype(dtc)::value;
+                    return with_vb(gvb, [&](auto vbc) -> int {
+                        constexpr int VB = decltype(vbc)::value;
+                        if constexpr (!vb_ok<DT, VB>()) {
+                            return RAVEL_ERR_INVALID_ARG;
+                        } else {
+                            k_lk_bwd_gather<KeyT, DT, VB><<<grid_cap((warps * 32 + 255) / 256), 256, 0, st>>>(
+                                a, static_cast<const KeyT*>(tv.rkeys), tv.rridx, tv.bstart, lsh);
+                            return check_launch();
+                        }
                     });
                 });
             });
@@ -813,19 +785,16 @@ int ss_bwd(const void* tape, int flags, const void* raddr, int addr_dtype, const
                 int lsh = 0;
                 while ((int64_t{1} << lsh) < grv) ++lsh;
                 const int64_t warps = (B * C * T + (32 >> lsh) - 1) / (32 >> lsh);
-                int e = with_key(tl.rkey64, [&](auto rkt) -> int {
-                    using RKeyT = decltype(rkt);
-                    return with_vb(gvb, [&](auto vbc) -> int {
-                        constexpr int VB = decltype(vbc)::value;
-                        if constexpr (!vb_ok<DT, VB>()) {
-                            return RAVEL_ERR_INVALID_ARG;
-                        } else {
-                            k_ss_bwd_gather<RKeyT, DT, VB><<<grid_cap((warps * 32 + 255) / 256), 256, 0, st>>>(
-                                static_cast<const RKeyT*>(tv.rkeys), tv.bstart, tv.nvalid, grad_sums, accbuf, B * C, T,
-                                C, D, tl.kl.tbits, lsh);
-                            return check_launch();
-                        }
-                    });
+                int e = with_vb(gvb, [&](auto vbc) -> int {
+                    constexpr int VB = decltype(vbc)::value;
+                    if constexpr (!vb_ok<DT, VB>()) {
+                        return RAVEL_ERR_INVALID_ARG;
+                    } else {
+                        k_ss_bwd_gather<KeyT, DT, VB><<<grid_cap((warps * 32 + 255) / 256), 256, 0, st>>>(
+                            static_cast<const KeyT*>(tv.keys), static_cast<const KeyT*>(tv.rkeys), tv.bstart, tv.nvalid,
+                            grad_sums, accbuf, B * C, T, C, D, tl.kl.tbits, lsh);
+                        return check_launch();
+                    }
                 });
                 if (e) return e;
                 return launch_segscan<KeyT, DT>(tv, tl, B, T, C, D, accbuf, 1, grad_payload, 0, nullptr, 1, 1,

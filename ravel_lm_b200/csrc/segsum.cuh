@@ -1201,13 +1201,13 @@ __global__ void __launch_bounds__(256) k_ss_scatter(SsGenArgs a) {
 }
 
 // General sum backward, first half, as a gather (no atomics, deterministic):
-// accbuf[s*T + q] = the sum of grad_sums over the reads whose latest valid write
-// is q (bucket q of the read tape); zero rows past nvalid.  A group of 2^lshift
+// accbuf[s*T + q] = the sum of grad_sums over the reads of q's address whose
+// latest earlier write is q (in bucket q of the read tape); zero rows past nvalid.  A group of 2^lshift
 // lanes takes one tape position, a lane one VB-byte vector of the gradient row.
-template <typename RKeyT, int DT, int VB>
-__global__ void __launch_bounds__(256) k_ss_bwd_gather(const RKeyT* rkeys, const int32_t* bstart, const int* nvalid,
-                                                       const void* grad, void* accbuf, int64_t S, int64_t T,
-                                                       int64_t C, int64_t D, int tbits, int lshift) {
+template <typename KeyT, int DT, int VB>
+__global__ void __launch_bounds__(256) k_ss_bwd_gather(const KeyT* wkeys, const KeyT* rkeys, const int32_t* bstart,
+                                                       const int* nvalid, const void* grad, void* accbuf, int64_t S,
+                                                       int64_t T, int64_t C, int64_t D, int tbits, int lshift) {
     using E = Elem<DT>;
     using Acc = typename E::Acc;
     using V = typename E::T;
@@ -1218,7 +1218,7 @@ __global__ void __launch_bounds__(256) k_ss_bwd_gather(const RKeyT* rkeys, const
     const int64_t gpw = 32 >> lshift;
     const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
-    const RKeyT rtmask = (static_cast<RKeyT>(1) << tbits) - 1;
+    const KeyT tmask = (static_cast<KeyT>(1) << tbits) - 1;
     const V* g = static_cast<const V*>(grad);
     for (int64_t gi = warp0 * gpw + grp; gi < S * T; gi += nwarps * gpw) {
         const int64_t s = gi / T, q = gi - s * T;
@@ -1229,17 +1229,23 @@ __global__ void __launch_bounds__(256) k_ss_bwd_gather(const RKeyT* rkeys, const
         for (int e = 0; e < EPV; ++e) acc[e] = Acc(0);
         if (q < n_s) {
             const int32_t* bs = bstart + s * (T + 2);
-            const RKeyT* rk = rkeys + s * T;
+            const KeyT* rk = rkeys + s * T;
+            const KeyT aq = wkeys[s * T + q] >> tbits;
             const int32_t i1 = bs[q + 2];
             for (int32_t i = bs[q + 1]; i < i1; i += 4) {  // 4 reads' loads in flight
                 uint32_t rrow[4];
+                bool use[4];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) rrow[u] = rows_of((i + u < i1 ? rk[i + u] : RKeyT(0)) & rtmask);
+                for (int u = 0; u < 4; ++u) {
+                    const KeyT key = i + u < i1 ? rk[i + u] : KeyT(0);
+                    rrow[u] = rows_of(key & tmask);
+                    use[u] = i + u < i1 && (key >> tbits) == aq;  // a read of q's own address
+                }
                 uint4 x[4];
 #pragma unroll
                 for (int u = 0; u < 4; ++u)
-                    x[u] = i + u < i1 ? ldg_vec<VB>(g + static_cast<uint64_t>(rrow[u]) * D + lig * EPV)
-                                      : make_uint4(0u, 0u, 0u, 0u);
+                    x[u] = use[u] ? ldg_vec<VB>(g + static_cast<uint64_t>(rrow[u]) * D + lig * EPV)
+                                  : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const V* xv = reinterpret_cast<const V*>(&x[u]);

@@ -14,9 +14,9 @@
 //                 warp, warp-private digit histograms and a block-wide scan.
 //   k_merge       merge-path merge of sorted runs for streams longer than a
 //                 tile (log2(tiles) passes, global memory ping-pong).
-//   k_read_search per read: lower bound of (addr, t) in its stream's sorted keys
-//                 = searchsorted(right=True)-1 of ravel_memory.py:159, restricted
-//                 to the stream.
+//   k_read_ranks  general tapes: the reads sorted like the writes, then each
+//                 ranked against the sorted writes = searchsorted(right=True)-1 of
+//                 ravel_memory.py:159, restricted to the stream.
 #pragma once
 
 #include <cooperative_groups.h>
@@ -35,34 +35,17 @@ struct SortArgs {
     int64_t tiles;         // tiles per stream
     void* keys_out;        // [S][T]
     int* nvalid;           // [S], pre-zeroed, or null when there is no mask
-    // read tape: when ridx is set, the sort orders each stream's READS by
-    // (latest valid earlier write + 1, t) instead of its writes by (address, t);
-    // waddr then holds the read addresses and wkeys the sorted write keys
-    const int32_t* ridx;   // [N] latest earlier write of every read (any address), -1 if none
-    const void* wkeys;     // [S][T] sorted write keys
-    int wkey64;            // write keys are 64-bit
     int clamp;             // addresses clamped to [0, A-1] (decode cache) instead of wrapped
 };
 
-// Sort key of event (b, c, t) (stream s = b*C + c).  Writes: (invalid bit | folded
-// address) above t; a masked write sorts after every valid one.  Reads (read
-// tape): 1 + the index of the latest earlier write when that write has the
-// read's address, else 0 (the read sees no write), above t.
+// Sort key of event (b, c, t) (stream s = b*C + c): (invalid bit | address)
+// above t, the address folded as the reference does (or clamped for the decode
+// cache); a masked write sorts after every valid one.
 template <typename KeyT>
 __device__ __forceinline__ KeyT sort_key(const SortArgs& a, int64_t b, int64_t c, int64_t s, int64_t t,
                                          int& nvalid_local) {
+    (void)s;
     const int64_t row = (b * a.T + t) * a.C + c;
-    if (a.ridx != nullptr) {
-        const int32_t q = a.ridx[row];
-        uint64_t v = 0;
-        if (q >= 0) {
-            const uint64_t ra = fold_addr(load_addr(a.waddr, row, a.addr_i64), a.A, a.key32);
-            const uint64_t wa = a.wkey64 ? (static_cast<const uint64_t*>(a.wkeys)[s * a.T + q] >> a.tbits)
-                                         : (static_cast<const uint32_t*>(a.wkeys)[s * a.T + q] >> a.tbits);
-            if (wa == ra) v = static_cast<uint64_t>(q) + 1;
-        }
-        return (static_cast<KeyT>(v) << a.tbits) | static_cast<KeyT>(t);
-    }
     const int64_t raw = load_addr(a.waddr, row, a.addr_i64);
     const uint64_t ad = a.clamp ? static_cast<uint64_t>(clamp_addr(raw, a.A)) : fold_addr(raw, a.A, a.key32);
     const bool valid = a.wmask == nullptr || a.wmask[b * a.T + t] != 0;
@@ -407,55 +390,52 @@ __global__ void k_stream_offsets(const int* __restrict__ nvalid, int64_t* __rest
     if (threadIdx.x == 0) soff[S] = carry;
 }
 
-struct SearchArgs {
-    const void* keys;
-    const int* nvalid;     // null: every stream holds T writes
-    const void* raddr;
-    int addr_i64, key32;
-    int64_t B, T, C, A;
-    int tbits;
-    int32_t* ridx;         // [N] local index of the latest earlier write (may be any address), -1 if none
-    FastDiv fd_C, fd_T;    // flat row -> (b, t, c)
-};
-
-// ravel_memory.py:153-159 restricted to the read's stream: the number of the
-// stream's valid keys below (addr, t), minus one.
+// Read tape ranks (ravel_memory.py:153-159 restricted to the read's stream):
+// the reads of every stream, sorted by (address, t) like the writes, each get the
+// index of the latest valid write below them in that order (any address), -1 if
+// none: rridx[s][i] for sorted read i, and ridx[r] for the read's flat row r.  The
+// ranks are non-decreasing along the sorted reads, so a thread takes 8
+// consecutive reads and bounds each binary search below by the previous rank.
 template <typename KeyT>
-__global__ void __launch_bounds__(256) k_read_search(SearchArgs a) {
-    const int64_t N = a.B * a.T * a.C;
-    for (int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; r < N;
-         r += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        uint32_t bt, c32, b32, t32;
-        a.fd_C.divmod(static_cast<uint32_t>(r), bt, c32);
-        a.fd_T.divmod(bt, b32, t32);
-        const int64_t t = t32;
-        const int64_t s = static_cast<int64_t>(b32) * a.C + c32;
-        const uint64_t ra = fold_addr(load_addr(a.raddr, r, a.addr_i64), a.A, a.key32);
-        const KeyT q = (static_cast<KeyT>(ra) << a.tbits) | static_cast<KeyT>(t);
-        const KeyT* k = static_cast<const KeyT*>(a.keys) + s * a.T;
-        int64_t lo = 0, hi = a.nvalid ? a.nvalid[s] : a.T;
-        while (lo < hi) {
-            const int64_t mid = (lo + hi) >> 1;
-            if (k[mid] < q) lo = mid + 1; else hi = mid;
+__global__ void __launch_bounds__(256) k_read_ranks(const KeyT* wkeys, const int* nvalid, const KeyT* rkeys,
+                                                   int64_t S, int64_t T, int64_t C, int tbits, int32_t* rridx,
+                                                   int32_t* ridx) {
+    const KeyT tmask = (static_cast<KeyT>(1) << tbits) - 1;
+    const int64_t per = (T + 7) / 8;
+    for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < S * per;
+         e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t s = e / per, i0 = (e - s * per) * 8;
+        const KeyT* wk = wkeys + s * T;
+        const KeyT* rk = rkeys + s * T;
+        const int64_t n = nvalid ? nvalid[s] : T;
+        const int64_t b = s / C, c = s - b * C;
+        int64_t lo = 0;
+        const int64_t i1 = i0 + 8 < T ? i0 + 8 : T;
+        for (int64_t i = i0; i < i1; ++i) {
+            const KeyT q = rk[i];
+            int64_t hi = n;
+            while (lo < hi) {
+                const int64_t mid = (lo + hi) >> 1;
+                if (wk[mid] < q) lo = mid + 1; else hi = mid;
+            }
+            rridx[s * T + i] = static_cast<int32_t>(lo - 1);
+            ridx[(b * T + static_cast<int64_t>(q & tmask)) * C + c] = static_cast<int32_t>(lo - 1);
         }
-        a.ridx[r] = static_cast<int32_t>(lo - 1);
     }
 }
 
 // Read tape bucket starts: bstart[s][j] = the number of stream s's sorted reads
-// whose field (key >> tbits, = latest valid write + 1) is below j, j = 0..T+1.
-// The reads whose latest valid write is q are rkeys[s][bstart[q+1] .. bstart[q+2]).
-// Thread (s, i) fills the starts between sorted reads i-1 and i (i = T: the end),
-// so every entry is written once.
-template <typename KeyT>
-__global__ void __launch_bounds__(256) k_bucket_starts(const KeyT* rkeys, int64_t S, int64_t T, int tbits,
-                                                      int32_t* bstart) {
+// whose rank + 1 is below j, j = 0..T+1.  The reads whose latest valid write
+// (any address) is q are the sorted reads bstart[q+1] .. bstart[q+2].  Thread
+// (s, i) fills the starts between sorted reads i-1 and i (i = T: the end), so
+// every entry is written once.
+__global__ void __launch_bounds__(256) k_bucket_starts(const int32_t* rridx, int64_t S, int64_t T, int32_t* bstart) {
     for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < S * (T + 1);
          e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         const int64_t s = e / (T + 1), i = e - s * (T + 1);
-        const KeyT* k = rkeys + s * T;
-        const int64_t lo = i > 0 ? static_cast<int64_t>(k[i - 1] >> tbits) + 1 : 0;
-        const int64_t hi = i < T ? static_cast<int64_t>(k[i] >> tbits) : T + 1;
+        const int32_t* r = rridx + s * T;
+        const int64_t lo = i > 0 ? static_cast<int64_t>(r[i - 1]) + 2 : 0;
+        const int64_t hi = i < T ? static_cast<int64_t>(r[i]) + 1 : T + 1;
         for (int64_t j = lo; j <= hi; ++j) bstart[s * (T + 2) + j] = static_cast<int32_t>(i);
     }
 }
