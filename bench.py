@@ -55,6 +55,8 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=4)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-general", action="store_true",
+                    help="skip the extra timing of the general path (reads drawn apart from the writes)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-streams", type=int, default=8, help="streams in the CPU baseline sample")
     ap.add_argument("--batch", type=int, default=None, help="override B per GPU (small profiling cases)")
@@ -421,6 +423,9 @@ def main():
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e(cfg, x, dev, args.e2e_steps, world)
+    general = None
+    if not args.no_general and cfg.addressing == "zipf":
+        general = run_general(cfg, x, dev, world)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = run_cpu_baseline(cfg, 1, 1, args.cpu_streams)
@@ -441,6 +446,7 @@ def main():
             "step_roofline": {"algorithmic_bytes": step_bytes, "achieved_gbs": step_bytes / (ms * 1e-3) / 1e9,
                               "frac": step_bytes / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], "peak": peaks["hbm_gbs"]},
             "roofline": roofline, "kernels": kernels, "e2e": e2e, "cpu_baseline": cpu, "decode": decode,
+            "general_path": general,
             "clocks": clk, "gpu_launches": launches,
         }
         print(json.dumps(line), flush=True)
@@ -470,6 +476,54 @@ def load_traffic(kernel: str, cfg):
         return None if ent is None else float(ent)
     except (ValueError, OSError):
         return None
+
+
+def run_general(cfg, x, dev, world, steps: int = 5) -> dict:
+    """The same step with reads drawn apart from the writes (the path of the model's
+    learned read heads, model.py:367-384): independent Zipf reads of the same shape."""
+    import torch
+    import ravel_lm_b200._lib as L
+    from ravel_lm_b200 import causal_last_k_lookup, causal_sum_lookup
+    from ravel_lm_b200.ravel_memory import clear_tape_cache
+    from ravel_lm_b200.workloads import zipf_ranks
+    g = torch.Generator(device=dev).manual_seed(2000 + cfg.cfg)
+    w = x["write"]
+    r = zipf_ranks(cfg.A, cfg.zipf_s, tuple(w.shape), g)
+    p = x["payload"].detach().requires_grad_(True)
+    gv, gs = x["g_vals"], x["g_sums"]
+    records = defaultdict(list)
+
+    def hook(name, thunk):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        rc = thunk()
+        e1.record()
+        records[name].append((e0, e1))
+        return rc
+
+    def step():
+        clear_tape_cache()
+        p.grad = None
+        vals, _m = causal_last_k_lookup(w, p, r, address_space=cfg.A, k=cfg.k)
+        sums, _s = causal_sum_lookup(w, p, r, address_space=cfg.A)
+        torch.autograd.backward([vals, sums], [gv, gs])
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize(dev)
+    L.set_call_hook(hook)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize(dev)
+    L.set_call_hook(None)
+    ms = max_over_ranks(t0.elapsed_time(t1) / steps, world)
+    per = {n: sum(a.elapsed_time(b) for a, b in v) / len(v) * 1000.0 for n, v in records.items()}
+    return {"reads": f"independent Zipf(s={cfg.zipf_s}) reads of the same shape", "ms_per_step": ms,
+            "value": cfg.tokens * world / (ms * 1e-3), "unit": "tokens/s", "steps": steps,
+            "kernels_us": per}
 
 
 def run_e2e(cfg, x, dev, steps, world):
