@@ -141,26 +141,41 @@ ScanPlan scan_plan(int64_t T, int64_t D, int dtype) {
     return s;
 }
 
-// Ranges per stream for the range scan: exactly one wave of CTAs (`slots` =
-// resident CTAs per SM x SMs) over all streams, at least one 256-position chunk
-// per range.  Scratch is sized for the most ranges any plan can use.
+// Ranges per stream for the range scan: `slots` ranges over T positions, each
+// range between rl_min and rl_max positions (a multiple of 8).  Scratch is
+// sized for the most ranges any plan can use (max_ranges).
 struct RangePlan {
     int64_t R, RL;
 };
 
-RangePlan range_plan(int64_t S, int64_t T, int64_t slots) {
+RangePlan range_plan(int64_t S, int64_t T, int64_t slots, int64_t rl_max = int64_t{1} << 40, int64_t rl_min = 64) {
     RangePlan p;
     int64_t R = S > 0 ? slots / S : 1;
     if (R < 1) R = 1;
     int64_t RL = (T + R - 1) / R;
     RL = (RL + 7) / 8 * 8;
-    if (RL < 64) RL = 64;
+    if (RL > rl_max) RL = rl_max;
+    if (RL < rl_min) RL = rl_min;
     p.RL = RL;
     p.R = T > 0 ? (T + RL - 1) / RL : 1;
     return p;
 }
 
-int64_t max_ranges(int64_t T) { return T > 0 ? (T + 63) / 64 : 1; }
+// Range-scan launch shape (overridable at build time for sweeps): blocks for
+// RAVEL_RS_WAVES waves of resident blocks, so that blocks at different phases
+// (piece sums, look-back, scan) share an SM; ranges of at least RAVEL_RS_RLMIN
+// positions, more than the 32-position snap window so that none is empty.
+// Measured at config 3 (sum forward / backward, µs): 1 wave 197 / 183,
+// 2 waves 173 / 170, 3 waves 167 / 158-166; 2-warp blocks, 48-position ranges
+// and a deeper ring were no faster.
+#ifndef RAVEL_RS_WAVES
+#define RAVEL_RS_WAVES 3
+#endif
+#ifndef RAVEL_RS_RLMIN
+#define RAVEL_RS_RLMIN 64
+#endif
+static_assert(RAVEL_RS_RLMIN > 32 && RAVEL_RS_RLMIN <= 64 && RAVEL_RS_RLMIN % 8 == 0, "ranges outgrow the snap window");
+int64_t max_ranges(int64_t T) { return T > 0 ? (T + RAVEL_RS_RLMIN - 1) / RAVEL_RS_RLMIN : 1; }
 
 int sm_count() {
     static int n = 0;
@@ -174,8 +189,7 @@ int sm_count() {
 }
 
 struct ScratchLayout {
-    size_t off_sort, off_flags, off_ticket, off_agg, off_incl, off_tail, off_tail_hs, off_bounds, off_rot, off_big,
-        total;
+    size_t off_sort, off_flags, off_ticket, off_agg, off_incl, off_bflags, off_bval, off_big, total;
 };
 
 ScratchLayout scratch_layout(int64_t B, int64_t T, int64_t C, int64_t D, int64_t A, int dtype, int flags) {
@@ -191,12 +205,11 @@ ScratchLayout scratch_layout(int64_t B, int64_t T, int64_t C, int64_t D, int64_t
     l.off_ticket = l.off_flags + align_up(nch * 4);
     l.off_agg = l.off_ticket + 256;
     l.off_incl = l.off_agg + align_up(nch * static_cast<size_t>(D) * ab);
-    const size_t nr = S * static_cast<size_t>(max_ranges(T));
-    l.off_tail = l.off_incl + align_up(nch * static_cast<size_t>(D) * ab);
-    l.off_tail_hs = l.off_tail + align_up(nr * static_cast<size_t>(D) * ab);
-    l.off_bounds = l.off_tail_hs + align_up(nr * 4);
-    l.off_rot = l.off_bounds + align_up((nr + S) * 4);
-    l.off_big = l.off_rot + align_up(nr * 4);
+    // range-scan blocks hold at least GS_WARPS ranges
+    const size_t nb = S * static_cast<size_t>((max_ranges(T) + GS_WARPS - 1) / GS_WARPS);
+    l.off_bflags = l.off_incl + align_up(nch * static_cast<size_t>(D) * ab);
+    l.off_bval = l.off_bflags + align_up((nb + 1) * 4);
+    l.off_big = l.off_bval + align_up(nb * 2 * static_cast<size_t>(D) * ab);
     l.total = l.off_big + (t.general ? align_up(N * static_cast<size_t>(D) * ab) : 0);
     return l;
 }
@@ -613,34 +626,38 @@ int launch_segscan(const TapeView& tv, const TapeLayout& tl, int64_t B, int64_t 
         ga.lshift = lshift;
         ga.snap = GS_SNAP;
         ga.in = in; ga.out = out; ga.out_mask = out_mask;
-        ga.piece = sc + sl.off_tail;
-        ga.rflags = reinterpret_cast<uint32_t*>(sc + sl.off_tail_hs);
-        ga.bounds = reinterpret_cast<int32_t*>(sc + sl.off_bounds);
-        ga.rot = reinterpret_cast<int32_t*>(sc + sl.off_rot);
         auto go = [&](auto vplc, auto inc, auto outc) -> int {
             constexpr int VPL = decltype(vplc)::value;
             constexpr bool IS = decltype(inc)::value != 0;
             constexpr bool OS = decltype(outc)::value != 0;
-            auto kern = inclusive ? k_group_scan<KeyT, DT, IS, OS, true, VPL>
-                                  : k_group_scan<KeyT, DT, IS, OS, false, VPL>;
-            const size_t smem = group_scan_smem<VPL>();
-            if (int e = set_smem(kern, smem)) return e;
+            auto kern = inclusive ? k_range_scan<KeyT, DT, IS, OS, true, VPL>
+                                  : k_range_scan<KeyT, DT, IS, OS, false, VPL>;
+            const int64_t gpb = GS_WARPS * (int64_t{32} >> lshift);
+            constexpr int64_t kRlMax = 1024;
+            const int64_t bmw_max = gpb * kRlMax / 32 + 2;
+            const size_t smem_max = range_scan_smem(VPL, gpb, D, sizeof(Acc), bmw_max);
+            if (int e = set_smem(kern, smem_max)) return e;
             int occ = 0;
-            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, GS_WARPS * 32, smem) != cudaSuccess ||
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, GS_WARPS * 32,
+                                                              range_scan_smem(VPL, gpb, D, sizeof(Acc), 2)) !=
+                    cudaSuccess ||
                 occ < 1)
                 occ = 1;
-            // one range per lane group, one wave of groups
-            const int64_t groups_per_warp = int64_t{32} >> lshift;
-            const RangePlan rp =
-                range_plan(B * C, T, static_cast<int64_t>(occ) * GS_WARPS * groups_per_warp * sm_count());
+            // one range per lane group; whole blocks per stream, RAVEL_RS_WAVES waves of blocks
+            int64_t bps = static_cast<int64_t>(occ) * sm_count() * RAVEL_RS_WAVES / (B * C > 0 ? B * C : 1);
+            if (bps < 1) bps = 1;
+            const RangePlan rp = range_plan(1, T, bps * gpb, kRlMax, RAVEL_RS_RLMIN);
             ga.R = rp.R;
             ga.RL = rp.RL;
-            const int64_t nranges = B * C * rp.R;
-            k_group_prep<KeyT, DT, IS, VPL>
-                <<<static_cast<unsigned>((nranges + GS_WARPS - 1) / GS_WARPS), GS_WARPS * 32, 0, st>>>(ga);
-            if (int e = check_launch()) return e;
-            const int64_t per_block = GS_WARPS * groups_per_warp;
-            kern<<<static_cast<unsigned>((nranges + per_block - 1) / per_block), GS_WARPS * 32, smem, st>>>(ga);
+            ga.CB = (rp.R + gpb - 1) / gpb;
+            ga.bmw = static_cast<int>(gpb * rp.RL / 32 + 2);
+            ga.bflags = reinterpret_cast<unsigned*>(sc + sl.off_bflags);
+            ga.bval = sc + sl.off_bval;
+            const int64_t nblocks = B * C * ga.CB;
+            if (cudaMemsetAsync(ga.bflags, 0, static_cast<size_t>(nblocks + 1) * 4, st) != cudaSuccess)
+                return RAVEL_ERR_CUDA;
+            const size_t smem = range_scan_smem(VPL, gpb, D, sizeof(Acc), ga.bmw);
+            kern<<<static_cast<unsigned>(nblocks), GS_WARPS * 32, smem, st>>>(ga);
             return check_launch();
         };
         auto by_mode = [&](auto vplc) -> int {

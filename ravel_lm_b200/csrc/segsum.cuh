@@ -664,28 +664,37 @@ __device__ __forceinline__ RawWords<EL * sizeof(X)> pack(const Acc (&v)[EL]) {
     return r;
 }
 
-// ------------------------------------------------------------------ group scan (two kernels)
+// ------------------------------------------------------------------ group scan
 // The scan used for rows that are whole multiples of 16 bytes, up to 1 KB.
 // Each stream's tape (in scan order) is cut into R ranges of about RL
 // positions; a nominal boundary r*RL moves forward to a segment start when one
-// lies within `snap` positions, so every range stays within RL + snap.
-//   k_group_prep  one warp per range: writes its lower boundary lo, its last
-//                 segment start ls, and -- when its upper boundary hi falls
-//                 inside a segment -- its piece: the sum of its rows from ls
-//                 (from lo when it holds no start) to hi, which is the carry it
-//                 hands to the next range.  Pieces never overlap.
-//   k_group_scan  a group of L = row_bytes / (16 VPL) lanes per range (32/L
-//                 ranges per warp); each lane owns VPL 16-byte column slices of
-//                 every row.  A lane stages its own slices with cp.async into a
-//                 lane-private ring of shared memory GS_Q blocks of GS_U rows
-//                 deep, so no lane ever waits on another.  The group visits
-//                 ls .. hi-1 first -- the rows the prep kernel has just read,
-//                 so likely still in L2 -- then lo .. ls-1; the carry (the pieces of the
-//                 ranges before, back to one that holds a segment start)
-//                 enters at lo.  The running sum is reset at segment starts.
-// No block waits on another.  Rows are read and written in tape order, i.e. at
-// random row addresses, so the scan kernel is bounded by random 16-byte-sliced
-// row traffic rather than by streaming bandwidth.
+// lies within `snap` positions, so every range stays within RL + snap.  A
+// range's *piece* is the sum of its rows from its last segment start (from its
+// lower boundary lo when it holds none) to its upper boundary hi, when hi falls
+// inside a segment: the carry it hands to the next range.
+//
+// k_range_scan: a block owns GPB = GS_WARPS * 32 / L consecutive ranges of one
+// stream, one range per lane group of L = row_bytes / (16 VPL) lanes (each lane
+// owns VPL 16-byte column slices of every row).  Blocks take tickets, so every
+// block one waits on is already running.
+//   1. segment-start bitmap of the block's span from one coalesced pass over
+//      its keys; each range's bounds, its last segment start and whether hi
+//      falls inside a segment;
+//   2. each lane group sums its range's piece;
+//   3. warp 0 publishes the block's outgoing carry (the pieces back to the last
+//      range with a segment start: final at once when there is one, else an
+//      aggregate until the incoming carry is known), looks back over the
+//      blocks before for the incoming carry when the block's first position
+//      does not start a segment, and turns the pieces into every range's
+//      incoming carry;
+//   4. each lane group scans its range through a lane-private cp.async ring
+//      of GS_Q blocks of GS_U rows in shared memory, so no lane waits on
+//      another: the piece rows first (just read, still in L2), then lo .. rot-1
+//      with the carry entering at lo.  The running sum resets at segment starts.
+// Rows are read and written in tape order, i.e. at random row addresses, so
+// the kernel is bounded by random 16-byte-sliced row traffic rather than by
+// streaming bandwidth.  Look-back waits are bounded (RAVEL_DEVERR_SPIN, the
+// carry taken as found).
 // Tuning constants (overridable at build time for sweeps).
 #ifndef RAVEL_GS_WARPS
 #define RAVEL_GS_WARPS 4
@@ -719,243 +728,253 @@ struct GsArgs {
     const void* in;        // dtype [N, D] by flat row, or Acc [S*T, D] by tape index
     void* out;             // dtype [N, D] by flat row, or Acc [S*T, D] by tape index
     uint8_t* out_mask;     // optional [N]: 1 where an earlier write of the segment exists
-    void* piece;           // Acc [S*R, D]
-    int32_t* bounds;       // [S*(R+1)] lower boundaries in scan order, then n_s
-    int32_t* rot;          // [S*R] last segment start in the range, else lo
-    uint32_t* rflags;      // [S*R] bit 0: range holds a segment start; bit 1: piece written
+    int64_t CB;            // blocks per stream
+    int bmw;               // segment-start bitmap words per block
+    unsigned* bflags;      // [S*CB] look-back states, then the ticket counter; zeroed before launch
+    void* bval;            // Acc [S*CB][2][D]: block aggregate, block inclusive carry
 };
 
-// Keys of one stream addressed in scan order.
-template <typename KeyT>
-struct ScanKeys {
-    const KeyT* k;
-    int64_t n;
-    int reverse, tbits;
-    __device__ __forceinline__ int64_t pos(int64_t si) const { return reverse ? n - 1 - si : si; }
-    __device__ __forceinline__ KeyT at(int64_t si) const { return k[pos(si)]; }
-    __device__ __forceinline__ bool start(int64_t si) const {
-        return si == 0 || ((at(si) ^ at(si - 1)) >> tbits) != 0;
-    }
-};
-
-template <typename KeyT, int DT, bool IN_SORTED, int VPL>
-__global__ void __launch_bounds__(GS_WARPS * 32) k_group_prep(GsArgs a) {
-    using E = Elem<DT>;
-    using Acc = typename E::Acc;
-    using InT = typename std::conditional<IN_SORTED, Acc, typename E::T>::type;
-    constexpr int EL = 16 / static_cast<int>(sizeof(InT));
-    constexpr int NE = VPL * EL;
-    const int lane = threadIdx.x & 31;
-    const int64_t g = static_cast<int64_t>(blockIdx.x) * GS_WARPS + (threadIdx.x >> 5);
-    if (g >= a.S * a.R) return;  // whole warp
-    const int64_t s = g / a.R, r = g - s * a.R;
-    const int64_t n_s = a.nvalid ? a.nvalid[s] : a.T;
-    const ScanKeys<KeyT> kk{static_cast<const KeyT*>(a.keys) + s * a.T, n_s, a.reverse, a.tbits};
-    // One round of key loads for the whole geometry: window 0 at the nominal lower
-    // boundary xl, window 1 at the nominal upper boundary xh, windows 2..9 the 256
-    // scan indices below the largest possible hi.  Lane l of window w holds the key
-    // of scan index base[w] + l; the key before it comes from lane l-1 (lane 0
-    // loads its own).  All loads are issued before the first ballot.
-    constexpr int NWIN = 10;
-    const int64_t xl = r * a.RL, xh = (r + 1) * a.RL;
-    const int64_t emax = xh + 32 < n_s ? xh + 32 : n_s;
-    int64_t base[NWIN];
-    base[0] = xl;
-    base[1] = xh;
-#pragma unroll
-    for (int w = 2; w < NWIN; ++w) base[w] = emax - 32 * (w - 1);
-    KeyT kv[NWIN], kb[NWIN];
-#pragma unroll
-    for (int w = 0; w < NWIN; ++w) {
-        const int64_t si = base[w] + lane;
-        kv[w] = (si >= 0 && si < n_s) ? kk.at(si) : KeyT(0);
-        kb[w] = (lane == 0 && si > 0 && si - 1 < n_s) ? kk.at(si - 1) : KeyT(0);
-    }
-    unsigned bits[NWIN];  // bit l: scan index base[w] + l (< n_s) begins a segment
-#pragma unroll
-    for (int w = 0; w < NWIN; ++w) {
-        const int64_t si = base[w] + lane;
-        KeyT kp = __shfl_up_sync(0xffffffffu, kv[w], 1);
-        if (lane == 0) kp = kb[w];
-        bits[w] = __ballot_sync(0xffffffffu, si >= 0 && si < n_s && (si == 0 || ((kv[w] ^ kp) >> a.tbits) != 0));
-    }
-    // boundary at nominal scan index x: the first segment start in [x, x + snap), else x
-    const unsigned smask = a.snap >= 32 ? 0xffffffffu : ((1u << a.snap) - 1u);
-    auto snap = [&](int64_t x, unsigned win) -> int64_t {
-        if (x >= n_s) return n_s;
-        if (x == 0) return 0;
-        const unsigned m = win & smask;
-        return m ? x + __ffs(m) - 1 : x;
-    };
-    const int64_t lo = snap(xl, bits[0]);
-    const int64_t hi = snap(xh, bits[1]);
-    const bool hi_start = hi < n_s && hi - xh < 32 && ((bits[1] >> (hi - xh)) & 1u);
-    const bool hi_open = hi < n_s && lo < hi && !hi_start;
-    // last segment start in [lo, hi): the search windows first, further down only
-    // when the range reaches below them
-    auto keep = [&](unsigned v, int64_t x) -> unsigned {  // bits of [lo, hi) within [x, x + 32)
-        const int64_t b0 = lo - x, b1 = hi - x;
-        if (b0 > 0) v = b0 >= 32 ? 0u : v & ~((1u << b0) - 1u);
-        if (b1 < 32) v = b1 <= 0 ? 0u : v & ((1u << b1) - 1u);
-        return v;
-    };
-    int64_t ls = -1;
-#pragma unroll
-    for (int w = 2; w < NWIN; ++w) {
-        const unsigned v = keep(bits[w], base[w]);
-        if (ls < 0 && v != 0u) ls = base[w] + 31 - __clz(v);
-    }
-    for (int64_t e0 = emax - 32 * (NWIN - 2); e0 > lo && ls < 0; e0 -= 128) {
-        unsigned m[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const int64_t si = e0 - 1 - 32 * q - lane;
-            m[q] = __ballot_sync(0xffffffffu, si >= lo && si < hi && kk.start(si));
-        }
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-            if (ls < 0 && m[q] != 0u) ls = e0 - 32 * q - __ffs(m[q]);
-    }
-    const int64_t rot = ls >= 0 ? ls : lo;
-    if (lane == 0) {
-        int32_t* bounds = a.bounds + s * (a.R + 1);
-        bounds[r] = static_cast<int32_t>(lo);
-        if (r == a.R - 1) bounds[a.R] = static_cast<int32_t>(n_s);
-        a.rot[g] = static_cast<int32_t>(rot);
-        a.rflags[g] = (ls >= 0 ? 1u : 0u) | (hi_open ? 2u : 0u);
-    }
-    if (!hi_open) return;
-    // piece = sum of rows [rot, hi): lane l fetches the row of piece index 32q + l for
-    // 8 chunks q at once; groups of L lanes then read each chunk's rows, L rows a group
-    const uint32_t L = 1u << a.lshift, G = 32u >> a.lshift;
-    const uint32_t grp = static_cast<uint32_t>(lane) >> a.lshift, lig = static_cast<uint32_t>(lane) & (L - 1);
-    const RowMap rows_of(s, a.T, a.C);
-    const KeyT tmask = (static_cast<KeyT>(1) << a.tbits) - 1;
-    const char* in = static_cast<const char*>(a.in) + lig * 16u;
-    const uint64_t rb = static_cast<uint64_t>(a.D) * sizeof(InT);
-    Acc acc[NE];
-#pragma unroll
-    for (int q = 0; q < NE; ++q) acc[q] = Acc(0);
-    const int64_t n = hi - rot;
-    auto row_of = [&](int64_t i) -> uint32_t {
-        if (i >= n) return 0u;
-        const int64_t p = kk.pos(rot + i);
-        return IN_SORTED ? static_cast<uint32_t>(s * a.T + p) : rows_of(kk.k[p] & tmask);
-    };
-    for (int64_t c0 = 0; c0 < n; c0 += 256) {
-        uint32_t rw[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) rw[q] = row_of(c0 + 32 * q + lane);
-#pragma unroll
-        for (int q = 0; q < 8; q += 2) {  // two chunks of row loads in flight
-            const int64_t cnt0 = n - c0 - 32 * q;  // rows left from chunk q on
-            if (cnt0 <= 0) break;
-            const int64_t cnt1 = cnt0 - 32;
-#pragma unroll 8
-            for (uint32_t u = 0; u < L; ++u) {
-                const uint32_t j = u * G + grp;
-                const uint32_t row0 = __shfl_sync(0xffffffffu, rw[q], static_cast<int>(j));
-                const uint32_t row1 = __shfl_sync(0xffffffffu, rw[q + 1], static_cast<int>(j));
-                uint4 w0[VPL], w1[VPL];
-#pragma unroll
-                for (int v = 0; v < VPL; ++v) {
-                    w0[v] = static_cast<int64_t>(j) < cnt0 ? ld_nc_v4(in + row0 * rb + v * L * 16u)
-                                                           : make_uint4(0u, 0u, 0u, 0u);
-                    w1[v] = static_cast<int64_t>(j) < cnt1 ? ld_nc_v4(in + row1 * rb + v * L * 16u)
-                                                           : make_uint4(0u, 0u, 0u, 0u);
-                }
-#pragma unroll
-                for (int v = 0; v < VPL; ++v) {
-                    RawWords<16> x0, x1;
-                    x0.w[0] = w0[v].x; x0.w[1] = w0[v].y; x0.w[2] = w0[v].z; x0.w[3] = w0[v].w;
-                    x1.w[0] = w1[v].x; x1.w[1] = w1[v].y; x1.w[2] = w1[v].z; x1.w[3] = w1[v].w;
-                    Acc f0[EL], f1[EL];
-                    unpack<InT, Acc, EL>(x0, f0);
-                    unpack<InT, Acc, EL>(x1, f1);
-#pragma unroll
-                    for (int e = 0; e < EL; ++e) acc[v * EL + e] += f0[e] + f1[e];
-                }
-            }
-        }
-    }
-    for (uint32_t off = L; off < 32u; off <<= 1)
-#pragma unroll
-        for (int q = 0; q < NE; ++q) acc[q] += __shfl_xor_sync(0xffffffffu, acc[q], static_cast<int>(off));
-    if (grp == 0) {
-        Acc* pc = static_cast<Acc*>(a.piece) + g * a.D;
-#pragma unroll
-        for (int v = 0; v < VPL; ++v)
-#pragma unroll
-            for (int e = 0; e < EL; ++e) pc[(lig + v * L) * EL + e] = acc[v * EL + e];
-    }
-}
-
-template <int VPL>
-constexpr size_t group_scan_smem() {
-    return static_cast<size_t>(GS_WARPS) * GS_Q * GS_U * 32 * (16 * VPL + 4);
+inline size_t range_scan_smem(int vpl, int64_t gpb, int64_t D, size_t acc_bytes, int64_t bmw) {
+    size_t b = static_cast<size_t>(GS_WARPS) * GS_Q * GS_U * 32 * (16 * vpl + 4);
+    b += static_cast<size_t>(gpb) * D * acc_bytes;
+    b += static_cast<size_t>(bmw) * 4 + static_cast<size_t>(gpb + 1) * 4 + static_cast<size_t>(gpb) * 8;
+    return b;
 }
 
 template <typename KeyT, int DT, bool IN_SORTED, bool OUT_SORTED, bool INCL, int VPL>
-__global__ void __launch_bounds__(GS_WARPS * 32) k_group_scan(GsArgs a) {
+__global__ void __launch_bounds__(GS_WARPS * 32) k_range_scan(GsArgs a) {
     using E = Elem<DT>;
     using Acc = typename E::Acc;
     using V = typename E::T;
     using InT = typename std::conditional<IN_SORTED, Acc, V>::type;
-    using OutT = V;  // sorted outputs too are stored in the payload dtype
+    using OutT = V;
     constexpr int EL = 16 / static_cast<int>(sizeof(InT));
     constexpr int NE = VPL * EL;
     constexpr int SLOTS = GS_Q * GS_U;
+    constexpr int PU = 8 / VPL;  // piece rows per lane in flight
     extern __shared__ __align__(16) unsigned char smem[];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    // lane-private ring: slot j of this lane's data at ring + (j*32 + lane)*16*VPL,
-    // its row word (output row | start bit 31) at meta + (j*32 + lane)*4
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t L = 1u << a.lshift;
+    const int gpw = 32 >> a.lshift, GPB = GS_WARPS * gpw;
+    const uint32_t grp = static_cast<uint32_t>(lane) >> a.lshift, lig = static_cast<uint32_t>(lane) & (L - 1);
+    const int gib = warp * gpw + static_cast<int>(grp);
+    const uint32_t D = a.D;
+    const int tb = a.tbits;
     const uint32_t ring = smem_u32(smem) + static_cast<uint32_t>(warp) * SLOTS * 32 * (16 * VPL + 4);
     const uint32_t meta = ring + SLOTS * 32 * 16 * VPL;
-    const uint32_t L = 1u << a.lshift;
-    const uint32_t grp = static_cast<uint32_t>(lane) >> a.lshift, lig = static_cast<uint32_t>(lane) & (L - 1);
-    const int64_t g = (static_cast<int64_t>(blockIdx.x) * GS_WARPS + warp) * (32 >> a.lshift) + grp;
-    if (g >= a.S * a.R) return;  // this group only: nothing below synchronises lanes
-    const int64_t s = g / a.R, r = g - s * a.R;
-    const int32_t* bounds = a.bounds + s * (a.R + 1);
-    const int32_t lo = bounds[r], hi = bounds[r + 1];
-    if (lo >= hi) return;
+    Acc* cpc = reinterpret_cast<Acc*>(smem + static_cast<size_t>(GS_WARPS) * SLOTS * 32 * (16 * VPL + 4));
+    uint32_t* bm = reinterpret_cast<uint32_t*>(cpc + static_cast<size_t>(GPB) * D);
+    int32_t* glo = reinterpret_cast<int32_t*>(bm + a.bmw);  // [GPB + 1] range bounds
+    int32_t* grot = glo + GPB + 1;                           // [GPB] first piece position
+    int32_t* gfl = grot + GPB;                               // [GPB] bit 0 start inside, bit 1 hi open, bit 2 lo starts
+    __shared__ unsigned s_tk;
+    if (tid == 0) s_tk = atomicAdd(a.bflags + a.S * a.CB, 1u);
+    __syncthreads();
+    const int64_t tk = s_tk;
+    const int64_t s = tk / a.CB, cb = tk - s * a.CB;
     const int32_t n_s = a.nvalid ? a.nvalid[s] : static_cast<int32_t>(a.T);
-    const ScanKeys<KeyT> kk{static_cast<const KeyT*>(a.keys) + s * a.T, n_s, a.reverse, a.tbits};
-    // key of scan position si at kbase[dir * si]; tape index tix0 + dir * si
+    const int64_t r0 = cb * GPB;
+    const int nr = static_cast<int>(a.R - r0 < GPB ? a.R - r0 : GPB);
+    const int32_t RL = static_cast<int32_t>(a.RL);
+    const int32_t X0 = static_cast<int32_t>(r0 * a.RL);
+    if (nr <= 0 || X0 >= n_s) return;  // whole block: the empty tail of the stream
+
     const int32_t dir = a.reverse ? -1 : 1;
     const KeyT* kbase = static_cast<const KeyT*>(a.keys) + s * a.T + (a.reverse ? n_s - 1 : 0);
     const uint32_t tix0 = static_cast<uint32_t>(s * a.T) + static_cast<uint32_t>(a.reverse ? n_s - 1 : 0);
-    const int32_t rot = a.rot[g];
-    const int32_t len = hi - lo, nA = hi - rot;
-    const int32_t offA = rot, offB = lo - nA;  // si = i + (i < nA ? offA : offB)
-    const int32_t inj = nA == len ? 0 : nA;    // sequence index of position lo
-    const uint32_t D = a.D;
-    const int tb = a.tbits;
-
-    // carry entering at lo: pieces of the ranges before, back to one with a segment start
-    Acc carry[NE];
-#pragma unroll
-    for (int q = 0; q < NE; ++q) carry[q] = Acc(0);
-    if (!kk.start(lo)) {
-        const Acc* pc = static_cast<const Acc*>(a.piece) + s * a.R * D;
-        for (int64_t rr = r - 1; rr >= 0; --rr) {
-#pragma unroll
-            for (int v = 0; v < VPL; ++v)
-#pragma unroll
-                for (int e = 0; e < EL; ++e) carry[v * EL + e] += pc[rr * D + (lig + v * L) * EL + e];
-            if (a.rflags[s * a.R + rr] & 1u) break;
+    // 1. segment starts of scan positions [X0, X0 + 32 bmw)
+    for (int w = warp; w < a.bmw; w += GS_WARPS) {
+        const int32_t si = X0 + 32 * w + lane;
+        const bool live = si < n_s;
+        const KeyT k = live ? kbase[dir * si] : KeyT(0);
+        KeyT kp = __shfl_up_sync(0xffffffffu, k, 1);
+        if (lane == 0 && live && si > 0) kp = kbase[dir * (si - 1)];
+        const unsigned b = __ballot_sync(0xffffffffu, live && (si == 0 || ((k ^ kp) >> tb) != 0));
+        if (lane == 0) bm[w] = b;
+    }
+    __syncthreads();
+    auto bit = [&](int32_t x) -> bool {
+        if (x >= n_s) return false;
+        const int32_t o = x - X0;
+        return (bm[o >> 5] >> (o & 31)) & 1u;
+    };
+    if (warp == 0) {
+        const unsigned smask = a.snap >= 32 ? 0xffffffffu : ((1u << a.snap) - 1u);
+        for (int j = lane; j <= nr; j += 32) {
+            const int32_t x = X0 + j * RL;
+            int32_t lo;
+            if (x >= n_s) lo = n_s;
+            else if (x == 0) lo = 0;
+            else {
+                const int32_t o = x - X0;
+                const uint64_t w2 = static_cast<uint64_t>(bm[o >> 5]) | (static_cast<uint64_t>(bm[(o >> 5) + 1]) << 32);
+                const unsigned win = static_cast<unsigned>(w2 >> (o & 31)) & smask;
+                lo = win ? x + __ffs(win) - 1 : x;
+            }
+            glo[j] = lo;
+        }
+        __syncwarp();
+        for (int j = lane; j < nr; j += 32) {
+            const int32_t l = glo[j], h = glo[j + 1];
+            int32_t ls = -1;
+            for (int32_t e = h; e > l && ls < 0;) {  // last start in [l, h), a word at a time
+                const int32_t o = e - 1 - X0;
+                const int w = o >> 5;
+                unsigned m = bm[w] & (0xffffffffu >> (31 - (o & 31)));
+                const int32_t wb = X0 + 32 * w;
+                if (wb < l) m &= ~((1u << (l - wb)) - 1u);
+                if (m) ls = wb + 31 - __clz(m);
+                e = wb;
+            }
+            grot[j] = ls >= 0 ? ls : l;
+            gfl[j] = (ls >= 0 ? 1 : 0) | ((h < n_s && l < h && !bit(h)) ? 2 : 0) | (bit(l) ? 4 : 0);
         }
     }
-    // keys before the two sequence breaks (i = 0 at rot, i = nA at lo); ~key marks a stream start
-    const KeyT kbr0 = rot > 0 ? kbase[dir * (rot - 1)] : ~kbase[dir * rot];
-    const KeyT kbrA = (nA < len && lo > 0) ? kbase[dir * (lo - 1)] : ~kbase[dir * lo];
+    __syncthreads();
 
     const RowMap rows_of(s, a.T, a.C);
     const KeyT tmask = (static_cast<KeyT>(1) << tb) - 1;
     const char* in = static_cast<const char*>(a.in) + lig * 16u;
+    const uint32_t rbi = D * static_cast<uint32_t>(sizeof(InT));
+    auto row_in = [&](int32_t si, KeyT k) -> uint32_t {
+        return IN_SORTED ? tix0 + static_cast<uint32_t>(dir * si) : rows_of(k & tmask);
+    };
+    // 2. pieces
+    {
+        int32_t p0 = 0, n = 0;
+        if (gib < nr && (gfl[gib] & 2)) {
+            p0 = grot[gib];
+            n = glo[gib + 1] - p0;
+        }
+        int32_t nmax = n;
+        for (uint32_t off = L; off < 32u; off <<= 1) {
+            const int32_t o = __shfl_xor_sync(0xffffffffu, nmax, static_cast<int>(off));
+            nmax = o > nmax ? o : nmax;
+        }
+        Acc acc[NE];
+#pragma unroll
+        for (int q = 0; q < NE; ++q) acc[q] = Acc(0);
+        KeyT kn[PU];
+#pragma unroll
+        for (int u = 0; u < PU; ++u) kn[u] = u < n ? kbase[dir * (p0 + u)] : KeyT(0);
+        for (int32_t i0 = 0; i0 < nmax; i0 += PU) {
+            uint4 w[PU][VPL];
+#pragma unroll
+            for (int u = 0; u < PU; ++u) {
+                const int32_t i = i0 + u;
+                const uint32_t row = row_in(p0 + i, kn[u]);
+#pragma unroll
+                for (int v = 0; v < VPL; ++v)
+                    w[u][v] = i < n ? ld_nc_v4(in + static_cast<uint64_t>(row) * rbi + v * L * 16u)
+                                    : make_uint4(0u, 0u, 0u, 0u);
+            }
+#pragma unroll
+            for (int u = 0; u < PU; ++u) {
+                const int32_t i = i0 + PU + u;
+                kn[u] = i < n ? kbase[dir * (p0 + i)] : KeyT(0);
+            }
+#pragma unroll
+            for (int u = 0; u < PU; ++u)
+#pragma unroll
+                for (int v = 0; v < VPL; ++v) {
+                    RawWords<16> x;
+                    x.w[0] = w[u][v].x; x.w[1] = w[u][v].y; x.w[2] = w[u][v].z; x.w[3] = w[u][v].w;
+                    Acc f[EL];
+                    unpack<InT, Acc, EL>(x, f);
+#pragma unroll
+                    for (int e = 0; e < EL; ++e) acc[v * EL + e] += f[e];
+                }
+        }
+#pragma unroll
+        for (int v = 0; v < VPL; ++v)
+#pragma unroll
+            for (int e = 0; e < EL; ++e) cpc[static_cast<uint32_t>(gib) * D + (lig + v * L) * EL + e] = acc[v * EL + e];
+    }
+    __syncthreads();
+    // 3. block carry: publish, look back, per-range carries (warp 0, lane owns columns lane + 32 q)
+    if (warp == 0) {
+        Acc* bv = static_cast<Acc*>(a.bval);
+        int jstar = -1;
+        for (int j = 0; j < nr; ++j)
+            if (gfl[j] & 1) jstar = j;
+        const bool closed = jstar >= 0;
+        for (uint32_t col = lane; col < D; col += 32) {
+            Acc o = Acc(0);
+            for (int j = closed ? jstar : 0; j < nr; ++j) o += cpc[static_cast<uint32_t>(j) * D + col];
+            bv[(tk * 2 + (closed ? 1 : 0)) * D + col] = o;
+        }
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) st_release(a.bflags + tk, closed ? 2u : 1u);
+        const bool need = cb > 0 && !(gfl[0] & 4);
+        // incoming carry of the block, per owned column
+        constexpr int MAXC = (1024 / static_cast<int>(sizeof(V)) + 31) / 32;  // rows up to 1 KB
+        Acc cin[MAXC];
+#pragma unroll
+        for (int q = 0; q < MAXC; ++q) cin[q] = Acc(0);
+        if (need) {
+            for (int64_t j = tk - 1;; --j) {
+                unsigned f = 0, spins = 0;
+                while ((f = ld_acquire(a.bflags + j)) == 0u) {
+                    if (++spins > SPIN_LIMIT) break;
+                    __nanosleep(64);
+                }
+                if (f == 0u) {
+                    if (lane == 0) flag_error(RAVEL_DEVERR_SPIN);
+                    break;
+                }
+                const Acc* src = bv + (j * 2 + (f == 2u ? 1 : 0)) * D;
+#pragma unroll
+                for (int q = 0; q < MAXC; ++q) {
+                    const uint32_t col = lane + 32u * q;
+                    if (col < D) cin[q] += __ldcg(src + col);
+                }
+                if (f == 2u || j == tk - cb) break;
+            }
+        }
+        if (!closed) {
+#pragma unroll
+            for (int q = 0; q < MAXC; ++q) {
+                const uint32_t col = lane + 32u * q;
+                if (col < D) bv[(tk * 2 + 1) * D + col] = cin[q] + bv[(tk * 2) * D + col];
+            }
+            __threadfence();
+            __syncwarp();
+            if (lane == 0) st_release(a.bflags + tk, 2u);
+        }
+        // carries: c_0 = cin; c_{j+1} = 0 if lo_{j+1} starts a segment, else piece_j (+ c_j when range j holds no start)
+#pragma unroll
+        for (int q = 0; q < MAXC; ++q) {
+            const uint32_t col = lane + 32u * q;
+            if (col >= D) continue;
+            Acc c = cin[q];
+            for (int j = 0; j < nr; ++j) {
+                const Acc p = cpc[static_cast<uint32_t>(j) * D + col];
+                cpc[static_cast<uint32_t>(j) * D + col] = c;
+                const int fl = gfl[j];
+                c = (j + 1 < nr && (gfl[j + 1] & 4)) ? Acc(0) : ((fl & 1) ? p : c + p);
+            }
+        }
+    }
+    __syncthreads();
+    // 4. scan of the range, the carry entering at lo
+    if (gib >= nr) return;  // this group only: nothing below synchronises lanes
+    const int32_t lo = glo[gib], hi = glo[gib + 1];
+    if (lo >= hi) return;
+    Acc carry[NE];
+#pragma unroll
+    for (int v = 0; v < VPL; ++v)
+#pragma unroll
+        for (int e = 0; e < EL; ++e) carry[v * EL + e] = cpc[static_cast<uint32_t>(gib) * D + (lig + v * L) * EL + e];
+    // rows rot .. hi-1 first (the piece rows just read), then lo .. rot-1
+    const int32_t rot = grot[gib];
+    const int32_t len = hi - lo, nA = hi - rot;
+    const int32_t offA = rot, offB = lo - nA;  // scan position of sequence index i: i + (i < nA ? offA : offB)
+    const int32_t inj = nA == len ? 0 : nA;    // sequence index of position lo
+    const KeyT kbr0 = rot > 0 ? kbase[dir * (rot - 1)] : ~kbase[dir * rot];
+    const KeyT kbrA = (nA < len && lo > 0) ? kbase[dir * (lo - 1)] : ~kbase[dir * lo];
     char* out = static_cast<char*>(a.out) + lig * static_cast<uint32_t>(EL * sizeof(OutT));
     uint8_t* omask = (a.out_mask != nullptr && lig == 0) ? a.out_mask : nullptr;
-    const uint32_t rbi = D * static_cast<uint32_t>(sizeof(InT));
     const uint32_t rbo = D * static_cast<uint32_t>(sizeof(OutT));
     const int32_t nb = (len + GS_U - 1) / GS_U;
     const uint32_t lane_slot = static_cast<uint32_t>(lane);
@@ -968,7 +987,6 @@ __global__ void __launch_bounds__(GS_WARPS * 32) k_group_scan(GsArgs a) {
         }
     };
     KeyT klast = KeyT(0);  // key of the row staged last
-    // stage block b into ring block b % GS_Q from its keys (always commits one group)
     auto stage = [&](int32_t b, const KeyT (&kb)[GS_U]) {
         if (b < nb) {
             const uint32_t slot0 = static_cast<uint32_t>(b % GS_Q) * GS_U;
@@ -1002,11 +1020,9 @@ __global__ void __launch_bounds__(GS_WARPS * 32) k_group_scan(GsArgs a) {
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
-
     Acc acc[NE];
 #pragma unroll
     for (int q = 0; q < NE; ++q) acc[q] = Acc(0);
-    // process block b (staged GS_Q - 1 blocks earlier)
     auto process = [&](int32_t b) {
         asm volatile("cp.async.wait_group %0;" ::"n"(GS_Q - 1) : "memory");
         const uint32_t slot0 = static_cast<uint32_t>(b % GS_Q) * GS_U;
@@ -1043,7 +1059,6 @@ __global__ void __launch_bounds__(GS_WARPS * 32) k_group_scan(GsArgs a) {
             }
         }
     };
-    // keys run two blocks ahead of staging, staging GS_Q - 1 blocks ahead of processing
     KeyT k0[GS_U], k1[GS_U];
 #pragma unroll
     for (int b = 0; b < GS_Q - 1; ++b) {
