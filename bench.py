@@ -362,6 +362,12 @@ def main():
             grads.append(gs)
         torch.autograd.backward(outs, grads)
 
+    # The clock sampler starts before the warm-up, so that the warm-up steps, not
+    # an idle pause, come right before the timed region (an idle GPU drops its
+    # clocks and the first timed step would pay for the ramp back up).
+    clocks = ClockSampler(gpu_uuid(dev))
+    clocks.start()
+    time.sleep(0.3)
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize(dev)
@@ -378,9 +384,6 @@ def main():
         records[name].append((e0, e1))
         return rc
 
-    clocks = ClockSampler(gpu_uuid(dev))
-    clocks.start()
-    time.sleep(0.3)
     barrier(world)
     torch.cuda.synchronize(dev)
     launches0 = L.kernel_launches()

@@ -8,8 +8,8 @@
  * caller owns every buffer: outputs, the "tape" that carries the sorted event
  * order from a forward call to its backward call, and per-call scratch.
  * Sizes of the tape and scratch come from ravel_tape_bytes() and
- * ravel_scratch_bytes().  Work is enqueued on `stream` and may be captured in
- * a CUDA graph.
+ * ravel_scratch_bytes().  Work is enqueued on `stream`; the entry points that
+ * take their tape and scratch from the caller may be captured in a CUDA graph.
  *
  * Layouts (all C-contiguous, element strides only):
  *   addresses     [B, T, C]         int32 or int64  (addr_dtype)
@@ -189,8 +189,8 @@ int ravel_cache_prefill(void* values, uint8_t* filled, const void* addr, int add
  * causal_sum_lookup forward for callers that cannot allocate device memory.
  * No counterpart in the reference: it exists for hosts that may not call
  * cudaMalloc or a caching allocator on this path -- plugin interfaces whose
- * enqueue step must not allocate, code running inside a CUDA-graph capture,
- * or foreign-language callers with no CUDA allocator of their own.  Same
+ * enqueue step must not allocate, or foreign-language callers with no CUDA
+ * allocator of their own.  Same
  * arguments and results as ravel_segsum_fwd, minus tape and scratch: both live
  * in one file-scope device array of RAVEL_NOALLOC_SCRATCH_BYTES that every GPU
  * loading this library holds until the process exits.  Returns

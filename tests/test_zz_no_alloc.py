@@ -1,9 +1,8 @@
 """The no-allocation entry point ``ravel_segsum_fwd_noalloc`` (GPU).
 
 Some hosts of this library cannot hand it device scratch: a plugin whose
-enqueue callback is not allowed to allocate, code that runs while a CUDA graph
-is being captured, or a caller in another language that has no CUDA
-allocator.  ``ravel_segsum_fwd_noalloc`` serves them by keeping its tape and
+enqueue callback is not allowed to allocate, or a caller in another language
+that has no CUDA allocator.  ``ravel_segsum_fwd_noalloc`` serves them by keeping its tape and
 scratch in a fixed-size device array inside the library.  This test calls it
 through the C ABI and checks it against the allocating ``ravel_segsum_fwd`` on
 two calls in a row with different sizes, flags and inputs (the array keeps the
