@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--no-general", action="store_true",
                     help="skip the extra timing of the general path (reads drawn apart from the writes)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip timing the reference's own functions on CUDA tensors (needs baseline/_ref)")
     ap.add_argument("--cpu-streams", type=int, default=8, help="streams in the CPU baseline sample")
     ap.add_argument("--batch", type=int, default=None, help="override B per GPU (small profiling cases)")
     ap.add_argument("--ops", choices=["all", "lk", "ss"], default="all",
@@ -375,9 +377,17 @@ def main():
     assert L.device_error(stream) == 0
 
     records = defaultdict(list)
+    # events made before the timed region, so that timing each entry point adds
+    # only two event records per call to the host's work
+    pool = [torch.cuda.Event(enable_timing=True) for _ in range(2 * 16 * args.steps)]
+    used = [0]
 
     def hook(name, thunk):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        i = used[0]
+        if i + 2 > len(pool):
+            return thunk()
+        used[0] = i + 2
+        e0, e1 = pool[i], pool[i + 1]
         e0.record()
         rc = thunk()
         e1.record()
@@ -429,6 +439,9 @@ def main():
     general = None
     if not args.no_general and cfg.addressing == "zipf":
         general = run_general(cfg, x, dev, world)
+    ref_gpu = None
+    if world == 1 and not args.no_reference_gpu:
+        ref_gpu = run_reference_gpu(cfg, x, dev, steps=5, warmup=args.warmup)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = run_cpu_baseline(cfg, 1, 1, args.cpu_streams)
@@ -449,7 +462,7 @@ def main():
             "step_roofline": {"algorithmic_bytes": step_bytes, "achieved_gbs": step_bytes / (ms * 1e-3) / 1e9,
                               "frac": step_bytes / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], "peak": peaks["hbm_gbs"]},
             "roofline": roofline, "kernels": kernels, "e2e": e2e, "cpu_baseline": cpu, "decode": decode,
-            "general_path": general,
+            "general_path": general, "reference_gpu": ref_gpu,
             "clocks": clk, "gpu_launches": launches,
         }
         print(json.dumps(line), flush=True)
@@ -479,6 +492,50 @@ def load_traffic(kernel: str, cfg):
         return None if ent is None else float(ent)
     except (ValueError, OSError):
         return None
+
+
+def run_reference_gpu(cfg, x, dev, steps: int = 5, warmup: int = 3) -> dict:
+    """The reference's own causal_last_k_lookup + causal_sum_lookup (torch CUDA ops,
+    ravel_memory.py:52-241) on the same CUDA inputs, forward + backward through
+    autograd: the GPU comparator of the benchmark plan.  It runs from an installed
+    copy of the reference under baseline/_ref (pip install --no-deps --target
+    baseline/_ref <reference>), never from the reference's source tree."""
+    import torch
+    ref = ROOT / "baseline" / "_ref"
+    if not (ref / "ravel_lm" / "ravel_memory.py").exists():
+        return {"unavailable": "baseline/_ref holds no installed reference"}
+    sys.path.insert(0, str(ref))
+    try:
+        from ravel_lm.ravel_memory import causal_last_k_lookup as ref_lk, causal_sum_lookup as ref_ss
+    except Exception as exc:  # an install that does not import is reported, not fatal
+        return {"unavailable": f"import of the installed reference failed: {exc}"[:200]}
+    finally:
+        sys.path.remove(str(ref))
+    w, r = x["write"], x["read"]
+    p = x["payload"].detach().clone().requires_grad_(True)
+    gv, gs = x["g_vals"], x["g_sums"]
+
+    def step():
+        p.grad = None
+        vals, _m = ref_lk(w, p, r, address_space=cfg.A, k=cfg.k)
+        sums, _s = ref_ss(w, p, r, address_space=cfg.A)
+        torch.autograd.backward([vals, sums], [gv, gs])
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize(dev)
+    ms = t0.elapsed_time(t1) / steps
+    del p
+    torch.cuda.empty_cache()
+    return {"path": "reference ravel_lm.ravel_memory on CUDA tensors (torch ops), forward + backward",
+            "ms_per_step": ms, "value": cfg.tokens / (ms * 1e-3), "unit": "tokens/s", "steps": steps,
+            "warmup": warmup}
 
 
 def run_general(cfg, x, dev, world, steps: int = 5) -> dict:

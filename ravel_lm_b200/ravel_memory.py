@@ -10,9 +10,10 @@ the reference module (``ravel_lm/ravel_memory.py:16-292``):
 * ``RavelLayerCache(values, filled)`` with ``empty``, ``read``, ``write``.
 
 The computation runs in the CUDA library ``libravel_b200.so`` (C ABI in
-``include/ravel_b200.h``), reached through ctypes.  The two lookups are
-``torch.library`` custom ops with fake (meta) implementations and autograd
-formulas, so they work under autograd, ``torch.compile`` and CUDA-graph
+``include/ravel_b200.h``), reached through ctypes.  In eager mode the two
+lookups are ``torch.autograd.Function``s (the least host time per call); under
+``torch.compile`` they are ``torch.library`` custom ops with fake (meta)
+implementations and the same autograd formulas.  Both work under CUDA-graph
 capture.  Tensors must live on a CUDA device: there is no CPU path and no
 fallback.
 
@@ -28,6 +29,7 @@ Differences from the reference that a caller can observe:
 """
 from __future__ import annotations
 
+import functools
 from dataclasses import dataclass
 from typing import Optional, Tuple
 
@@ -110,10 +112,12 @@ def _ptr(t: Optional[Tensor]) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
 
+@functools.lru_cache(maxsize=256)
 def tape_bytes(B: int, T: int, C: int, A: int, flags: int) -> int:
     return int(_lib.load().ravel_tape_bytes(B, T, C, A, flags))
 
 
+@functools.lru_cache(maxsize=256)
 def scratch_bytes(B: int, T: int, C: int, D: int, A: int, k: int, dtype_code: int, flags: int) -> int:
     return int(_lib.load().ravel_scratch_bytes(B, T, C, D, A, k, dtype_code, flags))
 
@@ -204,9 +208,8 @@ def _build_tape(write: Tensor, read: Optional[Tensor], write_mask: Optional[Tens
 
 
 # ------------------------------------------------------------------ latest-k custom ops
-@torch.library.custom_op("ravel_b200::latestk_fwd", mutates_args=())
-def _latestk_fwd(write: Tensor, payload: Tensor, read: Optional[Tensor], write_mask: Optional[Tensor],
-                 address_space: int, k: int) -> Tuple[Tensor, Tensor, Tensor]:
+def _latestk_fwd_impl(write: Tensor, payload: Tensor, read: Optional[Tensor], write_mask: Optional[Tensor],
+                      address_space: int, k: int) -> Tuple[Tensor, Tensor, Tensor]:
     B, T, C = write.shape
     D = payload.shape[-1]
     device = _require_cuda(write, payload, read, write_mask)
@@ -221,6 +224,12 @@ def _latestk_fwd(write: Tensor, payload: Tensor, read: Optional[Tensor], write_m
     return vals, mask, tape
 
 
+@torch.library.custom_op("ravel_b200::latestk_fwd", mutates_args=())
+def _latestk_fwd(write: Tensor, payload: Tensor, read: Optional[Tensor], write_mask: Optional[Tensor],
+                 address_space: int, k: int) -> Tuple[Tensor, Tensor, Tensor]:
+    return _latestk_fwd_impl(write, payload, read, write_mask, address_space, k)
+
+
 @_latestk_fwd.register_fake
 def _latestk_fwd_fake(write, payload, read, write_mask, address_space, k):
     B, T, C = write.shape
@@ -231,9 +240,8 @@ def _latestk_fwd_fake(write, payload, read, write_mask, address_space, k):
             torch.empty(tape_bytes(B, T, C, address_space, flags), dtype=torch.uint8, device=payload.device))
 
 
-@torch.library.custom_op("ravel_b200::latestk_bwd", mutates_args=())
-def _latestk_bwd(tape: Tensor, grad_vals: Tensor, raddr: Tensor, flags: int, B: int, T: int, C: int,
-                 address_space: int, k: int) -> Tensor:
+def _latestk_bwd_impl(tape: Tensor, grad_vals: Tensor, raddr: Tensor, flags: int, B: int, T: int, C: int,
+                      address_space: int, k: int) -> Tensor:
     D = grad_vals.shape[-1]
     device = _require_cuda(tape, grad_vals)
     g = grad_vals.contiguous()
@@ -245,6 +253,12 @@ def _latestk_bwd(tape: Tensor, grad_vals: Tensor, raddr: Tensor, flags: int, B: 
               g.data_ptr(), _payload_code(g), B, T, C, D, address_space, k, grad.data_ptr(), scratch.data_ptr(),
               scratch.numel(), _stream(device))
     return grad
+
+
+@torch.library.custom_op("ravel_b200::latestk_bwd", mutates_args=())
+def _latestk_bwd(tape: Tensor, grad_vals: Tensor, raddr: Tensor, flags: int, B: int, T: int, C: int,
+                 address_space: int, k: int) -> Tensor:
+    return _latestk_bwd_impl(tape, grad_vals, raddr, flags, B, T, C, address_space, k)
 
 
 @_latestk_bwd.register_fake
@@ -274,9 +288,8 @@ _latestk_fwd.register_autograd(_latestk_backward, setup_context=_latestk_setup)
 
 
 # ------------------------------------------------------------------ sum custom ops
-@torch.library.custom_op("ravel_b200::segsum_fwd", mutates_args=())
-def _segsum_fwd(write: Tensor, payload: Tensor, read: Optional[Tensor], write_mask: Optional[Tensor],
-                address_space: int) -> Tuple[Tensor, Tensor, Tensor]:
+def _segsum_fwd_impl(write: Tensor, payload: Tensor, read: Optional[Tensor], write_mask: Optional[Tensor],
+                     address_space: int) -> Tuple[Tensor, Tensor, Tensor]:
     B, T, C = write.shape
     D = payload.shape[-1]
     device = _require_cuda(write, payload, read, write_mask)
@@ -291,6 +304,12 @@ def _segsum_fwd(write: Tensor, payload: Tensor, read: Optional[Tensor], write_ma
     return sums, mask, tape
 
 
+@torch.library.custom_op("ravel_b200::segsum_fwd", mutates_args=())
+def _segsum_fwd(write: Tensor, payload: Tensor, read: Optional[Tensor], write_mask: Optional[Tensor],
+                address_space: int) -> Tuple[Tensor, Tensor, Tensor]:
+    return _segsum_fwd_impl(write, payload, read, write_mask, address_space)
+
+
 @_segsum_fwd.register_fake
 def _segsum_fwd_fake(write, payload, read, write_mask, address_space):
     B, T, C = write.shape
@@ -301,9 +320,8 @@ def _segsum_fwd_fake(write, payload, read, write_mask, address_space):
             torch.empty(tape_bytes(B, T, C, address_space, flags), dtype=torch.uint8, device=payload.device))
 
 
-@torch.library.custom_op("ravel_b200::segsum_bwd", mutates_args=())
-def _segsum_bwd(tape: Tensor, grad_sums: Tensor, raddr: Tensor, flags: int, B: int, T: int, C: int,
-                address_space: int) -> Tensor:
+def _segsum_bwd_impl(tape: Tensor, grad_sums: Tensor, raddr: Tensor, flags: int, B: int, T: int, C: int,
+                     address_space: int) -> Tensor:
     D = grad_sums.shape[-1]
     device = _require_cuda(tape, grad_sums)
     g = grad_sums.contiguous()
@@ -315,6 +333,12 @@ def _segsum_bwd(tape: Tensor, grad_sums: Tensor, raddr: Tensor, flags: int, B: i
               g.data_ptr(), _payload_code(g), B, T, C, D, address_space, grad.data_ptr(), scratch.data_ptr(),
               scratch.numel(), _stream(device))
     return grad
+
+
+@torch.library.custom_op("ravel_b200::segsum_bwd", mutates_args=())
+def _segsum_bwd(tape: Tensor, grad_sums: Tensor, raddr: Tensor, flags: int, B: int, T: int, C: int,
+                address_space: int) -> Tensor:
+    return _segsum_bwd_impl(tape, grad_sums, raddr, flags, B, T, C, address_space)
 
 
 @_segsum_bwd.register_fake
@@ -340,6 +364,49 @@ def _segsum_backward(ctx, grad_sums, _gm, _gt):
 
 
 _segsum_fwd.register_autograd(_segsum_backward, setup_context=_segsum_setup)
+
+
+# ------------------------------------------------------------------ eager autograd functions
+# Outside torch.compile the public functions call these instead of the custom
+# ops: same implementation functions, same saved tensors and gradients, without
+# the custom-op dispatch (tens of microseconds of host time per call, which
+# decides the step time whenever the kernels are short).
+class _LatestKFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, write, payload, read, write_mask, address_space, k):
+        vals, mask, tape = _latestk_fwd_impl(write, payload, read, write_mask, address_space, k)
+        ctx.save_for_backward(tape, write if read is None else read)
+        ctx.meta = (_flags(read, write_mask), *write.shape, int(address_space), int(k))
+        ctx.mark_non_differentiable(mask)
+        ctx.set_materialize_grads(False)
+        return vals, mask
+
+    @staticmethod
+    def backward(ctx, grad_vals, _gm):
+        if grad_vals is None:
+            return None, None, None, None, None, None
+        tape, raddr = ctx.saved_tensors
+        flags, B, T, C, A, k = ctx.meta
+        return None, _latestk_bwd_impl(tape, grad_vals, raddr, flags, B, T, C, A, k), None, None, None, None
+
+
+class _SegSumFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, write, payload, read, write_mask, address_space):
+        sums, mask, tape = _segsum_fwd_impl(write, payload, read, write_mask, address_space)
+        ctx.save_for_backward(tape, write if read is None else read)
+        ctx.meta = (_flags(read, write_mask), *write.shape, int(address_space))
+        ctx.mark_non_differentiable(mask)
+        ctx.set_materialize_grads(False)
+        return sums, mask
+
+    @staticmethod
+    def backward(ctx, grad_sums, _gm):
+        if grad_sums is None:
+            return None, None, None, None, None
+        tape, raddr = ctx.saved_tensors
+        flags, B, T, C, A = ctx.meta
+        return None, _segsum_bwd_impl(tape, grad_sums, raddr, flags, B, T, C, A), None, None, None
 
 
 # ------------------------------------------------------------------ public API
@@ -389,8 +456,10 @@ def causal_last_k_lookup(
     if B * T * C == 0:
         return payloads.new_zeros(B, T, C, k, payloads.shape[-1]), torch.zeros(
             B, T, C, k, dtype=torch.bool, device=payloads.device)
-    vals, mask, _tape = _latestk_fwd(write_addresses, payloads, read, write_mask, int(address_space), int(k))
-    return vals, mask
+    if torch.compiler.is_compiling():
+        vals, mask, _tape = _latestk_fwd(write_addresses, payloads, read, write_mask, int(address_space), int(k))
+        return vals, mask
+    return _LatestKFn.apply(write_addresses, payloads, read, write_mask, int(address_space), int(k))
 
 
 def causal_sum_lookup(
@@ -422,8 +491,10 @@ def causal_sum_lookup(
     if B * T * C == 0:
         return payloads.new_zeros(B, T, C, payloads.shape[-1]), torch.zeros(
             B, T, C, dtype=torch.bool, device=payloads.device)
-    sums, mask, _tape = _segsum_fwd(write_addresses, payloads, read, write_mask, int(address_space))
-    return sums, mask
+    if torch.compiler.is_compiling():
+        sums, mask, _tape = _segsum_fwd(write_addresses, payloads, read, write_mask, int(address_space))
+        return sums, mask
+    return _SegSumFn.apply(write_addresses, payloads, read, write_mask, int(address_space))
 
 
 # ------------------------------------------------------------------ decode cache
