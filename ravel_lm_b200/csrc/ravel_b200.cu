@@ -163,8 +163,10 @@ RangePlan range_plan(int64_t S, int64_t T, int64_t slots, int64_t rl_max = int64
 
 // Range-scan launch shape (overridable at build time for sweeps): blocks for
 // RAVEL_RS_WAVES waves of resident blocks, so that blocks at different phases
-// (piece sums, look-back, scan) share an SM; ranges of at least RAVEL_RS_RLMIN
-// positions, more than the 32-position snap window so that none is empty.
+// (piece sums, look-back, scan) share an SM.  Ranges hold at least 64
+// positions, or down to RAVEL_RS_RLMIN when 64-position ranges would not fill
+// one wave of blocks (short streams); the snap window is at most half a range,
+// so that no range is empty.
 // Measured at config 3 (sum forward / backward, µs): 1 wave 197 / 183,
 // 2 waves 173 / 170, 3 waves 167 / 158-166; 2-warp blocks, 48-position ranges
 // and a deeper ring were no faster.
@@ -172,9 +174,9 @@ RangePlan range_plan(int64_t S, int64_t T, int64_t slots, int64_t rl_max = int64
 #define RAVEL_RS_WAVES 3
 #endif
 #ifndef RAVEL_RS_RLMIN
-#define RAVEL_RS_RLMIN 64
+#define RAVEL_RS_RLMIN 16
 #endif
-static_assert(RAVEL_RS_RLMIN > 32 && RAVEL_RS_RLMIN <= 64 && RAVEL_RS_RLMIN % 8 == 0, "ranges outgrow the snap window");
+static_assert(RAVEL_RS_RLMIN >= 16 && RAVEL_RS_RLMIN <= 64 && RAVEL_RS_RLMIN % 8 == 0, "range length floor");
 int64_t max_ranges(int64_t T) { return T > 0 ? (T + RAVEL_RS_RLMIN - 1) / RAVEL_RS_RLMIN : 1; }
 
 int sm_count() {
@@ -644,11 +646,17 @@ int launch_segscan(const TapeView& tv, const TapeLayout& tl, int64_t B, int64_t 
                 occ < 1)
                 occ = 1;
             // one range per lane group; whole blocks per stream, RAVEL_RS_WAVES waves of blocks
-            int64_t bps = static_cast<int64_t>(occ) * sm_count() * RAVEL_RS_WAVES / (B * C > 0 ? B * C : 1);
+            // Short streams (64-position ranges do not fill one wave): about two
+            // blocks per SM, ranges down to RAVEL_RS_RLMIN positions.
+            const int64_t S = B * C > 0 ? B * C : 1;
+            const int64_t blocks64 = S * (((T + 63) / 64 + gpb - 1) / gpb);
+            const bool short_streams = blocks64 < static_cast<int64_t>(occ) * sm_count();
+            int64_t bps = short_streams ? 2 * sm_count() / S : static_cast<int64_t>(occ) * sm_count() * RAVEL_RS_WAVES / S;
             if (bps < 1) bps = 1;
-            const RangePlan rp = range_plan(1, T, bps * gpb, kRlMax, RAVEL_RS_RLMIN);
+            const RangePlan rp = range_plan(1, T, bps * gpb, kRlMax, short_streams ? RAVEL_RS_RLMIN : 64);
             ga.R = rp.R;
             ga.RL = rp.RL;
+            ga.snap = static_cast<int>(rp.RL / 2 < GS_SNAP ? rp.RL / 2 : GS_SNAP);
             ga.CB = (rp.R + gpb - 1) / gpb;
             ga.bmw = static_cast<int>(gpb * rp.RL / 32 + 2);
             ga.bflags = reinterpret_cast<unsigned*>(sc + sl.off_bflags);
