@@ -466,7 +466,10 @@ int lk_fwd_tape(const void* tape, int flags, const void* raddr, int addr_dtype, 
                 } else {
                     if (!tl.general) {
                         int64_t P = 40960 / (a.row_bytes + 16) - k;
-                        if (P > 128) P = 128;
+#ifndef RAVEL_LK_PMAX
+#define RAVEL_LK_PMAX 128
+#endif
+                        if (P > RAVEL_LK_PMAX) P = RAVEL_LK_PMAX;
                         if (P < 16) P = 16;
                         a.P = static_cast<int>(P);
                         a.nchunks = (T + P - 1) / P;
@@ -802,28 +805,33 @@ int ss_bwd(const void* tape, int flags, const void* raddr, int addr_dtype, const
             if (tl.has_mask &&
                 cudaMemsetAsync(grad_payload, 0, static_cast<size_t>(N) * D * elem_bytes(DT), st) != cudaSuccess)
                 return RAVEL_ERR_CUDA;
-            // read gradients gathered at their latest write over the read tape when a
-            // row splits into 2^m <= 32 vectors; otherwise atomics
-            const int gvb = pick_vec_bytes(D * elem_bytes(DT), addr_bits(grad_sums));
+            // rows of 2^m <= 32 vectors: a reverse inclusive scan of the read
+            // gradients over the read tape (suffix sums per address, payload dtype,
+            // in accbuf), then each write copies the suffix at its first read
+            // ranked at or after it; otherwise atomics
+            const int gvb = pick_vec_bytes(D * elem_bytes(DT), addr_bits(grad_sums) | addr_bits(grad_payload));
             const int64_t grv = D * elem_bytes(DT) / gvb;
             if (grv >= 1 && grv <= 32 && (grv & (grv - 1)) == 0) {
+                TapeView rv = tv;
+                rv.keys = tv.rkeys;
+                rv.nvalid = nullptr;  // every read is on the read tape
+                if (int e = launch_segscan<KeyT, DT>(rv, tl, B, T, C, D, grad_sums, 0, accbuf, 1, nullptr,
+                                                     /*inclusive=*/1, /*reverse=*/1, scratch, sl, st))
+                    return e;
                 int lsh = 0;
                 while ((int64_t{1} << lsh) < grv) ++lsh;
                 const int64_t warps = (B * C * T + (32 >> lsh) - 1) / (32 >> lsh);
-                int e = with_vb(gvb, [&](auto vbc) -> int {
+                return with_vb(gvb, [&](auto vbc) -> int {
                     constexpr int VB = decltype(vbc)::value;
                     if constexpr (!vb_ok<DT, VB>()) {
                         return RAVEL_ERR_INVALID_ARG;
                     } else {
-                        k_ss_bwd_gather<KeyT, DT, VB><<<grid_cap((warps * 32 + 255) / 256), 256, 0, st>>>(
+                        k_ss_bwd_suffix<KeyT, DT, VB><<<grid_cap((warps * 32 + 255) / 256), 256, 0, st>>>(
                             static_cast<const KeyT*>(tv.keys), static_cast<const KeyT*>(tv.rkeys), tv.bstart, tv.nvalid,
-                            grad_sums, accbuf, B * C, T, C, D, tl.kl.tbits, lsh);
+                            accbuf, grad_payload, B * C, T, C, D, tl.kl.tbits, lsh);
                         return check_launch();
                     }
                 });
-                if (e) return e;
-                return launch_segscan<KeyT, DT>(tv, tl, B, T, C, D, accbuf, 1, grad_payload, 0, nullptr, 1, 1,
-                                                scratch, sl, st);
             }
             if (cudaMemsetAsync(accbuf, 0, acc_sz, st) != cudaSuccess) return RAVEL_ERR_CUDA;
             SsGenArgs g;

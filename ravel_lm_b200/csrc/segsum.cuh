@@ -1215,17 +1215,20 @@ __global__ void __launch_bounds__(256) k_ss_scatter(SsGenArgs a) {
     }
 }
 
-// General sum backward, first half, as a gather (no atomics, deterministic):
-// accbuf[s*T + q] = the sum of grad_sums over the reads of q's address whose
-// latest earlier write is q (in bucket q of the read tape); zero rows past nvalid.  A group of 2^lshift
-// lanes takes one tape position, a lane one VB-byte vector of the gradient row.
+// General sum backward, second half.  The first half is a reverse inclusive
+// segmented scan over the *read* tape (reads sorted by (address, t)), which
+// leaves at each sorted read the sum of the gradients of itself and of every
+// later read of its address, in the payload dtype.  The reads whose latest
+// valid write is at or after write q are, among the reads of q's address,
+// exactly those from the first read ranked >= q to the end of that address:
+// grad_payload[write q] = suffix[bs[q + 1]] when that read has q's address,
+// else zero (ravel_memory.py:223-240 through autograd).  One lane group per
+// write; a row copy.
 template <typename KeyT, int DT, int VB>
-__global__ void __launch_bounds__(256) k_ss_bwd_gather(const KeyT* wkeys, const KeyT* rkeys, const int32_t* bstart,
-                                                       const int* nvalid, const void* grad, void* accbuf, int64_t S,
+__global__ void __launch_bounds__(256) k_ss_bwd_suffix(const KeyT* wkeys, const KeyT* rkeys, const int32_t* bstart,
+                                                       const int* nvalid, const void* suffix, void* grad, int64_t S,
                                                        int64_t T, int64_t C, int64_t D, int tbits, int lshift) {
-    using E = Elem<DT>;
-    using Acc = typename E::Acc;
-    using V = typename E::T;
+    using V = typename Elem<DT>::T;
     constexpr int EPV = VB / static_cast<int>(sizeof(V));
     const int lane = threadIdx.x & 31;
     const uint32_t L = 1u << lshift;
@@ -1234,44 +1237,17 @@ __global__ void __launch_bounds__(256) k_ss_bwd_gather(const KeyT* wkeys, const 
     const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
     const KeyT tmask = (static_cast<KeyT>(1) << tbits) - 1;
-    const V* g = static_cast<const V*>(grad);
     for (int64_t gi = warp0 * gpw + grp; gi < S * T; gi += nwarps * gpw) {
         const int64_t s = gi / T, q = gi - s * T;
         const int64_t n_s = nvalid ? nvalid[s] : T;
+        if (q >= n_s) continue;  // masked writes: their rows were zeroed before
+        const KeyT wk = wkeys[gi];
+        const int32_t i = bstart[s * (T + 2) + q + 1];
+        const bool valid = i < T && (rkeys[s * T + i] >> tbits) == (wk >> tbits);
+        uint4 x = make_uint4(0u, 0u, 0u, 0u);
+        if (valid) x = ldg_vec<VB>(static_cast<const V*>(suffix) + (s * T + i) * D + lig * EPV);
         const RowMap rows_of(s, T, C);
-        Acc acc[EPV];
-#pragma unroll
-        for (int e = 0; e < EPV; ++e) acc[e] = Acc(0);
-        if (q < n_s) {
-            const int32_t* bs = bstart + s * (T + 2);
-            const KeyT* rk = rkeys + s * T;
-            const KeyT aq = wkeys[s * T + q] >> tbits;
-            const int32_t i1 = bs[q + 2];
-            for (int32_t i = bs[q + 1]; i < i1; i += 4) {  // 4 reads' loads in flight
-                uint32_t rrow[4];
-                bool use[4];
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const KeyT key = i + u < i1 ? rk[i + u] : KeyT(0);
-                    rrow[u] = rows_of(key & tmask);
-                    use[u] = i + u < i1 && (key >> tbits) == aq;  // a read of q's own address
-                }
-                uint4 x[4];
-#pragma unroll
-                for (int u = 0; u < 4; ++u)
-                    x[u] = use[u] ? ldg_vec<VB>(g + static_cast<uint64_t>(rrow[u]) * D + lig * EPV)
-                                  : make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const V* xv = reinterpret_cast<const V*>(&x[u]);
-#pragma unroll
-                    for (int e = 0; e < EPV; ++e) acc[e] += E::to_acc(xv[e]);
-                }
-            }
-        }
-        Acc* dst = static_cast<Acc*>(accbuf) + gi * D + lig * EPV;
-#pragma unroll
-        for (int e = 0; e < EPV; ++e) dst[e] = acc[e];
+        st_vec<VB>(static_cast<V*>(grad) + static_cast<uint64_t>(rows_of(wk & tmask)) * D + lig * EPV, x);
     }
 }
 
