@@ -16,7 +16,7 @@
 // elements is one contiguous streaming store.
 //
 // General reads or a write mask: each read's latest index comes from
-// k_read_ranks; the forward takes reads in their original order so the output
+// k_merge_ranks; the forward takes reads in their original order so the output
 // is written sequentially, and gathers the candidate rows directly; the backward
 // gathers over the read tape (k_lk_bwd_gather).
 #pragma once

@@ -399,11 +399,10 @@ int tape_build(const void* waddr, const void* raddr, int addr_dtype, const uint8
             ra.nvalid = nullptr;
             ra.mbit = 0;
             if (int e3 = sort_streams<KeyT>(ra, tv.rkeys, other, S, T, st)) return e3;
-            k_read_ranks<KeyT><<<grid_cap((S * ((T + 7) / 8) + 255) / 256), 256, 0, st>>>(
+            const int64_t per = (2 * T + MR_K - 1) / MR_K + 1;
+            k_merge_ranks<KeyT><<<grid_cap((S * per + 255) / 256), 256, 0, st>>>(
                 static_cast<const KeyT*>(tv.keys), tv.nvalid, static_cast<const KeyT*>(tv.rkeys), S, T, C,
-                tl.kl.tbits, tv.rridx, tv.ridx);
-            if (int e3 = check_launch()) return e3;
-            k_bucket_starts<<<grid_cap((S * (T + 1) + 255) / 256), 256, 0, st>>>(tv.rridx, S, T, tv.bstart);
+                tl.kl.tbits, tv.rridx, tv.ridx, tv.bstart);
             if (int e3 = check_launch()) return e3;
         }
         return RAVEL_OK;

@@ -14,9 +14,10 @@
 //                 warp, warp-private digit histograms and a block-wide scan.
 //   k_merge       merge-path merge of sorted runs for streams longer than a
 //                 tile (log2(tiles) passes, global memory ping-pong).
-//   k_read_ranks  general tapes: the reads sorted like the writes, then each
-//                 ranked against the sorted writes = searchsorted(right=True)-1 of
-//                 ravel_memory.py:159, restricted to the stream.
+//   k_merge_ranks general tapes: the reads sorted like the writes, then merged
+//                 with the sorted writes; each read's rank = searchsorted(right=
+//                 True)-1 of ravel_memory.py:159, restricted to the stream, and
+//                 each write's first read ranked at or after it.
 #pragma once
 
 #include <cooperative_groups.h>
@@ -390,53 +391,58 @@ __global__ void k_stream_offsets(const int* __restrict__ nvalid, int64_t* __rest
     if (threadIdx.x == 0) soff[S] = carry;
 }
 
-// Read tape ranks (ravel_memory.py:153-159 restricted to the read's stream):
-// the reads of every stream, sorted by (address, t) like the writes, each get the
-// index of the latest valid write below them in that order (any address), -1 if
-// none: rridx[s][i] for sorted read i, and ridx[r] for the read's flat row r.  The
-// ranks are non-decreasing along the sorted reads, so a thread takes 8
-// consecutive reads and bounds each binary search below by the previous rank.
+// Read ranks and bucket starts in one pass: the merge of a stream's sorted
+// writes W (its valid ones, n) and sorted reads R, a read placed before a write
+// of equal key.  A read's rank is then the number of writes merged before it,
+// minus one (searchsorted(right=True)-1 of ravel_memory.py:159, restricted to
+// the stream: the latest valid write strictly below it), and bstart[j + 1] for
+// write j is the number of reads merged before it.  Each thread merges MR_K
+// consecutive elements of the merged order from its merge-path co-rank (a binary
+// search on its diagonal); bstart[0] = 0 and bstart[n + 1 .. T + 1] = T.
+constexpr int MR_K = 16;
 template <typename KeyT>
-__global__ void __launch_bounds__(256) k_read_ranks(const KeyT* wkeys, const int* nvalid, const KeyT* rkeys,
+__global__ void __launch_bounds__(256) k_merge_ranks(const KeyT* wkeys, const int* nvalid, const KeyT* rkeys,
                                                    int64_t S, int64_t T, int64_t C, int tbits, int32_t* rridx,
-                                                   int32_t* ridx) {
+                                                   int32_t* ridx, int32_t* bstart) {
     const KeyT tmask = (static_cast<KeyT>(1) << tbits) - 1;
-    const int64_t per = (T + 7) / 8;
+    const int64_t per = (2 * T + MR_K - 1) / MR_K + 1;  // chunks of the longest merge, plus one for the tail
     for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < S * per;
          e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t s = e / per, i0 = (e - s * per) * 8;
-        const KeyT* wk = wkeys + s * T;
-        const KeyT* rk = rkeys + s * T;
+        const int64_t s = e / per, chunk = e - s * per;
         const int64_t n = nvalid ? nvalid[s] : T;
-        const int64_t b = s / C, c = s - b * C;
-        int64_t lo = 0;
-        const int64_t i1 = i0 + 8 < T ? i0 + 8 : T;
-        for (int64_t i = i0; i < i1; ++i) {
-            const KeyT q = rk[i];
-            int64_t hi = n;
-            while (lo < hi) {
-                const int64_t mid = (lo + hi) >> 1;
-                if (wk[mid] < q) lo = mid + 1; else hi = mid;
-            }
-            rridx[s * T + i] = static_cast<int32_t>(lo - 1);
-            ridx[(b * T + static_cast<int64_t>(q & tmask)) * C + c] = static_cast<int32_t>(lo - 1);
+        const KeyT* W = wkeys + s * T;
+        const KeyT* R = rkeys + s * T;
+        int32_t* bs = bstart + s * (T + 2);
+        const int64_t M = n + T;
+        if (chunk == per - 1) {  // bstart[0] and the entries past the last valid write
+            bs[0] = 0;
+            for (int64_t j = n + 1; j <= T + 1; ++j) bs[j] = static_cast<int32_t>(T);
+            continue;
         }
-    }
-}
-
-// Read tape bucket starts: bstart[s][j] = the number of stream s's sorted reads
-// whose rank + 1 is below j, j = 0..T+1.  The reads whose latest valid write
-// (any address) is q are the sorted reads bstart[q+1] .. bstart[q+2].  Thread
-// (s, i) fills the starts between sorted reads i-1 and i (i = T: the end), so
-// every entry is written once.
-__global__ void __launch_bounds__(256) k_bucket_starts(const int32_t* rridx, int64_t S, int64_t T, int32_t* bstart) {
-    for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < S * (T + 1);
-         e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t s = e / (T + 1), i = e - s * (T + 1);
-        const int32_t* r = rridx + s * T;
-        const int64_t lo = i > 0 ? static_cast<int64_t>(r[i - 1]) + 2 : 0;
-        const int64_t hi = i < T ? static_cast<int64_t>(r[i]) + 1 : T + 1;
-        for (int64_t j = lo; j <= hi; ++j) bstart[s * (T + 2) + j] = static_cast<int32_t>(i);
+        const int64_t d = chunk * MR_K;
+        if (d >= M) continue;
+        // co-rank: the largest i (reads among the first d merged) with R[i-1] <= W[d-i]
+        int64_t lo = d - n > 0 ? d - n : 0, hi = d < T ? d : T;
+        while (lo < hi) {
+            const int64_t mid = (lo + hi + 1) >> 1;
+            const int64_t j = d - mid;
+            if (j >= n || R[mid - 1] <= W[j]) lo = mid;
+            else hi = mid - 1;
+        }
+        int64_t i = lo, j = d - lo;
+        const int64_t b = s / C, c = s - b * C;
+        const int64_t dend = d + MR_K < M ? d + MR_K : M;
+        for (int64_t x = d; x < dend; ++x) {
+            if (i < T && (j >= n || R[i] <= W[j])) {
+                const KeyT q = R[i];
+                rridx[s * T + i] = static_cast<int32_t>(j - 1);
+                ridx[(b * T + static_cast<int64_t>(q & tmask)) * C + c] = static_cast<int32_t>(j - 1);
+                ++i;
+            } else {
+                bs[j + 1] = static_cast<int32_t>(i);
+                ++j;
+            }
+        }
     }
 }
 
