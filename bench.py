@@ -3,7 +3,7 @@
 
 One step = the operator's full training pass on one batch of synthetic input:
 causal_last_k_lookup + causal_sum_lookup forward and backward, through the
-public drop-in API (autograd), on BASELINE configuration 3 by default
+public drop-in API (autograd), on benchmark configuration 3 by default
 (B=4 T=32768 H=16 D=64 bf16, k=8, Zipf(1.05) addresses over 65536).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]

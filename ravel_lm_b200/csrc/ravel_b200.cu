@@ -271,8 +271,9 @@ int set_smem(K kernel, size_t bytes) {
 
 uintptr_t addr_bits(const void* p) { return reinterpret_cast<uintptr_t>(p); }
 
+// Grid-stride kernels: at most 64 blocks per SM of the current device.
 int grid_cap(int64_t blocks) {
-    const int64_t cap = 148 * 64;
+    const int64_t cap = static_cast<int64_t>(sm_count()) * 64;
     return static_cast<int>(blocks < 1 ? 1 : (blocks > cap ? cap : blocks));
 }
 

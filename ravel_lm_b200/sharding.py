@@ -20,6 +20,10 @@ Replicated outputs are optional (``gather_outputs``): one
 group (NCCL over NVLink on GPUs, gloo on CPU) and a local reorder back to the
 full layout.
 
+The reference's int64 -> int32 address truncation depends on the size of the
+whole call (ravel_lm/ravel_memory.py:45-49); ``sharded_lookup`` applies the
+whole problem's rule to every shard.
+
 Sharded results equal the unsharded ones as values.  The one bit that can
 differ is the sign of an invalid latest-k slot at the very start of a stream:
 the reference fills such a slot with candidate*0, where the candidate is the
@@ -117,22 +121,62 @@ def gather_outputs(local: torch.Tensor, shard: StreamShard, group=None) -> torch
     return full.view(torch.bool) if is_bool else full
 
 
+def _global_fold(addr: Optional[torch.Tensor], shard: StreamShard, T: int, A: int) -> Optional[torch.Tensor]:
+    """Addresses of one shard, reduced with the FULL problem's key-width rule.
+
+    The reference converts int64 addresses to its composite key dtype before
+    the floor modulo (ravel_lm/ravel_memory.py:126-128), and that dtype depends
+    on B*C*A*(T+1) of the whole call (:45-49).  A shard has a smaller B*C and can
+    fall under the int32 bound where the full problem does not; the library
+    would then truncate int64 addresses to 32 bits that the reference keeps.
+    When the two rules differ, the shard's int64 addresses are reduced here
+    with the full problem's rule (no truncation, floor modulo of A), which both
+    rules then leave unchanged.
+    """
+    from .ravel_memory import _composite_key_dtype
+    if addr is None or addr.dtype != torch.int64:
+        return addr
+    full = _composite_key_dtype(shard.B, T, shard.C, A)
+    local = _composite_key_dtype(shard.b1 - shard.b0, T, shard.c1 - shard.c0, A)
+    if full == local:
+        return addr
+    return addr.remainder(int(A))
+
+
 def sharded_lookup(write_addresses: torch.Tensor, payloads: torch.Tensor, read_addresses=None, *,
                    address_space: int, k: int = 1, write_mask=None, world: int, rank: int,
-                   replicate: bool = False, group=None, use_sum: bool = False):
+                   replicate: bool = False, group=None, use_sum: bool = False,
+                   full_shape: Optional[tuple[int, int]] = None):
     """Run this rank's shard of ``causal_last_k_lookup`` (or ``causal_sum_lookup``).
 
-    Inputs are the full [B, T, C, ...] tensors (or already this rank's slice of
-    them when their batch/head sizes equal the shard's).  Returns this rank's
-    outputs, or the replicated full outputs when ``replicate`` is set.
+    By default the inputs are the full [B, T, C, ...] tensors and this rank
+    slices its streams out of them.  When the caller already holds only this
+    rank's slice ([b1-b0, T, c1-c0, ...], and [b1-b0, T] for the mask), it
+    passes ``full_shape=(B, C)`` of the whole problem; the inputs are then used
+    as they are (their shape must be the shard's).  Either way the key-width
+    rule of the whole problem is applied (see ``_global_fold``), so the values
+    equal those of the unsharded call.  Returns this rank's outputs, or the
+    replicated full outputs when ``replicate`` is set (one NCCL all-gather per
+    output).
     """
     from .ravel_memory import causal_last_k_lookup, causal_sum_lookup
-    B, T, C = write_addresses.shape
-    sh = shard_streams(B, C, world, rank)
-    w = sh.take(write_addresses)
-    p = sh.take(payloads)
-    r = sh.take(read_addresses)
-    m = None if write_mask is None else sh.take(write_mask, head_dim=False)
+    Bi, T, Ci = write_addresses.shape
+    if full_shape is None:
+        sh = shard_streams(Bi, Ci, world, rank)
+        w, p, r = sh.take(write_addresses), sh.take(payloads), sh.take(read_addresses)
+        m = None if write_mask is None else sh.take(write_mask, head_dim=False)
+    else:
+        B, C = (int(x) for x in full_shape)
+        sh = shard_streams(B, C, world, rank)
+        if (Bi, Ci) != (sh.b1 - sh.b0, sh.c1 - sh.c0):
+            raise ValueError(f"inputs of shape {(Bi, T, Ci)} are not rank {rank}'s slice of a [{B}, T, {C}] "
+                             f"problem over {world} ranks (expected {(sh.b1 - sh.b0, T, sh.c1 - sh.c0)})")
+        w, p, r, m = write_addresses, payloads, read_addresses, write_mask
+    if r is None or r is w:
+        w = _global_fold(w, sh, T, address_space)
+        r = None if r is None else w
+    else:
+        w, r = _global_fold(w, sh, T, address_space), _global_fold(r, sh, T, address_space)
     if use_sum:
         vals, mask = causal_sum_lookup(w, p, r, address_space=address_space, write_mask=m)
     else:

@@ -1,4 +1,4 @@
-"""Seeded synthetic inputs for the operator at the BASELINE configurations.
+"""Seeded synthetic inputs for the operator at the five benchmark configurations.
 
 No dataset is involved anywhere: every configuration of the benchmark is
 synthetic by definition (address distributions, payloads and gradients drawn

@@ -17,7 +17,7 @@ tests/test_metal_kernels.py:18-64) plus seeded cases covering every option of
 the operator: read != write, write_mask, k > 1, int32 / int64 / negative /
 out-of-int32 addresses, float32 / bfloat16 / float16 / float64 payloads, odd D,
 T = 1, a single address, all writes masked, and the first rows of each
-BASELINE configuration at reduced T.
+benchmark configuration at reduced T.
 
 Stored per case (``None`` inputs are omitted):
   waddr, raddr, wmask, payload (bf16 as uint16 bits), A, k, dtype

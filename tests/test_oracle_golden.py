@@ -51,7 +51,7 @@ def test_oracle_matches_reference_golden(oracle_mod, name):
 
 
 def test_oracle_key_dtype_threshold(oracle_mod):
-    """tests/test_memory.py:11-13 of the reference, plus the BASELINE configs."""
+    """tests/test_memory.py:11-13 of the reference, plus the benchmark configurations."""
     z = load_golden("key_dtype")
     for (B, T, C, A), is32 in zip(z["cases"], z["is_int32"]):
         assert oracle_mod.key_is_int32(int(B), int(T), int(C), int(A)) == bool(is32)

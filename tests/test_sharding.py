@@ -95,3 +95,40 @@ def test_gloo_world2_sharded_equals_unsharded(B, C):
             pr.kill()
     assert all(pr.exitcode == 0 for pr in procs)
     assert q.get(timeout=5) is True
+
+
+def test_shards_apply_the_whole_problems_key_width():
+    """A shard small enough for int32 keys must not truncate int64 addresses that the
+    whole problem (int64 keys, ravel_lm/ravel_memory.py:45-49) keeps whole."""
+    import oracle
+    from ravel_lm_b200.ravel_memory import _composite_key_dtype
+    from ravel_lm_b200.sharding import _global_fold
+    B, T, C, D, A, k, world = 8, 70, 4, 3, 1_000_003, 2, 8
+    assert _composite_key_dtype(B, T, C, A) == torch.int64
+    assert _composite_key_dtype(B // world, T, C, A) == torch.int32
+    g = torch.Generator().manual_seed(5)
+    # addresses far outside int32: their low 32 bits and their true value fold differently
+    w = torch.randint(-(1 << 40), 1 << 40, (B, T, C), generator=g, dtype=torch.int64)
+    w[:, 1::3] = w[:, 0:-1:3]  # exact repeats: hits under either rule
+    w[:, 2::3] = w[:, 0:-2:3] + (1 << 32)  # equal low 32 bits: a hit only after truncation
+    p = torch.randn(B, T, C, D, generator=g)
+    ev, em, _, _ = oracle.latestk_fwd(w.numpy(), p.numpy(), address_space=A, k=k)
+    folded_differs = False
+    for sh in all_shards(B, C, world):
+        ws = sh.take(w)
+        fv, fm, _, _ = oracle.latestk_fwd(_global_fold(ws, sh, T, A).numpy(), sh.take(p).numpy(),
+                                          address_space=A, k=k)
+        assert np.array_equal(fm, em[sh.b0:sh.b1, :, sh.c0:sh.c1])
+        assert np.array_equal(fv * fm[..., None], ev[sh.b0:sh.b1, :, sh.c0:sh.c1] * fm[..., None])
+        _, raw_m, _, _ = oracle.latestk_fwd(ws.numpy(), sh.take(p).numpy(), address_space=A, k=k)
+        folded_differs |= not np.array_equal(raw_m, fm)
+    assert folded_differs, "the case does not exercise the truncation"
+
+
+def test_global_fold_leaves_equal_rules_alone():
+    from ravel_lm_b200.sharding import _global_fold
+    sh = shard_streams(4, 16, 2, 1)
+    a = torch.arange(-5, 5, dtype=torch.int64).view(1, 10, 1).expand(2, 10, 16).contiguous()
+    assert _global_fold(a, sh, 10, 7) is a
+    a32 = a.to(torch.int32)
+    assert _global_fold(a32, sh, 10, 7) is a32
