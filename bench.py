@@ -16,13 +16,17 @@ used only for the barrier and the max over ranks of the step time.
 The JSON line carries the device-timed throughput (``value``), the roofline
 of the dominant kernel (CUDA events around its entry point inside the timed
 region), an end-to-end number through the API with pinned host buffers
-(``e2e``), the CPU oracle port timed on the host (``cpu_baseline``, rank 0 at
-N=1), decode microseconds per step for configuration 4, and the SM clocks
-sampled during the timed region.
+(``e2e``) and its copy-only floor, the reference's CPU code timed on the host
+(``cpu_baseline``, rank 0 at N=1), decode microseconds per step for
+configuration 4, the configuration-5 model step, strong scaling under
+torchrun, and the SM clocks sampled during the timed region.
 
-``--impl reference`` times the CPU port of the reference's algorithm
-(oracle/, OpenMP over all host cores) on a bounded sample of the same
-workload; under torchrun only rank 0 works.
+``--impl reference`` times the reference's own CPU implementation: its
+``ravel_lm.ravel_memory`` functions on CPU tensors with every host core
+(torch threads), from the installed copy under baseline/_ref, on a bounded
+sample of the same workload; the C restatement in oracle/ (OpenMP) is timed
+beside it as ``cpu_port``, and replaces it when the install does not import.
+Under torchrun only rank 0 works.
 """
 from __future__ import annotations
 
@@ -51,13 +55,17 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, default=3, choices=[2, 3, 5])
+    ap.add_argument("--config", type=int, default=3, choices=[1, 2, 3, 5])
     ap.add_argument("--e2e-steps", type=int, default=8)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-general", action="store_true",
                     help="skip the extra timing of the general path (reads drawn apart from the writes)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-model", action="store_true",
+                    help="skip the whole-model training step of configuration 5 (needs baseline/_ref)")
+    ap.add_argument("--no-strong", action="store_true",
+                    help="under torchrun: skip the strong-scaling run of the fixed configuration-3 problem")
     ap.add_argument("--no-reference-gpu", action="store_true",
                     help="skip timing the reference's own functions on CUDA tensors (needs baseline/_ref)")
     ap.add_argument("--cpu-streams", type=int, default=8, help="streams in the CPU baseline sample")
@@ -172,8 +180,8 @@ def cpu_sample(cfg, n_streams: int, seed: int = 4242):
     w = x["write"][:, :, :C].contiguous().numpy()
     r = None if x["read"] is None else x["read"][:, :, :C].contiguous().numpy()
     p = x["payload"][:, :, :C].contiguous()
-    gv = x["g_vals"][:, :, :C].contiguous()
-    gs = x["g_sums"][:, :, :C].contiguous()
+    gv = x["g_vals"][:, :, :C].contiguous() if "g_vals" in x else None
+    gs = x["g_sums"][:, :, :C].contiguous() if "g_sums" in x else None
     code = {torch.bfloat16: "bf16", torch.float16: "f16"}.get(p.dtype)
     pbits = p.view(torch.int16).numpy().view(np.uint16) if code else p.numpy()
     return dict(w=w, r=r, p=p, pbits=pbits, code=code, gv=gv, gs=gs, streams=C, T=cfg.T,
@@ -181,9 +189,11 @@ def cpu_sample(cfg, n_streams: int, seed: int = 4242):
 
 
 def cpu_step(oracle, s, cfg):
-    """LK fwd + SS fwd + LK bwd + SS bwd of the CPU port on the sample."""
+    """LK fwd + SS fwd + LK bwd + SS bwd of the CPU port on the sample (LK fwd only for forward-only configs)."""
     vals, mask, src, tape = oracle.latestk_fwd(s["w"], s["pbits"], s["r"], address_space=cfg.A, k=cfg.k,
                                                dtype=s["code"])
+    if not cfg.backward:
+        return vals.sum()
     sums, smask, _ = oracle.segsum_fwd(s["w"], s["p"].double().numpy(), s["r"], address_space=cfg.A, tape=tape)
     B, T, C, D = s["p"].shape
     g1 = oracle.latestk_bwd(mask, src, s["gv"].double().numpy(), B * T * C)
@@ -201,9 +211,62 @@ def run_cpu_baseline(cfg, steps: int, warmup: int, n_streams: int) -> dict:
     for _ in range(steps):
         cpu_step(oracle, s, cfg)
     dt = (time.perf_counter() - t0) / max(steps, 1)
+    what = (f"latest-k k={cfg.k} + segmented-sum fwd+bwd" if cfg.backward else f"latest-k k={cfg.k} fwd")
     return {"value": s["tokens_equiv"] / dt, "unit": "tokens/s", "cores": oracle.num_threads(), "kind": "port",
-            "sample": f"{s['streams']} of {cfg.C} streams of one batch row (T={cfg.T}): latest-k k={cfg.k} + "
-                      f"segmented-sum fwd+bwd, = {s['tokens_equiv']:.0f} token-equivalents; "
+            "sample": f"{s['streams']} of {cfg.C} streams of one batch row (T={cfg.T}): {what}, "
+                      f"= {s['tokens_equiv']:.0f} token-equivalents; {steps} timed steps, {warmup} warm-up",
+            "sec_per_step": dt}
+
+
+def import_reference():
+    """The installed reference (baseline/_ref, a pip --target install of ravel-lm), or None."""
+    ref = ROOT / "baseline" / "_ref"
+    if not (ref / "ravel_lm" / "ravel_memory.py").exists():
+        return None
+    if str(ref) not in sys.path:
+        sys.path.insert(0, str(ref))
+    import ravel_lm.ravel_memory as mem
+    return mem
+
+
+def run_reference_torch_cpu(cfg, steps: int, warmup: int, n_streams: int) -> dict:
+    """The reference's own torch code (ravel_memory.py:52-241) on the host cores, on the same
+    bounded sample as the CPU port: latest-k + sum forward and backward through autograd."""
+    import torch
+    try:
+        mem = import_reference()
+    except Exception as exc:  # an install that does not import is reported, not fatal
+        return {"unavailable": f"import of the installed reference failed: {exc}"[:200]}
+    if mem is None:
+        return {"unavailable": "baseline/_ref holds no installed reference"}
+    cores = os.cpu_count() or 1
+    old_threads = torch.get_num_threads()
+    torch.set_num_threads(cores)
+    s = cpu_sample(cfg, n_streams)
+    w = torch.from_numpy(s["w"])
+    r = None if s["r"] is None else torch.from_numpy(s["r"])
+    p = s["p"].clone().requires_grad_(cfg.backward)
+
+    def step():
+        p.grad = None
+        vals, _ = mem.causal_last_k_lookup(w, p, r, address_space=cfg.A, k=cfg.k)
+        if not cfg.backward:
+            return
+        sums, _ = mem.causal_sum_lookup(w, p, r, address_space=cfg.A)
+        torch.autograd.backward([vals, sums], [s["gv"], s["gs"]])
+
+    for _ in range(warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    dt = (time.perf_counter() - t0) / max(steps, 1)
+    torch.set_num_threads(old_threads)
+    return {"value": s["tokens_equiv"] / dt, "unit": "tokens/s", "cores": cores, "kind": "reference",
+            "sample": f"{s['streams']} of {cfg.C} streams of one batch row (T={cfg.T}), "
+                      f"= {s['tokens_equiv']:.0f} token-equivalents: the reference's causal_last_k_lookup"
+                      f"{' + causal_sum_lookup forward + backward (autograd)' if cfg.backward else ' forward'} "
+                      f"on CPU tensors, torch {torch.__version__} with {cores} threads; "
                       f"{steps} timed steps, {warmup} warm-up",
             "sec_per_step": dt}
 
@@ -263,47 +326,80 @@ def run_decode(dev) -> dict:
         raise RuntimeError("bulk prefill differs from token-by-token prefill")
     del bulk, pa, pp
     ra = torch.randint(0, A, (steps, S, H), generator=g, device=dev)
+    wa = torch.randint(0, A, (steps, S, H), generator=g, device=dev)  # independent write addresses
     pay = torch.randn(steps, S, H, D, generator=g, device=dev).to(dt)
     torch.cuda.synchronize(dev)
-    # eager: one read + one write launch per step through the API
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    for i in range(16):
-        cache.read(ra[i])
-        cache.write(ra[i], pay[i])
-    e0.record()
-    for i in range(steps):
-        cache.read(ra[i])
-        cache.write(ra[i], pay[i])
-    e1.record()
-    torch.cuda.synchronize(dev)
-    eager_us = e0.elapsed_time(e1) * 1000.0 / steps
-    # graph: the 1024 fused read+write steps captured once and replayed
-    stream = torch.cuda.Stream(dev)
-    stream.wait_stream(torch.cuda.current_stream(dev))
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(stream):
-        cache.step(ra[0], ra[0], pay[0])
-        with torch.cuda.graph(graph, stream=stream):
-            for i in range(steps):
-                cache.step(ra[i], ra[i], pay[i])
-    torch.cuda.current_stream(dev).wait_stream(stream)
-    graph.replay()
-    torch.cuda.synchronize(dev)
-    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 3
-    g0.record()
-    for _ in range(reps):
+
+    def timed(fn, n):
+        for i in range(16):
+            fn(i)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(n):
+            fn(i)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) * 1000.0 / n
+
+    def graphed(rd, wr):
+        """The 1024 fused read+write steps captured once and replayed: µs per step."""
+        stream = torch.cuda.Stream(dev)
+        stream.wait_stream(torch.cuda.current_stream(dev))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            cache.step(rd[0], wr[0], pay[0])
+            with torch.cuda.graph(graph, stream=stream):
+                for i in range(steps):
+                    cache.step(rd[i], wr[i], pay[i])
+        torch.cuda.current_stream(dev).wait_stream(stream)
         graph.replay()
-    g1.record()
-    torch.cuda.synchronize(dev)
-    graph_us = g0.elapsed_time(g1) * 1000.0 / (steps * reps)
-    del graph
+        torch.cuda.synchronize(dev)
+        reps = 3
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record()
+        for _ in range(reps):
+            graph.replay()
+        g1.record()
+        torch.cuda.synchronize(dev)
+        del graph
+        return g0.elapsed_time(g1) * 1000.0 / (steps * reps)
+
+    # eager: one read + one write launch per step through the API (what model.py:421,424 calls)
+    eager_us = timed(lambda i: (cache.read(ra[i]), cache.write(ra[i], pay[i])), steps)
+    # eager: the one-launch step
+    step_us = timed(lambda i: cache.step(ra[i], ra[i], pay[i]), steps)
+    graph_us = graphed(ra, ra)
+    graph_ind_us = graphed(ra, wa)
     step_bytes = S * H * (2 * 8 + 4 * D * 2 + 3)
-    return {"config": "cfg4: 256 streams x 16 heads, A=4096 uniform, D=64 bf16, cache prefilled by 4096 writes",
-            "us_per_step_graph": graph_us, "us_per_step_eager": eager_us,
-            "prefill_us_token_by_token": prefill_tok_us, "prefill_us_bulk": prefill_bulk_us,
-            "bytes_per_step": step_bytes, "gbs_graph": step_bytes / (graph_us * 1e-6) / 1e9,
-            "target_us": 10.0}
+    out = {"config": "cfg4: 256 streams x 16 heads, A=4096 uniform, D=64 bf16, cache prefilled by 4096 writes",
+           "us_per_step_graph": graph_us, "us_per_step_graph_independent_rw": graph_ind_us,
+           "us_per_step_eager": eager_us, "us_per_step_eager_one_launch": step_us,
+           "prefill_us_token_by_token": prefill_tok_us, "prefill_us_bulk": prefill_bulk_us,
+           "bytes_per_step": step_bytes, "gbs_graph": step_bytes / (graph_us * 1e-6) / 1e9,
+           "target_us": 10.0}
+    # the reference's own cache (gather / scatter_, ravel_memory.py:271-292) on the same GPU
+    try:
+        mem = import_reference()
+    except Exception as exc:
+        mem, out["reference"] = None, f"unavailable: {exc}"[:200]
+    if mem is not None:
+        rc = mem.RavelLayerCache(values=cache.values.clone(), filled=cache.filled.clone())
+        out["us_per_step_reference_eager"] = timed(lambda i: (rc.read(ra[i]), rc.write(ra[i], pay[i])), steps)
+        stream = torch.cuda.Stream(dev)
+        stream.wait_stream(torch.cuda.current_stream(dev))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            rc.read(ra[0])
+            rc.write(ra[0], pay[0])
+            with torch.cuda.graph(graph, stream=stream):
+                for i in range(steps):
+                    rc.read(ra[i])
+                    rc.write(ra[i], pay[i])
+        torch.cuda.current_stream(dev).wait_stream(stream)
+        out["us_per_step_reference_graph"] = timed(lambda i: graph.replay(), 3) / steps
+        del graph, rc
+    return out
 
 
 def main():
@@ -318,8 +414,14 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        cb = run_cpu_baseline(cfg, args.steps, args.warmup, args.cpu_streams)
+        # the reference's own torch code on the host cores when its install imports, else the C port
+        cb = run_reference_torch_cpu(cfg, args.steps, args.warmup, args.cpu_streams)
+        port = run_cpu_baseline(cfg, 3, 1, args.cpu_streams)
+        if "unavailable" in cb:
+            cb, port = port, {"unavailable": cb["unavailable"]}
         line = {"metric": METRIC, "value": cb["value"], "unit": "tokens/s", "impl": "reference",
+                "cpu_port": {k: port[k] for k in ("value", "unit", "cores", "kind", "sample", "unavailable")
+                             if k in port},
                 "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": cb["sec_per_step"] * 1000.0, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": DTYPE_NAMES[str(cfg.dtype)],
@@ -344,14 +446,16 @@ def main():
         x["g_vals"] = None
         torch.cuda.empty_cache()
     w, r = x["write"], x["read"]
-    p = x["payload"].requires_grad_(True)
-    gv, gs = x["g_vals"], x["g_sums"]
+    p = x["payload"].requires_grad_(cfg.backward)
+    gv, gs = x.get("g_vals"), x.get("g_sums")
     A, k = cfg.A, cfg.k
 
     def step():
         # Each step stands for a new batch: forget the tape of the previous step
         # (only the latest-k -> sum reuse inside one step is legitimate).
         clear_tape_cache()
+        if not cfg.backward:  # configuration 1: the latest-1 forward alone
+            return causal_last_k_lookup(w, p, r, address_space=A, k=k)
         p.grad = None
         outs, grads = [], []
         if args.ops in ("all", "lk"):
@@ -429,28 +533,41 @@ def main():
                 "unit": "GB/s", "frac": kernels[dom]["frac"], "traffic": traffic,
                 "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)" if peaks["source"] == "measured"
                 else "fallback 6.65 TB/s"}
-    step_bytes = sum(kb.values())  # one tape per step: the sum reuses the latest-k tape
+    step_bytes = sum(kb[n] for n in kb if n in kernels)  # one tape per step: the sum reuses the latest-k tape
     tokens = cfg.tokens * world
     value = tokens / (ms * 1e-3)
 
-    e2e = None
-    if not args.no_e2e:
+    e2e = copy_bound = None
+    if not args.no_e2e and cfg.backward:
         e2e = run_e2e(cfg, x, dev, args.e2e_steps, world)
+        copy_bound = run_copy_bound(e2e, dev, args.e2e_steps, world)
     general = None
-    if not args.no_general and cfg.addressing == "zipf":
+    if not args.no_general and cfg.addressing == "zipf" and cfg.backward:
         general = run_general(cfg, x, dev, world)
-    ref_gpu = None
+    strong = None
+    if world > 1 and not args.no_strong and cfg.cfg == 3:
+        strong = run_strong(cfg, dev, rank, world)
+    ref_gpu = cfg1 = None
     if world == 1 and not args.no_reference_gpu:
-        ref_gpu = run_reference_gpu(cfg, x, dev, steps=5, warmup=args.warmup)
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cb = run_cpu_baseline(cfg, 1, 1, args.cpu_streams)
-        cpu = {k2: cb[k2] for k2 in ("value", "unit", "cores", "kind", "sample")}
+        if cfg.backward:
+            ref_gpu = run_reference_gpu(cfg, x, dev, steps=5, warmup=args.warmup)
+        cfg1 = run_cfg1(dev)
+    del x, p, gv, gs
+    torch.cuda.empty_cache()
+    model = None
+    if not args.no_model:
+        model = run_model(dev, rank, world)
     decode = None
     if not args.no_decode:
-        del x, p, gv, gs
-        torch.cuda.empty_cache()
         decode = run_decode(dev)
+    cpu = port = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cb = run_reference_torch_cpu(cfg, 3, 1, args.cpu_streams)
+        pb = run_cpu_baseline(cfg, 3, 1, args.cpu_streams)
+        if "unavailable" in cb:
+            cb, pb = pb, {"unavailable": cb["unavailable"]}
+        cpu = {k2: cb[k2] for k2 in ("value", "unit", "cores", "kind", "sample")}
+        port = {k2: pb[k2] for k2 in ("value", "unit", "cores", "kind", "sample", "unavailable") if k2 in pb}
 
     if rank == 0:
         line = {
@@ -461,9 +578,10 @@ def main():
             "tokens_per_sec_per_gpu": value / world,
             "step_roofline": {"algorithmic_bytes": step_bytes, "achieved_gbs": step_bytes / (ms * 1e-3) / 1e9,
                               "frac": step_bytes / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], "peak": peaks["hbm_gbs"]},
-            "roofline": roofline, "kernels": kernels, "e2e": e2e, "cpu_baseline": cpu, "decode": decode,
-            "general_path": general, "reference_gpu": ref_gpu,
-            "clocks": clk, "gpu_launches": launches,
+            "roofline": roofline, "kernels": kernels, "e2e": e2e, "e2e_copy_bound": copy_bound,
+            "cpu_baseline": cpu, "cpu_port": port, "decode": decode,
+            "general_path": general, "reference_gpu": ref_gpu, "config1": cfg1, "strong_scaling": strong,
+            "config5_model": model, "clocks": clk, "gpu_launches": launches,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -473,7 +591,8 @@ def main():
 
 
 def workload_config(cfg, world) -> dict:
-    return {"workload": f"cfg{cfg.cfg}: latest-k (k={cfg.k}) + causal segmented-sum, forward + backward",
+    what = "latest-k (k={}) + causal segmented-sum, forward + backward" if cfg.backward else "latest-k (k={}), forward"
+    return {"workload": f"cfg{cfg.cfg}: " + what.format(cfg.k),
             "B_per_gpu": cfg.B, "T": cfg.T, "H": cfg.C, "D": cfg.D, "A": cfg.A, "k": cfg.k,
             "addresses": cfg.addressing + (f" s={cfg.zipf_s}" if cfg.zipf_s else ""),
             "payload_dtype": str(cfg.dtype).replace("torch.", ""), "global_batch": cfg.B * world,
@@ -659,6 +778,279 @@ def run_e2e(cfg, x, dev, steps, world):
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps,
             "path": "pinned host -> ravel_lm_b200.causal_last_k_lookup/causal_sum_lookup (+autograd) -> pinned host",
             "overlap": "copies in and out on their own streams; step i+1 host->device overlaps step i device->host"}
+
+
+def run_copy_bound(e2e: dict, dev, steps: int, world: int) -> dict:
+    """The end-to-end number's floor: the same bytes per step copied host->device and
+    device->host (pinned, on two streams, as the end-to-end pipeline runs them) with no compute."""
+    import torch
+    hin = torch.empty(e2e["h2d_bytes_per_step"], dtype=torch.uint8).pin_memory()
+    hout = torch.empty(e2e["d2h_bytes_per_step"], dtype=torch.uint8).pin_memory()
+    din = torch.empty_like(hin, device=dev)
+    dout = torch.empty_like(hout, device=dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def one():
+        with torch.cuda.stream(s_in):
+            din.copy_(hin, non_blocking=True)
+        with torch.cuda.stream(s_out):
+            hout.copy_(dout, non_blocking=True)
+
+    one()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    cur = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(cur)
+    s_in.wait_stream(cur)
+    s_out.wait_stream(cur)
+    for _ in range(steps):
+        one()
+    cur.wait_stream(s_in)
+    cur.wait_stream(s_out)
+    e1.record(cur)
+    torch.cuda.synchronize(dev)
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    del din, dout
+    torch.cuda.empty_cache()
+    return {"ms_per_step": ms, "tokens_per_s": e2e["value"] * e2e["ms_per_step"] / ms,
+            "h2d_gbs": e2e["h2d_bytes_per_step"] / (ms * 1e-3) / 1e9,
+            "d2h_gbs": e2e["d2h_bytes_per_step"] / (ms * 1e-3) / 1e9,
+            "e2e_frac_of_bound": ms / e2e["ms_per_step"],
+            "what": "pinned host<->device copies of the end-to-end step's bytes, both directions at once, no compute"}
+
+
+def run_strong(cfg, dev, rank: int, world: int, steps: int = 10, warmup: int = 3) -> dict:
+    """Strong scaling: the fixed single-GPU problem (global batch cfg.B) split over the ranks
+    with sharding.sharded_lookup (batch rows, or heads when B < world), each rank holding only
+    its own slice.  Also times replicated outputs (one NCCL all-gather per output)."""
+    import torch
+    from ravel_lm_b200.ravel_memory import clear_tape_cache
+    from ravel_lm_b200.sharding import gather_outputs, shard_streams, sharded_lookup
+    from ravel_lm_b200.workloads import make_inputs
+    sh = shard_streams(cfg.B, cfg.C, world, rank)
+    x = make_inputs(cfg, seed=1000 + cfg.cfg, device=dev)  # identical global problem on every rank
+    w, p0 = sh.take(x["write"]), sh.take(x["payload"])
+    r = sh.take(x["read"])
+    gv, gs = sh.take(x["g_vals"]), sh.take(x["g_sums"])
+    del x
+    torch.cuda.empty_cache()
+    p = p0.requires_grad_(True)
+    kw = dict(address_space=cfg.A, world=world, rank=rank, full_shape=(cfg.B, cfg.C))
+
+    def step():
+        clear_tape_cache()
+        p.grad = None
+        vals, _ = sharded_lookup(w, p, r, k=cfg.k, **kw)
+        sums, _ = sharded_lookup(w, p, r, use_sum=True, **kw)
+        torch.autograd.backward([vals, sums], [gv, gs])
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize(dev)
+    ms = max_over_ranks(t0.elapsed_time(t1) / steps, world)
+    # replicated outputs: every rank receives the full [B, T, C, ...] results
+    with torch.no_grad():
+        vals, vmask = sharded_lookup(w, p, r, k=cfg.k, **kw)
+        sums, smask = sharded_lookup(w, p, r, use_sum=True, **kw)
+    outs = (vals, vmask, sums, smask)
+    for o in outs:
+        gather_outputs(o, sh)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record()
+    for o in outs:
+        gather_outputs(o, sh)
+    g1.record()
+    torch.cuda.synchronize(dev)
+    gms = max_over_ranks(g0.elapsed_time(g1), world)
+    full_bytes = sum(o.numel() * o.element_size() for o in outs) * world
+    recv = full_bytes * (world - 1) / world
+    return {"global_batch": cfg.B, "streams_per_rank": sh.streams, "split": "heads" if sh.splits_heads else "batch",
+            "ms_per_step": ms, "value": cfg.tokens / (ms * 1e-3), "unit": "tokens/s",
+            "replicate_ms": gms, "replicate_bytes": full_bytes,
+            "replicate_recv_gbs_per_rank": recv / (gms * 1e-3) / 1e9,
+            "what": "fixed cfg3 problem split over the ranks; latest-k + sum fwd+bwd per rank; replicate = "
+                    "all_gather_into_tensor of values, masks, sums, sum masks + local reorder"}
+
+
+def run_cfg1(dev, reps: int = 200) -> dict:
+    """Configuration 1 (latest-1 forward, fp32, B8 T256 H4 D16): ours against the kernel the
+    reference dispatches to on CUDA for it (Triton v2, triton_latest1.py:86-154), µs per call."""
+    import torch
+    from ravel_lm_b200 import causal_last_k_lookup
+    from ravel_lm_b200.ravel_memory import clear_tape_cache
+    from ravel_lm_b200.workloads import CONFIGS, make_inputs
+    cfg = CONFIGS[1]
+    x = make_inputs(cfg, seed=1001, device=dev)
+    w, p = x["write"], x["payload"]
+
+    def timed(fn):
+        for _ in range(10):
+            fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) * 1000.0 / reps
+
+    def ours():
+        clear_tape_cache()
+        return causal_last_k_lookup(w, p, address_space=cfg.A, k=1)
+
+    out = {"config": "cfg1: B8 T256 H4 D16 fp32, k=1, Zipf(1.1) over 256, forward", "us_ours_eager": timed(ours)}
+    # one CUDA graph per call (what a captured model step pays)
+    stream = torch.cuda.Stream(dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        ours()
+        with torch.cuda.graph(graph, stream=stream):
+            ours()
+    torch.cuda.current_stream(dev).wait_stream(stream)
+    out["us_ours_graph"] = timed(graph.replay)
+    del graph
+    try:
+        mem = import_reference()
+    except Exception as exc:
+        mem, out["reference"] = None, f"unavailable: {exc}"[:200]
+    if mem is not None:
+        import ravel_lm.triton_latest1 as tl1
+        if tl1.can_use_triton_latest1_v2(w, p, None, address_space=cfg.A, k=1, write_mask=None):
+            try:
+                out["us_reference_triton_v2"] = timed(
+                    lambda: mem.causal_last_k_lookup(w, p, address_space=cfg.A, k=1))
+                vr, mr = mem.causal_last_k_lookup(w, p, address_space=cfg.A, k=1)
+                vo, mo = ours()
+                out["values_equal_to_reference"] = bool(torch.equal(vr, vo) and torch.equal(mr, mo))
+            except Exception as exc:  # a Triton build failure on this stack is reported, not fatal
+                out["reference"] = f"Triton v2 failed: {exc}"[:200]
+        else:
+            out["reference"] = "Triton v2 not eligible here (no triton)"
+        old = tl1._HAS_TRITON
+        tl1._HAS_TRITON = False
+        try:
+            out["us_reference_torch"] = timed(lambda: mem.causal_last_k_lookup(w, p, address_space=cfg.A, k=1))
+        finally:
+            tl1._HAS_TRITON = old
+    return out
+
+
+def model_config(RavelConfig):
+    """Configuration 5's model: a random-init 6-layer RavelLM with both lookups in every layer."""
+    return RavelConfig(vocab_size=1024, block_size=1024, d_model=256, n_layers=6, address_space=1024,
+                       n_literal_heads=4, n_learned_heads=4, n_codebooks=2, codebook_size=32, payload_dim=32,
+                       last_k=2, use_sum_read=True, memory_every=1, dropout=0.0)
+
+
+def run_model(dev, rank: int, world: int, steps: int = 8, warmup: int = 3) -> dict:
+    """Configuration 5: the reference's own RavelLM (from baseline/_ref, unchanged) trained on
+    8 sequences of 1024 tokens per GPU, with this operator dropped in for ravel_lm.ravel_memory
+    (the import of model.py:11) and, for comparison, with the stock operator.  One step =
+    forward, backward, the deferred weight gradients (deferred.flush_deferred), a gradient
+    all-reduce over NCCL when world > 1 (data parallel), and an AdamW step."""
+    import torch
+    import ravel_lm_b200._lib as L
+    import ravel_lm_b200.ravel_memory as mine
+    from ravel_lm_b200.workloads import zipf_ranks
+    try:
+        mem = import_reference()
+        if mem is None:
+            return {"unavailable": "baseline/_ref holds no installed reference"}
+        import ravel_lm.deferred as deferred
+        import ravel_lm.model as model_mod
+        from ravel_lm.config import RavelConfig
+    except Exception as exc:
+        return {"unavailable": f"import of the installed reference failed: {exc}"[:200]}
+    cfg = model_config(RavelConfig)
+    B, T = 8, 1024
+    torch.manual_seed(0)  # same initial weights on every rank
+    model = model_mod.RavelLM(cfg).to(dev)
+    params = [q for q in model.parameters() if q.requires_grad]
+    opt = torch.optim.AdamW(params, lr=1e-4, fused=True)
+    g = torch.Generator(device=dev).manual_seed(5000 + rank)
+    toks = zipf_ranks(cfg.vocab_size, 1.1, (B, T + 1), g)
+    x, y = toks[:, :-1].contiguous(), toks[:, 1:].contiguous()
+    names = ("causal_last_k_lookup", "causal_sum_lookup", "RavelLayerCache")
+    stock = {n: getattr(model_mod, n) for n in names}
+
+    def use(impl):
+        for n in names:
+            setattr(model_mod, n, getattr(mine, n) if impl == "ours" else stock[n])
+
+    def step():
+        mine.clear_tape_cache()
+        opt.zero_grad(set_to_none=True)
+        loss = model(x, y)["loss"]
+        loss.backward()
+        deferred.flush_deferred()
+        if world > 1:
+            import torch.distributed as dist
+            for q in params:
+                if q.grad is None:
+                    q.grad = torch.zeros_like(q)
+            grads = [q.grad for q in params]
+            flat = torch._utils._flatten_dense_tensors(grads)
+            dist.all_reduce(flat)
+            flat.div_(world)
+            for gq, v in zip(grads, torch._utils._unflatten_dense_tensors(flat, grads)):
+                gq.copy_(v)
+        opt.step()
+        return loss
+
+    out = {"config": "cfg5: RavelLM vocab 1024, d_model 256, 6 layers, 4 literal + 4 learned heads (2x32 codes), "
+                     "A 1024, payload 32 fp32, last_k 2 + sum read; 8 x 1024 tokens per GPU",
+           "parallelism": f"data parallel over {world} GPU(s), NCCL all-reduce of gradients" if world > 1
+           else "1 GPU", "global_batch": B * world}
+    for impl in ("ours", "stock"):
+        use(impl)
+        try:
+            for _ in range(warmup):
+                step()
+            torch.cuda.synchronize(dev)
+            barrier(world)
+            ops = []
+            if impl == "ours":
+                def hook(name, thunk):
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    rc = thunk()
+                    e1.record()
+                    ops.append((e0, e1))
+                    return rc
+                L.set_call_hook(hook)
+            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0.record()
+            for _ in range(steps):
+                loss = step()
+            t1.record()
+            torch.cuda.synchronize(dev)
+            L.set_call_hook(None)
+            ms = max_over_ranks(t0.elapsed_time(t1) / steps, world)
+            ent = {"ms_per_step": ms, "value": B * T * world / (ms * 1e-3), "unit": "tokens/s",
+                   "loss": float(loss)}
+            if ops:
+                op_ms = sum(a.elapsed_time(b) for a, b in ops) / steps
+                ent["operator_ms_per_step"] = op_ms
+                ent["operator_share"] = op_ms / (t0.elapsed_time(t1) / steps)
+            out[impl] = ent
+        finally:
+            use("stock")
+            L.set_call_hook(None)
+    del model, opt
+    torch.cuda.empty_cache()
+    return out
 
 
 if __name__ == "__main__":

@@ -118,6 +118,19 @@ int ravel_latestk_bwd(const void* tape, int tape_flags, const void* raddr, int a
                       void* stream);
 
 /*
+ * ravel_latestk_bwd that adds its gradient to grad_payload instead of
+ * overwriting it (grad_payload += d values / d payloads, one rounding per
+ * element for 16-bit payloads).  Replaces autograd's sum of the latest-k and
+ * segmented-sum payload gradients when both lookups of a memory layer read the
+ * same payload tensor (ravel_lm/model.py:367-384): the sum's gradient is
+ * written first, this call adds the latest-k gradient to it in place.
+ */
+int ravel_latestk_bwd_accumulate(const void* tape, int tape_flags, const void* raddr, int addr_dtype,
+                                 const void* grad_vals, int dtype, int64_t B, int64_t T, int64_t C, int64_t D,
+                                 int64_t A, int64_t k, void* grad_payload, void* scratch, size_t scratch_bytes,
+                                 void* stream);
+
+/*
  * Segmented-sum lookup from a built tape: sums[b,t,c] = sum of payloads of
  * writes with the same (b, c, address) strictly before t (float32
  * accumulation, float64 for float64 payloads); mask = at least one such write.

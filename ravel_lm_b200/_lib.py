@@ -45,6 +45,8 @@ SIGNATURES = {
                           [_c_vp, _c_vp, _c_vp, _c_sz, _c_vp, _c_sz, _c_vp]),
     "ravel_latestk_bwd": (_c_int, [_c_vp, _c_int, _c_vp, _c_int, _c_vp, _c_int] + [_c_i64] * 6 +
                           [_c_vp, _c_vp, _c_sz, _c_vp]),
+    "ravel_latestk_bwd_accumulate": (_c_int, [_c_vp, _c_int, _c_vp, _c_int, _c_vp, _c_int] + [_c_i64] * 6 +
+                                     [_c_vp, _c_vp, _c_sz, _c_vp]),
     "ravel_segsum_fwd_tape": (_c_int, [_c_vp, _c_int, _c_vp, _c_int, _c_vp, _c_int] + [_c_i64] * 5 +
                               [_c_vp, _c_vp, _c_vp, _c_sz, _c_vp]),
     "ravel_segsum_fwd": (_c_int, [_c_vp, _c_vp, _c_int, _c_vp, _c_vp, _c_int] + [_c_i64] * 5 +

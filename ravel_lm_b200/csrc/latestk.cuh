@@ -43,6 +43,7 @@ struct LkArgs {
     int64_t nchunks;        // chunks per stream (fast path)
     FastDiv fd_rv, fd_bv, fd_k;  // divisions by vectors-per-row, vectors-per-block, k
     FastDiv fd_C, fd_T;          // flat row -> (b, t, c)
+    int accumulate;         // backward: add to grad payload instead of overwriting it
 };
 
 // Flat payload row of (stream s, time t) = ((s / C) * T + t) * C + s % C,
@@ -247,6 +248,12 @@ __global__ void __launch_bounds__(256) k_lk_bwd_fast(LkArgs a) {
         Acc acc[EPV];
 #pragma unroll
         for (int x = 0; x < EPV; ++x) acc[x] = Acc(0);
+        if (a.accumulate) {
+            const uint4 prev = ld_vec<VB>(outp + wrow[i] * a.row_bytes + v * VB);
+            const V* pv0 = reinterpret_cast<const V*>(&prev);
+#pragma unroll
+            for (int x = 0; x < EPV; ++x) acc[x] = E::to_acc(pv0[x]);
+        }
         const uint64_t my = wadr[i];
         for (int j = 0; j < k; ++j) {
             const int wi = static_cast<int>(i) + 1 + j;
@@ -426,9 +433,16 @@ __global__ void __launch_bounds__(256) k_lk_bwd_gather(LkArgs a, const KeyT* rke
         const KeyT* wk = static_cast<const KeyT*>(a.keys) + s * T;
         const KeyT kq = wk[q];
         const RowMap rows_of(s, T, a.C);
+        const uint64_t orow = static_cast<uint64_t>(rows_of(kq & tmask));
         Acc acc[EPV];
 #pragma unroll
         for (int e = 0; e < EPV; ++e) acc[e] = Acc(0);
+        if (a.accumulate) {
+            const uint4 prev = ld_vec<VB>(out + orow * D + lig * EPV);
+            const V* pv0 = reinterpret_cast<const V*>(&prev);
+#pragma unroll
+            for (int e = 0; e < EPV; ++e) acc[e] = E::to_acc(pv0[e]);
+        }
         if (q < n_s) {
             // slots j < jmax keep write q+j in q's segment: k write keys loaded 8 at a
             // time, independently
@@ -480,16 +494,17 @@ __global__ void __launch_bounds__(256) k_lk_bwd_gather(LkArgs a, const KeyT* rke
         V* ov = reinterpret_cast<V*>(&o);
 #pragma unroll
         for (int e = 0; e < EPV; ++e) ov[e] = E::from_acc(acc[e]);
-        st_vec<VB>(out + static_cast<uint64_t>(rows_of(kq & tmask)) * D + lig * EPV, o);
+        st_vec<VB>(out + orow * D + lig * EPV, o);
     }
 }
 
-// Convert a float accumulator [n] to the payload dtype.
+// Convert a float accumulator [n] to the payload dtype (added to `out` when accumulating).
 template <int DT>
-__global__ void k_acc_to_dtype(const float* __restrict__ acc, typename Elem<DT>::T* __restrict__ out, int64_t n) {
+__global__ void k_acc_to_dtype(const float* __restrict__ acc, typename Elem<DT>::T* __restrict__ out, int64_t n,
+                               int accumulate) {
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-        out[i] = Elem<DT>::from_acc(acc[i]);
+        out[i] = Elem<DT>::from_acc(accumulate ? acc[i] + Elem<DT>::to_acc(out[i]) : acc[i]);
 }
 
 }  // namespace ravel

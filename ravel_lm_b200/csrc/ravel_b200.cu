@@ -489,7 +489,7 @@ int lk_fwd_tape(const void* tape, int flags, const void* raddr, int addr_dtype, 
 
 int lk_bwd(const void* tape, int flags, const void* raddr, int addr_dtype, const void* grad_vals, int dtype,
            int64_t B, int64_t T, int64_t C, int64_t D, int64_t A, int64_t k, void* grad_payload, void* scratch,
-           size_t scratch_bytes, cudaStream_t st) {
+           size_t scratch_bytes, cudaStream_t st, int accumulate = 0) {
     if (int e = check_sizes(B, T, C, D, A)) return e;
     if (k <= 0) return RAVEL_ERR_INVALID_ARG;
     if (k > 512) return RAVEL_ERR_UNSUPPORTED;
@@ -502,6 +502,7 @@ int lk_bwd(const void* tape, int flags, const void* raddr, int addr_dtype, const
     const TapeView tv = tape_view(tape, tl);
     LkArgs a = lk_args(tv, tl, raddr, addr_dtype, B, T, C, D, A, k, dtype);
     a.grad = grad_vals;
+    a.accumulate = accumulate;
     const int64_t S = B * C;
     if (!tl.general) {
         a.out = grad_payload;
@@ -564,8 +565,10 @@ int lk_bwd(const void* tape, int flags, const void* raddr, int addr_dtype, const
         acc = static_cast<char*>(scratch) + sl.off_big;
     }
     const size_t acc_sz = static_cast<size_t>(N) * D * acc_bytes(dtype);
-    if (cudaMemsetAsync(acc, 0, acc_sz, st) != cudaSuccess) return RAVEL_ERR_CUDA;
+    // float32 / float64 accumulate straight into the output: it keeps its contents when accumulating
+    if ((!direct || !accumulate) && cudaMemsetAsync(acc, 0, acc_sz, st) != cudaSuccess) return RAVEL_ERR_CUDA;
     a.out = acc;
+    a.accumulate = 0;
     const int64_t rpc = 512 / k;
     const int vsh = vshift16(dtype, D, addr_bits(grad_vals) | addr_bits(acc));
     return with_key(tl.kl.key64, [&](auto kt) -> int {
@@ -577,7 +580,8 @@ int lk_bwd(const void* tape, int flags, const void* raddr, int addr_dtype, const
             if constexpr (DT == RAVEL_BF16 || DT == RAVEL_F16) {
                 const int64_t n = N * D;
                 k_acc_to_dtype<DT><<<grid_cap((n + 255) / 256), 256, 0, st>>>(
-                    static_cast<const float*>(acc), static_cast<typename Elem<DT>::T*>(grad_payload), n);
+                    static_cast<const float*>(acc), static_cast<typename Elem<DT>::T*>(grad_payload), n,
+                    accumulate);
                 return check_launch();
             } else {
                 return RAVEL_OK;
@@ -1028,6 +1032,14 @@ int ravel_latestk_bwd(const void* tape, int tape_flags, const void* raddr, int a
                       void* grad_payload, void* scratch, size_t scratch_bytes, void* stream) {
     return lk_bwd(tape, tape_flags, raddr, addr_dtype, grad_vals, dtype, B, T, C, D, A, k, grad_payload, scratch,
                   scratch_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int ravel_latestk_bwd_accumulate(const void* tape, int tape_flags, const void* raddr, int addr_dtype,
+                                 const void* grad_vals, int dtype, int64_t B, int64_t T, int64_t C, int64_t D,
+                                 int64_t A, int64_t k, void* grad_payload, void* scratch, size_t scratch_bytes,
+                                 void* stream) {
+    return lk_bwd(tape, tape_flags, raddr, addr_dtype, grad_vals, dtype, B, T, C, D, A, k, grad_payload, scratch,
+                  scratch_bytes, static_cast<cudaStream_t>(stream), /*accumulate=*/1);
 }
 
 int ravel_segsum_fwd_tape(const void* tape, int tape_flags, const void* raddr, int addr_dtype,

@@ -30,6 +30,7 @@ Differences from the reference that a caller can observe:
 from __future__ import annotations
 
 import functools
+import weakref
 from dataclasses import dataclass
 from typing import Optional, Tuple
 
@@ -93,8 +94,16 @@ def _require_cuda(*tensors: Optional[Tensor]) -> torch.device:
 
 
 def _aliases(read: Optional[Tensor], write: Tensor) -> bool:
+    """Reads that are the write tensor (or a view of the same elements) take the aliased path.
+
+    Under torch.compile only identity is checked (data pointers are not
+    traceable); a distinct tensor over the same memory then takes the general
+    path, which gives the same results.
+    """
     if read is None or read is write:
         return True
+    if torch.compiler.is_compiling():
+        return False
     return (read.dtype == write.dtype and read.shape == write.shape and read.stride() == write.stride()
             and read.device == write.device and read.data_ptr() == write.data_ptr())
 
@@ -140,6 +149,7 @@ class _TapeCache:
         self.key = None
         self.refs = None
         self.value = None
+        self.partner = None  # (payload ref, payload version, latest-k node ref) of the tape's latest-k call
 
     @staticmethod
     def _key(write, read, mask, A, stream):
@@ -160,13 +170,27 @@ class _TapeCache:
     def put(self, write, read, mask, A, stream, value):
         if torch.cuda.is_current_stream_capturing():
             return
-        import weakref
         self.key = self._key(write, read, mask, A, stream)
         self.refs = tuple(None if t is None else weakref.ref(t) for t in (write, read, mask))
         self.value = value
+        self.partner = None
+
+    def note_latest_k(self, write, read, mask, A, stream, payload, node):
+        """Remember the latest-k call that used the cached tape (see ``_SegSumFn.backward``)."""
+        if node is not None and self.get(write, read, mask, A, stream) is not None:
+            self.partner = (weakref.ref(payload), payload._version, weakref.ref(node))
+
+    def latest_k_partner(self, write, read, mask, A, stream, payload):
+        """The latest-k node that read this same payload through this same tape, if any."""
+        if self.partner is None or self.get(write, read, mask, A, stream) is None:
+            return None
+        pref, version, node = self.partner
+        if pref() is not payload or payload._version != version:
+            return None
+        return node
 
     def clear(self):
-        self.key = self.refs = self.value = None
+        self.key = self.refs = self.value = self.partner = None
 
 
 _tape_cache = _TapeCache()
@@ -241,15 +265,21 @@ def _latestk_fwd_fake(write, payload, read, write_mask, address_space, k):
 
 
 def _latestk_bwd_impl(tape: Tensor, grad_vals: Tensor, raddr: Tensor, flags: int, B: int, T: int, C: int,
-                      address_space: int, k: int) -> Tensor:
+                      address_space: int, k: int, accumulate_into: Optional[Tensor] = None) -> Tensor:
+    """Payload gradient of the latest-k values; added to ``accumulate_into`` when given."""
     D = grad_vals.shape[-1]
     device = _require_cuda(tape, grad_vals)
     g = grad_vals.contiguous()
-    grad = torch.empty(B, T, C, D, dtype=g.dtype, device=device)
+    if accumulate_into is None:
+        grad, entry = torch.empty(B, T, C, D, dtype=g.dtype, device=device), "ravel_latestk_bwd"
+    else:
+        grad, entry = accumulate_into, "ravel_latestk_bwd_accumulate"
+        if grad.dtype != g.dtype or grad.shape != (B, T, C, D) or not grad.is_contiguous():
+            raise RuntimeError("accumulation target must be a contiguous [B, T, C, D] tensor of the gradient dtype")
     scratch = torch.empty(scratch_bytes(B, T, C, D, address_space, k, _payload_code(g), flags),
                           dtype=torch.uint8, device=device)
     r, code = _addr(raddr)
-    _lib.call("ravel_latestk_bwd", tape.data_ptr(), flags, r.data_ptr() if flags else None, code,
+    _lib.call(entry, tape.data_ptr(), flags, r.data_ptr() if flags else None, code,
               g.data_ptr(), _payload_code(g), B, T, C, D, address_space, k, grad.data_ptr(), scratch.data_ptr(),
               scratch.numel(), _stream(device))
     return grad
@@ -371,31 +401,51 @@ _segsum_fwd.register_autograd(_segsum_backward, setup_context=_segsum_setup)
 # ops: same implementation functions, same saved tensors and gradients, without
 # the custom-op dispatch (tens of microseconds of host time per call, which
 # decides the step time whenever the kernels are short).
+#
+# One payload, two lookups.  A memory layer reads the same payload tensor with
+# both lookups (ravel_lm/model.py:367-384), so autograd would add their two
+# payload gradients with an extra elementwise kernel (read both, write the
+# sum).  Instead, when the sum lookup reused the tape of a latest-k call on the
+# same payload (same tensor, unmodified), its backward -- which the engine runs
+# first, being the later node -- checks that the latest-k node runs in the same
+# backward pass (``torch._C._will_engine_execute_node``).  If so it hands its
+# gradient to that node instead of returning it, and the latest-k backward adds
+# its own gradient into that buffer in its kernel
+# (``ravel_latestk_bwd_accumulate``) and returns the total.  Whatever else
+# happens (only one output used, separate backward calls, create_graph, the
+# nodes in the other order) each backward returns its own gradient as usual.
 class _LatestKFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, write, payload, read, write_mask, address_space, k):
         vals, mask, tape = _latestk_fwd_impl(write, payload, read, write_mask, address_space, k)
         ctx.save_for_backward(tape, write if read is None else read)
         ctx.meta = (_flags(read, write_mask), *write.shape, int(address_space), int(k))
+        ctx.ravel_stash = None
         ctx.mark_non_differentiable(mask)
         ctx.set_materialize_grads(False)
         return vals, mask
 
     @staticmethod
     def backward(ctx, grad_vals, _gm):
+        stash, ctx.ravel_stash = ctx.ravel_stash, None
+        acc = None
+        if stash is not None and stash[0] == torch._C._current_graph_task_id():
+            acc = stash[1]  # the sum lookup's payload gradient, handed over in this same pass
         if grad_vals is None:
-            return None, None, None, None, None, None
+            return None, acc, None, None, None, None
         tape, raddr = ctx.saved_tensors
         flags, B, T, C, A, k = ctx.meta
-        return None, _latestk_bwd_impl(tape, grad_vals, raddr, flags, B, T, C, A, k), None, None, None, None
+        grad = _latestk_bwd_impl(tape, grad_vals, raddr, flags, B, T, C, A, k, accumulate_into=acc)
+        return None, grad, None, None, None, None
 
 
 class _SegSumFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, write, payload, read, write_mask, address_space):
+    def forward(ctx, write, payload, read, write_mask, address_space, partner):
         sums, mask, tape = _segsum_fwd_impl(write, payload, read, write_mask, address_space)
         ctx.save_for_backward(tape, write if read is None else read)
         ctx.meta = (_flags(read, write_mask), *write.shape, int(address_space))
+        ctx.partner = partner
         ctx.mark_non_differentiable(mask)
         ctx.set_materialize_grads(False)
         return sums, mask
@@ -403,10 +453,16 @@ class _SegSumFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_sums, _gm):
         if grad_sums is None:
-            return None, None, None, None, None
+            return None, None, None, None, None, None
         tape, raddr = ctx.saved_tensors
         flags, B, T, C, A = ctx.meta
-        return None, _segsum_bwd_impl(tape, grad_sums, raddr, flags, B, T, C, A), None, None, None
+        grad = _segsum_bwd_impl(tape, grad_sums, raddr, flags, B, T, C, A)
+        node = ctx.partner() if ctx.partner is not None else None
+        if (node is not None and not torch.is_grad_enabled() and getattr(node, "ravel_stash", 1) is None
+                and torch._C._will_engine_execute_node(node)):
+            node.ravel_stash = (torch._C._current_graph_task_id(), grad)
+            return None, None, None, None, None, None
+        return None, grad, None, None, None, None
 
 
 # ------------------------------------------------------------------ public API
@@ -459,7 +515,11 @@ def causal_last_k_lookup(
     if torch.compiler.is_compiling():
         vals, mask, _tape = _latestk_fwd(write_addresses, payloads, read, write_mask, int(address_space), int(k))
         return vals, mask
-    return _LatestKFn.apply(write_addresses, payloads, read, write_mask, int(address_space), int(k))
+    vals, mask = _LatestKFn.apply(write_addresses, payloads, read, write_mask, int(address_space), int(k))
+    if vals.grad_fn is not None:
+        _tape_cache.note_latest_k(write_addresses, read, write_mask, int(address_space), _stream(payloads.device),
+                                  payloads, vals.grad_fn)
+    return vals, mask
 
 
 def causal_sum_lookup(
@@ -494,7 +554,11 @@ def causal_sum_lookup(
     if torch.compiler.is_compiling():
         sums, mask, _tape = _segsum_fwd(write_addresses, payloads, read, write_mask, int(address_space))
         return sums, mask
-    return _SegSumFn.apply(write_addresses, payloads, read, write_mask, int(address_space))
+    partner = None
+    if payloads.requires_grad and torch.is_grad_enabled():
+        partner = _tape_cache.latest_k_partner(write_addresses, read, write_mask, int(address_space),
+                                               _stream(payloads.device), payloads)
+    return _SegSumFn.apply(write_addresses, payloads, read, write_mask, int(address_space), partner)
 
 
 # ------------------------------------------------------------------ decode cache
