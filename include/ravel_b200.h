@@ -220,6 +220,44 @@ int ravel_segsum_fwd_noalloc(const void* waddr, const void* raddr, int addr_dtyp
                              int64_t T, int64_t C, int64_t D, int64_t A, void* out_sums,
                              uint8_t* out_mask, void* stream);
 
+/*
+ * Gate residual of a memory layer, out = x + sigmoid(gate) * fused, elementwise
+ * over n elements of float32 or bfloat16 (gate_residual,
+ * ravel_lm/triton_block.py:383-387, called at ravel_lm/model.py:388).  Same
+ * arithmetic and rounding as the reference's torch ops (sigmoid, mul, add), so
+ * results are equal bit for bit.  Other dtypes: RAVEL_ERR_UNSUPPORTED.
+ */
+int ravel_gate_residual_fwd(const void* x, const void* gate, const void* fused, void* out, int64_t n, int dtype,
+                            void* stream);
+
+/*
+ * Its backward (the autograd of the same ops): grad_gate = ((grad_out * fused)
+ * * (1 - s)) * s, grad_fused = grad_out * s with s = sigmoid(gate); the
+ * gradient of x is grad_out itself.
+ */
+int ravel_gate_residual_bwd(const void* gate, const void* fused, const void* grad_out, void* grad_gate,
+                            void* grad_fused, int64_t n, int dtype, void* stream);
+
+/*
+ * RMSNorm over the last dimension: y = x * rsqrt(mean(x^2) + eps) * weight for
+ * M rows of K elements (rms_norm, ravel_lm/triton_block.py:320-323, the
+ * RMSNorm of ravel_lm/model.py:31-39), float32 or bfloat16 with float32 math.
+ * rstd [M] (float32) is kept for the backward.  K <= 4096.
+ */
+int ravel_rms_norm_fwd(const void* x, const void* weight, float eps, void* y, float* rstd, int64_t M, int64_t K,
+                       int dtype, void* stream);
+
+/* Scratch bytes of ravel_rms_norm_bwd (per-block partial weight gradients). */
+size_t ravel_rms_norm_scratch_bytes(int64_t M, int64_t K);
+
+/*
+ * RMSNorm backward: grad_x [M, K] and grad_weight [K] (deterministic: no
+ * atomics, a fixed summation order for a given M).
+ */
+int ravel_rms_norm_bwd(const void* x, const void* weight, const void* grad_y, const float* rstd, void* grad_x,
+                       void* grad_weight, int64_t M, int64_t K, int dtype, void* scratch, size_t scratch_bytes,
+                       void* stream);
+
 /* Copy the device error word (RAVEL_DEVERR_* bits) of the current device into
  * *out after the work queued on `stream`; synchronises that stream. */
 int ravel_device_error(int* out, void* stream);

@@ -5,6 +5,7 @@
 // scratch layouts, and the launch plumbing; the kernels live in the headers.
 #include <atomic>
 #include <cstring>
+#include <initializer_list>
 #include <mutex>
 #include <type_traits>
 
@@ -13,6 +14,7 @@
 #include "latestk.cuh"
 #include "segsum.cuh"
 #include "cache.cuh"
+#include "glue.cuh"
 
 namespace ravel {
 namespace {
@@ -981,11 +983,110 @@ int noalloc_base(void** out) {
     *out = g_noalloc_base[dev];
     return RAVEL_OK;
 }
+// ------------------------------------------------------------------ glue (gate residual, RMSNorm)
+constexpr int64_t kRmsMaxK = 4096;
+constexpr int64_t kRmsBwdBlocks = 296;  // fixed cap, so dg's summation order depends on M only
+
+int64_t rms_bwd_blocks(int64_t M) {
+    const int64_t b = (M + 7) / 8;
+    return b < 1 ? 1 : (b > kRmsBwdBlocks ? kRmsBwdBlocks : b);
+}
+
+template <typename F>
+int with_glue_type(int dtype, F&& f) {
+    if (dtype == RAVEL_F32) return f(float(0));
+    if (dtype == RAVEL_BF16) return f(__nv_bfloat16());
+    return RAVEL_ERR_UNSUPPORTED;
+}
+
+int elem_vec_ok(int64_t n, int esize, std::initializer_list<const void*> ptrs) {
+    if ((n * esize) % 16 != 0) return 0;
+    for (const void* p : ptrs)
+        if (reinterpret_cast<uintptr_t>(p) % 16 != 0) return 0;
+    return 1;
+}
 }  // namespace
 
 using namespace ravel;
 
 extern "C" {
+
+int ravel_gate_residual_fwd(const void* x, const void* gate, const void* fused, void* out, int64_t n, int dtype,
+                            void* stream) {
+    if (n < 0) return RAVEL_ERR_INVALID_ARG;
+    if (n == 0) return RAVEL_OK;
+    if (!x || !gate || !fused || !out) return RAVEL_ERR_INVALID_ARG;
+    return with_glue_type(dtype, [&](auto tv) -> int {
+        using T = decltype(tv);
+        const int vec = elem_vec_ok(n, sizeof(T), {x, gate, fused, out});
+        const int64_t units = vec ? n / (16 / sizeof(T)) : n;
+        k_gate_res_fwd<T><<<grid_cap((units + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+            static_cast<const T*>(x), static_cast<const T*>(gate), static_cast<const T*>(fused),
+            static_cast<T*>(out), n, vec);
+        return check_launch();
+    });
+}
+
+int ravel_gate_residual_bwd(const void* gate, const void* fused, const void* grad_out, void* grad_gate,
+                            void* grad_fused, int64_t n, int dtype, void* stream) {
+    if (n < 0) return RAVEL_ERR_INVALID_ARG;
+    if (n == 0) return RAVEL_OK;
+    if (!gate || !fused || !grad_out || !grad_gate || !grad_fused) return RAVEL_ERR_INVALID_ARG;
+    return with_glue_type(dtype, [&](auto tv) -> int {
+        using T = decltype(tv);
+        const int vec = elem_vec_ok(n, sizeof(T), {gate, fused, grad_out, grad_gate, grad_fused});
+        const int64_t units = vec ? n / (16 / sizeof(T)) : n;
+        k_gate_res_bwd<T><<<grid_cap((units + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+            static_cast<const T*>(gate), static_cast<const T*>(fused), static_cast<const T*>(grad_out),
+            static_cast<T*>(grad_gate), static_cast<T*>(grad_fused), n, vec);
+        return check_launch();
+    });
+}
+
+size_t ravel_rms_norm_scratch_bytes(int64_t M, int64_t K) {
+    if (M < 0 || K <= 0) return 0;
+    return static_cast<size_t>(rms_bwd_blocks(M) * K) * sizeof(float);
+}
+
+int ravel_rms_norm_fwd(const void* x, const void* weight, float eps, void* y, float* rstd, int64_t M, int64_t K,
+                       int dtype, void* stream) {
+    if (M < 0 || K <= 0) return RAVEL_ERR_INVALID_ARG;
+    if (K > kRmsMaxK) return RAVEL_ERR_UNSUPPORTED;
+    if (M == 0) return RAVEL_OK;
+    if (!x || !weight || !y || !rstd) return RAVEL_ERR_INVALID_ARG;
+    return with_glue_type(dtype, [&](auto tv) -> int {
+        using T = decltype(tv);
+        k_rms_fwd<T><<<grid_cap((M + 7) / 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+            static_cast<const T*>(x), static_cast<const T*>(weight), static_cast<T*>(y), rstd, M,
+            static_cast<int>(K), eps);
+        return check_launch();
+    });
+}
+
+int ravel_rms_norm_bwd(const void* x, const void* weight, const void* grad_y, const float* rstd, void* grad_x,
+                       void* grad_weight, int64_t M, int64_t K, int dtype, void* scratch, size_t scratch_bytes,
+                       void* stream) {
+    if (M < 0 || K <= 0) return RAVEL_ERR_INVALID_ARG;
+    if (K > kRmsMaxK) return RAVEL_ERR_UNSUPPORTED;
+    if (!x || !weight || !grad_y || !rstd || !grad_x || !grad_weight) return RAVEL_ERR_INVALID_ARG;
+    if (scratch == nullptr || scratch_bytes < ravel_rms_norm_scratch_bytes(M, K)) return RAVEL_ERR_WORKSPACE;
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    return with_glue_type(dtype, [&](auto tv) -> int {
+        using T = decltype(tv);
+        const int64_t nb = rms_bwd_blocks(M);
+        float* part = static_cast<float*>(scratch);
+        const size_t smem = static_cast<size_t>(8 * K) * sizeof(float);
+        if (int e = set_smem(k_rms_bwd<T>, smem)) return e;
+        k_rms_bwd<T><<<static_cast<unsigned>(nb), 256, smem, st>>>(
+            static_cast<const T*>(x), static_cast<const T*>(weight), static_cast<const T*>(grad_y), rstd,
+            static_cast<T*>(grad_x), part, M, static_cast<int>(K));
+        if (int e = check_launch()) return e;
+        k_rms_dg_reduce<T><<<static_cast<unsigned>((K + 255) / 256), 256, 0, st>>>(
+            part, static_cast<int>(nb), static_cast<int>(K), static_cast<T*>(grad_weight));
+        return check_launch();
+    });
+}
+
 
 size_t ravel_tape_bytes(int64_t B, int64_t T, int64_t C, int64_t A, int tape_flags) {
     if (B < 0 || T < 0 || C < 0 || A <= 0) return 0;

@@ -140,9 +140,12 @@ class _TapeCache:
     / read / mask tensors are the very same objects (checked through weak
     references, so a freed tensor whose memory is reused never matches), none
     of them was modified in place since (torch version counters), and the
-    address space, flags and stream agree.  It is bypassed while a CUDA graph
-    is being captured.  Writing into an address tensor behind torch's back
-    (raw pointers) is not detected: call ``clear_tape_cache()`` after that.
+    address space, flags and stream agree.  Whether a CUDA graph is being
+    captured is part of the key: a tape made during a capture (in the graph's
+    memory pool) is reused only inside that capture, and a tape made outside
+    one is never referenced by a captured graph.  Writing into an address
+    tensor behind torch's back (raw pointers) is not detected: call
+    ``clear_tape_cache()`` after that.
     """
 
     def __init__(self):
@@ -155,10 +158,10 @@ class _TapeCache:
     def _key(write, read, mask, A, stream):
         return (A, _flags(read, mask), tuple(write.shape), write.dtype, write.device, stream, write._version,
                 None if read is None else (read.dtype, read._version),
-                None if mask is None else (mask.dtype, mask._version))
+                None if mask is None else (mask.dtype, mask._version), torch.cuda.is_current_stream_capturing())
 
     def get(self, write, read, mask, A, stream):
-        if self.key is None or torch.cuda.is_current_stream_capturing():
+        if self.key is None:
             return None
         if self._key(write, read, mask, A, stream) != self.key:
             return None
@@ -168,8 +171,6 @@ class _TapeCache:
         return self.value
 
     def put(self, write, read, mask, A, stream, value):
-        if torch.cuda.is_current_stream_capturing():
-            return
         self.key = self._key(write, read, mask, A, stream)
         self.refs = tuple(None if t is None else weakref.ref(t) for t in (write, read, mask))
         self.value = value

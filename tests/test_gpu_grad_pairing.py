@@ -62,8 +62,8 @@ def _expected(oracle, c):
     w, p = c["w"].numpy(), payload_np(c["p"])
     r = None if c["r"] is None else c["r"].numpy()
     m = None if c["m"] is None else c["m"].numpy()
-    vals, mask, src, tape = oracle.latestk_fwd(w, p, r, m, address_space=c["A"], k=c["k"], dtype=code)
-    _, smask, _ = oracle.segsum_fwd(w, to_f64(c["p"]), r, m, address_space=c["A"], tape=tape)
+    vals, mask, src, tape = oracle.latestk_fwd(w, p, r, address_space=c["A"], k=c["k"], write_mask=m, dtype=code)
+    _, smask, _ = oracle.segsum_fwd(w, to_f64(c["p"]), r, address_space=c["A"], write_mask=m, tape=tape)
     B, T, C, D = c["p"].shape
     glk = oracle.latestk_bwd(mask, src, to_f64(c["gv"]), B * T * C).reshape(B, T, C, D)
     gss = oracle.segsum_bwd(tape, smask, to_f64(c["gs"]))

@@ -13,9 +13,11 @@ stock operator on the same weights and tokens:
   within 1e-9 (float64 makes the learned argmax addresses of later layers
   identical in both runs);
 * float32, six layers, latest-k only: logits bit for bit equal (the reference's
-  CUDA glue is used unchanged in both runs), gradients within 1e-4;
+  CUDA glue is used unchanged in both runs), gradients within 1e-4; the same
+  with this package's ``gate_residual`` kernel in place of ``model.py:12``'s;
 * float32, one layer with the sum read at B = 4, T = 1024: logits and gradients
-  within float32 tolerance;
+  within float32 tolerance (the reference's glue runs IEEE float32 dots here in
+  both runs, not its default TF32);
 * decode (float64): ``forward_step`` over a prompt equals the full forward
   (the reference's ``tests/test_model.py:78-91``) and equals the stock model's
   ``forward_step`` bit for bit; ``generate`` (float32) with greedy sampling
@@ -44,24 +46,35 @@ def ref():
         pytest.skip("no installed reference under baseline/_ref")
     if str(REF) not in sys.path:
         sys.path.insert(0, str(REF))
+    import triton
+    # The reference's CUDA glue multiplies float32 with Triton dots, TF32 by default.
+    # TF32 rounds the GEMM inputs to 10 mantissa bits, which turns last-bit
+    # differences of the operator's float32 sums into 1e-3 relative differences
+    # downstream; both runs of every comparison use IEEE float32 dots instead.
+    old_fp32 = triton.knobs.language.fp32_default
+    triton.knobs.language.fp32_default = "ieee"
     import ravel_lm.config as config
     import ravel_lm.deferred as deferred
     import ravel_lm.model as model
     import ravel_lm_b200._lib as L
     L.load()
     yield model, config.RavelConfig, deferred
+    triton.knobs.language.fp32_default = old_fp32
     torch.cuda.synchronize()
     assert L.device_error(torch.cuda.current_stream().cuda_stream) == 0
 
 
 @contextlib.contextmanager
-def ours(model_mod):
-    """``from ravel_lm_b200.ravel_memory import ...`` in place of ``model.py:11``."""
+def ours(model_mod, glue=False):
+    """``from ravel_lm_b200.ravel_memory import ...`` in place of ``model.py:11`` (and, with
+    ``glue``, ``gate_residual`` from ``ravel_lm_b200.glue`` in place of ``model.py:12``'s)."""
+    import ravel_lm_b200.glue as glue_mod
     import ravel_lm_b200.ravel_memory as mine
     from ravel_lm_b200.ravel_memory import clear_tape_cache
-    saved = {n: getattr(model_mod, n) for n in NAMES}
-    for n in NAMES:
-        setattr(model_mod, n, getattr(mine, n))
+    names = NAMES + (("gate_residual",) if glue else ())
+    saved = {n: getattr(model_mod, n) for n in names}
+    for n in names:
+        setattr(model_mod, n, getattr(glue_mod if n == "gate_residual" else mine, n))
     clear_tape_cache()
     try:
         yield
@@ -102,9 +115,9 @@ def _close(a, b, tol, what):
     assert err <= tol * max(scale, 1e-30), f"{what}: max abs err {err:.3g} vs tol {tol} * {scale:.3g}"
 
 
-def _compare(model_mod, model, deferred, x, y, tol_logits, tol_grads, exact_logits=False):
+def _compare(model_mod, model, deferred, x, y, tol_logits, tol_grads, exact_logits=False, glue=False):
     ref_logits, ref_loss, ref_grads = _step(model, deferred, x, y)
-    with ours(model_mod):
+    with ours(model_mod, glue=glue):
         logits, loss, grads = _step(model, deferred, x, y)
     if exact_logits:
         assert torch.equal(logits, ref_logits), "logits differ bitwise"
@@ -127,12 +140,13 @@ def test_config5_model_float64_fwd_bwd(ref):
     _compare(model_mod, model, deferred, x, y, 1e-9, 1e-9)
 
 
-def test_config5_model_float32_latest_k(ref):
+@pytest.mark.parametrize("glue", [False, True], ids=["operator", "operator+gate_residual"])
+def test_config5_model_float32_latest_k(ref, glue):
     model_mod, RavelConfig, deferred = ref
     torch.manual_seed(1)
     model = model_mod.RavelLM(cfg5(RavelConfig, use_sum_read=False)).cuda()
     x, y = _tokens(4, 1024, 1024, seed=6)
-    _compare(model_mod, model, deferred, x, y, 0.0, 1e-4, exact_logits=True)
+    _compare(model_mod, model, deferred, x, y, 0.0, 1e-4, exact_logits=True, glue=glue)
 
 
 def test_config5_layer_float32_with_sum_read(ref):

@@ -260,8 +260,17 @@ def test_torch_compile_fullgraph_matches_eager(ref):
             clear_tape_cache()
             p = p0.clone().requires_grad_(True)
             vals, mask, sums, smask = fn(w, p, reads, m)
+            # each lookup's gradient on its own (two backward passes), then both in one pass;
+            # the compiled graph adds the two gradients with one elementwise add, as eager
+            # autograd does when they come from separate passes
+            g_lk = torch.autograd.grad(vals, p, gv, retain_graph=True)[0]
+            g_ss = torch.autograd.grad(sums, p, gs, retain_graph=True)[0]
             torch.autograd.backward([vals, sums], [gv, gs])
-            results.append((vals.detach(), mask, sums.detach(), smask, p.grad))
+            results.append((vals.detach(), mask, sums.detach(), smask, g_lk, g_ss, g_lk + g_ss, p.grad))
+    names = ("values", "mask", "sums", "sum mask", "latest-k gradient", "sum gradient", "summed gradients")
     for eager, compiled in zip(results[:2], results[2:]):
-        for a, b, what in zip(eager, compiled, ("values", "mask", "sums", "sum mask", "payload gradient")):
+        for a, b, what in zip(eager, compiled, names):
             _assert_bits(b, a, f"compiled {what}")
+        _assert_bits(compiled[7], eager[6], "compiled one-pass gradient vs the eager sum of the two")
+        # eager's one pass adds the latest-k gradient inside its kernel: one rounding fewer
+        _assert_close(eager[7], eager[6], 1e-6, "eager one-pass gradient")
