@@ -221,6 +221,33 @@ int ravel_segsum_fwd_noalloc(const void* waddr, const void* raddr, int addr_dtyp
                              uint8_t* out_mask, void* stream);
 
 /*
+ * Literal address families of a memory layer (literal_addresses_from_tokens,
+ * ravel_lm/model.py:195-231): out[b, t, j] for j < n_heads, int64, from token
+ * ids [B, T] (int64), each family modulo A (floor), previous tokens before the
+ * start taken as bos_token_id.  Bit for bit the reference's values.
+ */
+int ravel_literal_addresses(const int64_t* tokens, int64_t B, int64_t T, int n_heads, int64_t bos_token_id,
+                            int64_t A, int64_t* out, void* stream);
+
+/*
+ * ravel_tape_build for a memory layer, straight from its token ids: head c <
+ * n_literal takes literal address family c of the tokens (as
+ * ravel_literal_addresses computes it), head c >= n_literal the learned address
+ * learned_write[b, t, c - n_literal] (reads: learned_read) -- the concatenation
+ * of ravel_lm/model.py:347-349 followed by the sort of
+ * ravel_lm/ravel_memory.py:126-159, with the literal hashing done in the sort's
+ * key build and no [B, T, C] address tensor materialised.  learned_* are
+ * [B, T, C - n_literal] int32/int64 (learned_dtype); NULL when C == n_literal.
+ * When tape_flags != 0, read_addr_out [B, T, C] int32 receives every read's
+ * folded address; pass it as raddr (RAVEL_I32) to the lookup entry points that
+ * use this tape.  A must be below 2^31.
+ */
+int ravel_tape_build_tokens(const int64_t* tokens, int n_literal, int64_t bos_token_id, const void* learned_write,
+                            const void* learned_read, int learned_dtype, const uint8_t* wmask, int64_t B, int64_t T,
+                            int64_t C, int64_t A, int tape_flags, int32_t* read_addr_out, void* tape,
+                            size_t tape_bytes, void* scratch, size_t scratch_bytes, void* stream);
+
+/*
  * Gate residual of a memory layer, out = x + sigmoid(gate) * fused, elementwise
  * over n elements of float32 or bfloat16 (gate_residual,
  * ravel_lm/triton_block.py:383-387, called at ravel_lm/model.py:388).  Same

@@ -11,7 +11,10 @@ from .ravel_memory import (  # noqa: F401
     _composite_key_dtype,
     causal_last_k_lookup,
     causal_sum_lookup,
+    literal_addresses_from_tokens,
+    memory_lookups,
 )
 
-__all__ = ["RavelLayerCache", "causal_last_k_lookup", "causal_sum_lookup"]
+__all__ = ["RavelLayerCache", "causal_last_k_lookup", "causal_sum_lookup", "literal_addresses_from_tokens",
+           "memory_lookups"]
 __version__ = "0.1.0"

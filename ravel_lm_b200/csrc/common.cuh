@@ -90,6 +90,51 @@ __device__ __forceinline__ uint64_t fold_addr(int64_t a, int64_t A, int key32) {
     return static_cast<uint64_t>(r);
 }
 
+// torch's remainder of an int64 by a positive A (floor modulo).
+__device__ __forceinline__ int64_t floor_mod(int64_t x, int64_t A) {
+    const int64_t r = x % A;
+    return r < 0 ? r + A : r;
+}
+
+// Literal address family j of token t in batch row b (ravel_lm/model.py:195-231):
+//   0: tok;  1: prev1*257 + tok*131 + 17;  2: prev2*65537 + prev1*257 + tok*131 + 31;
+//   j >= 3: tok*(1009 + 2j) + t*(9176 + j) + 97j;  all mod A (floor), with the
+// previous tokens taken as bos before the sequence starts.  The products wrap in
+// 64 bits, as torch's int64 arithmetic does.
+__device__ __forceinline__ int64_t literal_addr(const int64_t* tokens, int64_t T, int64_t b, int64_t t, int j,
+                                                int64_t bos, int64_t A) {
+    const int64_t* row = tokens + b * T;
+    const uint64_t x = static_cast<uint64_t>(row[t]);
+    if (j == 0) return floor_mod(static_cast<int64_t>(x), A);
+    const uint64_t p1 = static_cast<uint64_t>(t >= 1 ? row[t - 1] : bos);
+    if (j == 1) return floor_mod(static_cast<int64_t>(p1 * 257u + x * 131u + 17u), A);
+    const uint64_t p2 = static_cast<uint64_t>(t >= 2 ? row[t - 2] : bos);
+    if (j == 2) return floor_mod(static_cast<int64_t>(p2 * 65537u + p1 * 257u + x * 131u + 31u), A);
+    const uint64_t uj = static_cast<uint64_t>(j);
+    return floor_mod(static_cast<int64_t>(x * (1009u + 2u * uj) + static_cast<uint64_t>(t) * (9176u + uj) + uj * 97u),
+                     A);
+}
+
+// Where the address of event (b, t, c) comes from: a [B, T, C] integer tensor, or
+// (token mode, tokens != null) the literal families of the token ids for the
+// first `lit` heads and a [B, T, C - lit] tensor of learned addresses for the rest
+// -- the concatenation of ravel_lm/model.py:347-349, never materialised.
+struct AddrSrc {
+    const void* addr;       // plain: [B, T, C]; token mode: [B, T, C - lit] (null when C == lit)
+    int i64;                // addr holds int64 (else int32)
+    const int64_t* tokens;  // token mode: [B, T] token ids
+    int lit;
+    int64_t bos;
+};
+
+__device__ __forceinline__ int64_t src_addr(const AddrSrc& s, int64_t b, int64_t t, int64_t c, int64_t T,
+                                            int64_t C, int64_t A) {
+    if (s.tokens == nullptr) return load_addr(s.addr, (b * T + t) * C + c, s.i64);
+    if (c < s.lit) return literal_addr(s.tokens, T, b, t, static_cast<int>(c), s.bos, A);
+    const int64_t Cl = C - s.lit;
+    return load_addr(s.addr, (b * T + t) * Cl + (c - s.lit), s.i64);
+}
+
 // Decode-cache addresses are clamped, not wrapped (ravel_memory.py:276, :289).
 __device__ __forceinline__ int64_t clamp_addr(int64_t a, int64_t A) {
     return a < 0 ? 0 : (a > A - 1 ? A - 1 : a);

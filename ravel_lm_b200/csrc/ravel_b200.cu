@@ -359,16 +359,18 @@ int sort_streams(const SortArgs& a0, void* out, void* other, int64_t S, int64_t 
     return RAVEL_OK;
 }
 
-int tape_build(const void* waddr, const void* raddr, int addr_dtype, const uint8_t* wmask, int64_t B,
-               int64_t T, int64_t C, int64_t A, int flags, void* tape, size_t tape_bytes, void* scratch,
-               size_t scratch_bytes, cudaStream_t st) {
+// Sort the writes (and for general tapes the reads) of every stream.  `wsrc` /
+// `rsrc` say where addresses come from; `raddr_out`, when given, receives the
+// folded read addresses as int32 [B, T, C] (the reads' own pass for general
+// reads, else the writes' pass).
+int tape_build_src(const AddrSrc& wsrc, const AddrSrc& rsrc, int32_t* raddr_out, const uint8_t* wmask,
+                   int64_t B, int64_t T, int64_t C, int64_t A, int flags, void* tape, size_t tape_bytes,
+                   void* scratch, size_t scratch_bytes, cudaStream_t st) {
     if (int e = check_sizes(B, T, C, 0, A)) return e;
-    if (addr_dtype != RAVEL_I32 && addr_dtype != RAVEL_I64) return RAVEL_ERR_INVALID_ARG;
     if ((flags & RAVEL_TAPE_WRITE_MASK) && wmask == nullptr) return RAVEL_ERR_INVALID_ARG;
-    if ((flags & RAVEL_TAPE_GENERAL_READS) && raddr == nullptr) return RAVEL_ERR_INVALID_ARG;
     const int64_t S = B * C, N = B * T * C;
     if (N == 0) return RAVEL_OK;
-    if (waddr == nullptr || tape == nullptr) return RAVEL_ERR_INVALID_ARG;
+    if (tape == nullptr) return RAVEL_ERR_INVALID_ARG;
     const TapeLayout tl = tape_layout(B, T, C, A, flags);
     const ScratchLayout sl = scratch_layout(B, T, C, 0, A, RAVEL_F32, flags);
     if (tape_bytes < tl.total) return RAVEL_ERR_WORKSPACE;
@@ -378,9 +380,10 @@ int tape_build(const void* waddr, const void* raddr, int addr_dtype, const uint8
     if (tl.has_mask && cudaMemsetAsync(tv.nvalid, 0, S * sizeof(int), st) != cudaSuccess) return RAVEL_ERR_CUDA;
 
     SortArgs a;
-    a.waddr = waddr;
+    std::memset(&a, 0, sizeof(a));
+    a.src = wsrc;
+    a.addr_out = (flags & RAVEL_TAPE_GENERAL_READS) ? nullptr : raddr_out;
     a.wmask = tl.has_mask ? wmask : nullptr;
-    a.addr_i64 = addr_dtype == RAVEL_I64;
     a.key32 = key32_of(B, T, C, A);
     a.B = B; a.T = T; a.C = C; a.A = A;
     a.tbits = tl.kl.tbits; a.abits = tl.kl.abits; a.mbit = tl.kl.mbit;
@@ -397,7 +400,8 @@ int tape_build(const void* waddr, const void* raddr, int addr_dtype, const uint8
             // read tape: the reads sorted like the writes (by address, t), then ranked
             // against the sorted writes; the rank is each read's latest earlier write
             SortArgs ra = a;
-            ra.waddr = (raddr != nullptr) ? raddr : waddr;
+            ra.src = (flags & RAVEL_TAPE_GENERAL_READS) ? rsrc : wsrc;
+            ra.addr_out = (flags & RAVEL_TAPE_GENERAL_READS) ? raddr_out : nullptr;
             ra.wmask = nullptr;
             ra.nvalid = nullptr;
             ra.mbit = 0;
@@ -411,6 +415,24 @@ int tape_build(const void* waddr, const void* raddr, int addr_dtype, const uint8
         return RAVEL_OK;
     });
     return rc;
+}
+
+AddrSrc plain_src(const void* addr, int addr_dtype) {
+    AddrSrc s;
+    std::memset(&s, 0, sizeof(s));
+    s.addr = addr;
+    s.i64 = addr_dtype == RAVEL_I64;
+    return s;
+}
+
+int tape_build(const void* waddr, const void* raddr, int addr_dtype, const uint8_t* wmask, int64_t B,
+               int64_t T, int64_t C, int64_t A, int flags, void* tape, size_t tape_bytes, void* scratch,
+               size_t scratch_bytes, cudaStream_t st) {
+    if (addr_dtype != RAVEL_I32 && addr_dtype != RAVEL_I64) return RAVEL_ERR_INVALID_ARG;
+    if ((flags & RAVEL_TAPE_GENERAL_READS) && raddr == nullptr) return RAVEL_ERR_INVALID_ARG;
+    if (B * T * C != 0 && waddr == nullptr) return RAVEL_ERR_INVALID_ARG;
+    return tape_build_src(plain_src(waddr, addr_dtype), plain_src(raddr ? raddr : waddr, addr_dtype), nullptr,
+                          wmask, B, T, C, A, flags, tape, tape_bytes, scratch, scratch_bytes, st);
 }
 
 // ------------------------------------------------------------------ latest-k
@@ -894,8 +916,7 @@ int cache_prefill(void* values, uint8_t* filled, const void* addr, int addr_dtyp
     char* sc = static_cast<char*>(scratch);
     SortArgs a;
     std::memset(&a, 0, sizeof(a));
-    a.waddr = addr;
-    a.addr_i64 = addr_dtype == RAVEL_I64;
+    a.src = plain_src(addr, addr_dtype);
     a.key32 = 0;
     a.B = B; a.T = T; a.C = C; a.A = A;
     a.tbits = pl.kl.tbits; a.abits = pl.kl.abits; a.mbit = 0;
@@ -1010,6 +1031,43 @@ int elem_vec_ok(int64_t n, int esize, std::initializer_list<const void*> ptrs) {
 using namespace ravel;
 
 extern "C" {
+
+int ravel_tape_build_tokens(const int64_t* tokens, int n_literal, int64_t bos_token_id, const void* learned_write,
+                            const void* learned_read, int learned_dtype, const uint8_t* wmask, int64_t B, int64_t T,
+                            int64_t C, int64_t A, int tape_flags, int32_t* read_addr_out, void* tape,
+                            size_t tape_bytes, void* scratch, size_t scratch_bytes, void* stream) {
+    if (n_literal < 0 || n_literal > C) return RAVEL_ERR_INVALID_ARG;
+    if (learned_dtype != RAVEL_I32 && learned_dtype != RAVEL_I64) return RAVEL_ERR_INVALID_ARG;
+    if (B * T * C == 0) return RAVEL_OK;
+    if (tokens == nullptr) return RAVEL_ERR_INVALID_ARG;
+    if (n_literal < C && learned_write == nullptr) return RAVEL_ERR_INVALID_ARG;
+    if (n_literal < C && (tape_flags & RAVEL_TAPE_GENERAL_READS) && learned_read == nullptr)
+        return RAVEL_ERR_INVALID_ARG;
+    if (tape_flags != 0 && read_addr_out == nullptr) return RAVEL_ERR_INVALID_ARG;
+    if (A > 2147483647) return RAVEL_ERR_UNSUPPORTED;  // folded read addresses are stored as int32
+    AddrSrc w;
+    std::memset(&w, 0, sizeof(w));
+    w.addr = learned_write;
+    w.i64 = learned_dtype == RAVEL_I64;
+    w.tokens = tokens;
+    w.lit = n_literal;
+    w.bos = bos_token_id;
+    AddrSrc r = w;
+    if (tape_flags & RAVEL_TAPE_GENERAL_READS) r.addr = learned_read;
+    return tape_build_src(w, r, read_addr_out, wmask, B, T, C, A, tape_flags, tape, tape_bytes, scratch,
+                          scratch_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int ravel_literal_addresses(const int64_t* tokens, int64_t B, int64_t T, int n_heads, int64_t bos_token_id,
+                            int64_t A, int64_t* out, void* stream) {
+    if (B < 0 || T < 0 || n_heads < 0 || A <= 0) return RAVEL_ERR_INVALID_ARG;
+    const int64_t n = B * T * n_heads;
+    if (n == 0) return RAVEL_OK;
+    if (tokens == nullptr || out == nullptr) return RAVEL_ERR_INVALID_ARG;
+    k_literal_addresses<<<grid_cap((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        tokens, B, T, n_heads, bos_token_id, A, out);
+    return check_launch();
+}
 
 int ravel_gate_residual_fwd(const void* x, const void* gate, const void* fused, void* out, int64_t n, int dtype,
                             void* stream) {

@@ -27,9 +27,9 @@
 namespace ravel {
 
 struct SortArgs {
-    const void* waddr;
+    AddrSrc src;           // where the events' addresses come from
+    int32_t* addr_out;     // [B, T, C]: the folded addresses are stored here too, or null
     const uint8_t* wmask;  // [B, T] or null
-    int addr_i64;
     int key32;             // reference key dtype is int32 (address truncation)
     int64_t B, T, C, A;
     int tbits, abits, mbit;
@@ -46,9 +46,9 @@ template <typename KeyT>
 __device__ __forceinline__ KeyT sort_key(const SortArgs& a, int64_t b, int64_t c, int64_t s, int64_t t,
                                          int& nvalid_local) {
     (void)s;
-    const int64_t row = (b * a.T + t) * a.C + c;
-    const int64_t raw = load_addr(a.waddr, row, a.addr_i64);
+    const int64_t raw = src_addr(a.src, b, t, c, a.T, a.C, a.A);
     const uint64_t ad = a.clamp ? static_cast<uint64_t>(clamp_addr(raw, a.A)) : fold_addr(raw, a.A, a.key32);
+    if (a.addr_out != nullptr) a.addr_out[(b * a.T + t) * a.C + c] = static_cast<int32_t>(ad);
     const bool valid = a.wmask == nullptr || a.wmask[b * a.T + t] != 0;
     if (valid) {
         ++nvalid_local;
@@ -445,5 +445,21 @@ __global__ void __launch_bounds__(256) k_merge_ranks(const KeyT* wkeys, const in
         }
     }
 }
+
+// ------------------------------------------------------------------ literal addresses
+// literal_addresses_from_tokens (ravel_lm/model.py:195-231): out [B, T, L] int64,
+// one thread per element.
+__global__ void k_literal_addresses(const int64_t* __restrict__ tokens, int64_t B, int64_t T, int L, int64_t bos,
+                                    int64_t A, int64_t* __restrict__ out) {
+    const int64_t n = B * T * L;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t bt = i / L;
+        const int j = static_cast<int>(i - bt * L);
+        const int64_t b = bt / T, t = bt - (bt / T) * T;
+        out[i] = literal_addr(tokens, T, b, t, j, bos, A);
+    }
+}
+
 
 }  // namespace ravel

@@ -233,15 +233,32 @@ def _build_tape(write: Tensor, read: Optional[Tensor], write_mask: Optional[Tens
 
 
 # ------------------------------------------------------------------ latest-k custom ops
+class _TokenTape:
+    """A tape built from token ids (``ravel_tape_build_tokens``) and its reads' folded addresses."""
+
+    def __init__(self, tape: Tensor, raddr: Tensor, flags: int, shape: Tuple[int, int, int]):
+        self.tape, self.raddr, self.flags, self.shape = tape, raddr, flags, shape
+
+
+def _tape_of(write, read, write_mask, address_space, D, k, dcode, device, prebuilt):
+    if prebuilt is None:
+        return _build_tape(write, read, write_mask, address_space, D, k, dcode, device)
+    B, T, C = prebuilt.shape
+    scratch = torch.empty(scratch_bytes(B, T, C, D, address_space, k, dcode, prebuilt.flags), dtype=torch.uint8,
+                          device=device)
+    return prebuilt.tape, scratch, prebuilt.raddr, _lib.RAVEL_I32, prebuilt.flags
+
+
 def _latestk_fwd_impl(write: Tensor, payload: Tensor, read: Optional[Tensor], write_mask: Optional[Tensor],
-                      address_space: int, k: int) -> Tuple[Tensor, Tensor, Tensor]:
-    B, T, C = write.shape
+                      address_space: int, k: int, prebuilt: Optional[_TokenTape] = None
+                      ) -> Tuple[Tensor, Tensor, Tensor]:
+    B, T, C = write.shape if prebuilt is None else prebuilt.shape
     D = payload.shape[-1]
     device = _require_cuda(write, payload, read, write_mask)
     vals = payload.new_empty(B, T, C, k, D)
     mask = torch.empty(B, T, C, k, dtype=torch.bool, device=device)
-    tape, _scratch, r, code, flags = _build_tape(write, read, write_mask, address_space, D, k,
-                                                 _payload_code(payload), device)
+    tape, _scratch, r, code, flags = _tape_of(write, read, write_mask, address_space, D, k, _payload_code(payload),
+                                              device, prebuilt)
     p = payload.contiguous()
     _lib.call("ravel_latestk_fwd_tape", tape.data_ptr(), flags, r.data_ptr() if flags else None, code,
               p.data_ptr(), _payload_code(p), B, T, C, D, address_space, k, vals.data_ptr(), mask.data_ptr(),
@@ -320,14 +337,14 @@ _latestk_fwd.register_autograd(_latestk_backward, setup_context=_latestk_setup)
 
 # ------------------------------------------------------------------ sum custom ops
 def _segsum_fwd_impl(write: Tensor, payload: Tensor, read: Optional[Tensor], write_mask: Optional[Tensor],
-                     address_space: int) -> Tuple[Tensor, Tensor, Tensor]:
-    B, T, C = write.shape
+                     address_space: int, prebuilt: Optional[_TokenTape] = None) -> Tuple[Tensor, Tensor, Tensor]:
+    B, T, C = write.shape if prebuilt is None else prebuilt.shape
     D = payload.shape[-1]
     device = _require_cuda(write, payload, read, write_mask)
     sums = payload.new_empty(B, T, C, D)
     mask = torch.empty(B, T, C, dtype=torch.bool, device=device)
-    tape, scratch, r, code, flags = _build_tape(write, read, write_mask, address_space, D, 1,
-                                                _payload_code(payload), device)
+    tape, scratch, r, code, flags = _tape_of(write, read, write_mask, address_space, D, 1, _payload_code(payload),
+                                             device, prebuilt)
     p = payload.contiguous()
     _lib.call("ravel_segsum_fwd_tape", tape.data_ptr(), flags, r.data_ptr() if flags else None, code,
               p.data_ptr(), _payload_code(p), B, T, C, D, address_space, sums.data_ptr(), mask.data_ptr(),
@@ -417,10 +434,14 @@ _segsum_fwd.register_autograd(_segsum_backward, setup_context=_segsum_setup)
 # nodes in the other order) each backward returns its own gradient as usual.
 class _LatestKFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, write, payload, read, write_mask, address_space, k):
-        vals, mask, tape = _latestk_fwd_impl(write, payload, read, write_mask, address_space, k)
-        ctx.save_for_backward(tape, write if read is None else read)
-        ctx.meta = (_flags(read, write_mask), *write.shape, int(address_space), int(k))
+    def forward(ctx, write, payload, read, write_mask, address_space, k, prebuilt=None):
+        vals, mask, tape = _latestk_fwd_impl(write, payload, read, write_mask, address_space, k, prebuilt)
+        if prebuilt is None:
+            ctx.save_for_backward(tape, write if read is None else read)
+            ctx.meta = (_flags(read, write_mask), *write.shape, int(address_space), int(k))
+        else:
+            ctx.save_for_backward(tape, prebuilt.raddr)
+            ctx.meta = (prebuilt.flags, *prebuilt.shape, int(address_space), int(k))
         ctx.ravel_stash = None
         ctx.mark_non_differentiable(mask)
         ctx.set_materialize_grads(False)
@@ -433,19 +454,23 @@ class _LatestKFn(torch.autograd.Function):
         if stash is not None and stash[0] == torch._C._current_graph_task_id():
             acc = stash[1]  # the sum lookup's payload gradient, handed over in this same pass
         if grad_vals is None:
-            return None, acc, None, None, None, None
+            return None, acc, None, None, None, None, None
         tape, raddr = ctx.saved_tensors
         flags, B, T, C, A, k = ctx.meta
         grad = _latestk_bwd_impl(tape, grad_vals, raddr, flags, B, T, C, A, k, accumulate_into=acc)
-        return None, grad, None, None, None, None
+        return None, grad, None, None, None, None, None
 
 
 class _SegSumFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, write, payload, read, write_mask, address_space, partner):
-        sums, mask, tape = _segsum_fwd_impl(write, payload, read, write_mask, address_space)
-        ctx.save_for_backward(tape, write if read is None else read)
-        ctx.meta = (_flags(read, write_mask), *write.shape, int(address_space))
+    def forward(ctx, write, payload, read, write_mask, address_space, partner, prebuilt=None):
+        sums, mask, tape = _segsum_fwd_impl(write, payload, read, write_mask, address_space, prebuilt)
+        if prebuilt is None:
+            ctx.save_for_backward(tape, write if read is None else read)
+            ctx.meta = (_flags(read, write_mask), *write.shape, int(address_space))
+        else:
+            ctx.save_for_backward(tape, prebuilt.raddr)
+            ctx.meta = (prebuilt.flags, *prebuilt.shape, int(address_space))
         ctx.partner = partner
         ctx.mark_non_differentiable(mask)
         ctx.set_materialize_grads(False)
@@ -454,7 +479,7 @@ class _SegSumFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_sums, _gm):
         if grad_sums is None:
-            return None, None, None, None, None, None
+            return None, None, None, None, None, None, None
         tape, raddr = ctx.saved_tensors
         flags, B, T, C, A = ctx.meta
         grad = _segsum_bwd_impl(tape, grad_sums, raddr, flags, B, T, C, A)
@@ -462,8 +487,8 @@ class _SegSumFn(torch.autograd.Function):
         if (node is not None and not torch.is_grad_enabled() and getattr(node, "ravel_stash", 1) is None
                 and torch._C._will_engine_execute_node(node)):
             node.ravel_stash = (torch._C._current_graph_task_id(), grad)
-            return None, None, None, None, None, None
-        return None, grad, None, None, None, None
+            return None, None, None, None, None, None, None
+        return None, grad, None, None, None, None, None
 
 
 # ------------------------------------------------------------------ public API
@@ -671,5 +696,133 @@ class RavelLayerCache:
         return vals, mask
 
 
+# ------------------------------------------------------------------ memory-layer addresses from token ids
+@torch.library.custom_op("ravel_b200::literal_addresses", mutates_args=())
+def _literal_addresses(token_ids: Tensor, address_space: int, n_heads: int, bos_token_id: int) -> Tensor:
+    B, T = token_ids.shape
+    device = _require_cuda(token_ids)
+    toks = token_ids.to(torch.int64).contiguous()
+    out = torch.empty(B, T, n_heads, dtype=torch.int64, device=device)
+    _lib.call("ravel_literal_addresses", toks.data_ptr(), B, T, n_heads, bos_token_id, address_space, out.data_ptr(),
+              _stream(device))
+    return out
+
+
+@_literal_addresses.register_fake
+def _literal_addresses_fake(token_ids, address_space, n_heads, bos_token_id):
+    return torch.empty(*token_ids.shape, n_heads, dtype=torch.int64, device=token_ids.device)
+
+
+def literal_addresses_from_tokens(token_ids: Tensor, *, address_space: int, n_heads: int,
+                                  bos_token_id: int) -> Tensor:
+    """Literal address families from token ids (ravel_lm/model.py:195-231), one kernel.
+
+    Heads, in order: the token id; a rolling bigram hash; a rolling trigram hash;
+    token/position mixed hashes; each modulo ``address_space``.  Returns
+    [B, T, n_heads] int64, equal to the reference's values.
+    """
+    if token_ids.ndim != 2:
+        raise ValueError("token_ids must have shape [B,T]")
+    if int(address_space) <= 0:
+        raise ValueError("address_space must be positive")
+    B, T = token_ids.shape
+    if B * T * int(n_heads) == 0:
+        return torch.empty(B, T, int(n_heads), dtype=torch.long, device=token_ids.device)
+    return _literal_addresses(token_ids, int(address_space), int(n_heads), int(bos_token_id))
+
+
+def memory_lookups(token_ids: Tensor, payloads: Tensor, learned_write: Optional[Tensor] = None,
+                   learned_read: Optional[Tensor] = None, *, address_space: int, n_literal_heads: int,
+                   bos_token_id: int, k: int = 1, use_sum_read: bool = False, write_mask: Optional[Tensor] = None
+                   ) -> Tuple[Tensor, Tensor, Optional[Tensor], Optional[Tensor]]:
+    """The lookups of one memory layer, addressed from its token ids.
+
+    Equal to what ``RavelMemoryLayer.forward`` (ravel_lm/model.py:333-384) computes
+    with this package's three functions::
+
+        literal = literal_addresses_from_tokens(token_ids, address_space=A, n_heads=L, bos_token_id=bos)
+        write = torch.cat([literal, learned_write], -1); read = torch.cat([literal, learned_read], -1)
+        values, mask = causal_last_k_lookup(write, payloads, read, address_space=A, k=k, write_mask=m)
+        sums, smask = causal_sum_lookup(write, payloads, read, address_space=A, write_mask=m)
+
+    but the literal heads are hashed inside the sort's key build
+    (``ravel_tape_build_tokens``): no [B, T, C] address tensor is made, one sort
+    serves both lookups, and one backward pass writes the payload gradient once.
+
+    Args:
+        token_ids:     [B, T] integer token ids.
+        payloads:      [B, T, C, D] with C = n_literal_heads + learned heads.
+        learned_write: [B, T, C - n_literal_heads] integer addresses of the learned
+                       heads' writes (None when every head is literal).
+        learned_read:  the same for reads; None (or the write tensor) reads where it writes.
+        use_sum_read:  also return the segmented sums.
+    Returns:
+        values [B, T, C, k, D], mask [B, T, C, k], and sums [B, T, C, D] and their
+        mask [B, T, C] (None, None without ``use_sum_read``).
+    """
+    if token_ids.ndim != 2 or payloads.ndim != 4:
+        raise ValueError("expected token_ids [B,T] and payloads [B,T,C,D]")
+    B, T = token_ids.shape
+    L = int(n_literal_heads)
+    C = payloads.shape[2]
+    if payloads.shape[:2] != (B, T) or not 0 <= L <= C:
+        raise ValueError("payloads must be [B, T, C, D] with C >= n_literal_heads")
+    if (learned_write is None) != (C == L):
+        raise ValueError("learned_write must be given exactly when there are learned heads")
+    for t in (learned_write, learned_read):
+        if t is not None and tuple(t.shape) != (B, T, C - L):
+            raise ValueError("learned addresses must have shape [B, T, C - n_literal_heads]")
+    if k <= 0:
+        raise ValueError("k must be positive")
+    if write_mask is not None and write_mask.shape != (B, T):
+        raise ValueError("write_mask must have shape [B, T]")
+    A = int(address_space)
+    if A <= 0 or A > 2**31 - 1:
+        raise ValueError("address_space must be in [1, 2^31 - 1]")
+    if torch.compiler.is_compiling() or B * T * C == 0:
+        lit = literal_addresses_from_tokens(token_ids, address_space=A, n_heads=L, bos_token_id=bos_token_id)
+        write = lit if learned_write is None else torch.cat([lit, learned_write.to(torch.int64)], -1)
+        read = None
+        if learned_read is not None and learned_read is not learned_write:
+            read = torch.cat([lit, learned_read.to(torch.int64)], -1)
+        vals, mask = causal_last_k_lookup(write, payloads, read, address_space=A, k=k, write_mask=write_mask)
+        if not use_sum_read:
+            return vals, mask, None, None
+        sums, smask = causal_sum_lookup(write, payloads, read, address_space=A, write_mask=write_mask)
+        return vals, mask, sums, smask
+    device = _require_cuda(token_ids, payloads, learned_write, learned_read, write_mask)
+    toks = token_ids.to(torch.int64).contiguous()
+    lw = lr = None
+    code = _lib.RAVEL_I64
+    if learned_write is not None:
+        lw, code = _addr(learned_write)
+        lr = lw
+        if learned_read is not None and not _aliases(learned_read, learned_write):
+            lr, rcode = _addr(learned_read)
+            if rcode != code:
+                lw, lr, code = lw.to(torch.int64), lr.to(torch.int64), _lib.RAVEL_I64
+    general = lr is not None and lr is not lw
+    flags = (_lib.RAVEL_TAPE_GENERAL_READS if general else 0) | (_lib.RAVEL_TAPE_WRITE_MASK if write_mask is not None
+                                                                else 0)
+    m = None if write_mask is None else write_mask.to(torch.bool).contiguous()
+    D = payloads.shape[-1]
+    tape = torch.empty(tape_bytes(B, T, C, A, flags), dtype=torch.uint8, device=device)
+    scratch = torch.empty(scratch_bytes(B, T, C, D, A, k, _payload_code(payloads), flags), dtype=torch.uint8,
+                          device=device)
+    raddr = torch.empty((B, T, C) if flags else (0,), dtype=torch.int32, device=device)
+    _lib.call("ravel_tape_build_tokens", toks.data_ptr(), L, int(bos_token_id), _ptr(lw), _ptr(lr), code, _ptr(m),
+              B, T, C, A, flags, raddr.data_ptr() if flags else None, tape.data_ptr(), tape.numel(),
+              scratch.data_ptr(), scratch.numel(), _stream(device))
+    pre = _TokenTape(tape, raddr, flags, (B, T, C))
+    vals, mask = _LatestKFn.apply(None, payloads, None, m, A, int(k), pre)
+    if not use_sum_read:
+        return vals, mask, None, None
+    partner = None
+    if vals.grad_fn is not None and torch.is_grad_enabled():
+        partner = weakref.ref(vals.grad_fn)
+    sums, smask = _SegSumFn.apply(None, payloads, None, m, A, partner, pre)
+    return vals, mask, sums, smask
+
+
 __all__ = ["RavelLayerCache", "causal_last_k_lookup", "causal_sum_lookup", "clear_tape_cache",
-           "_composite_key_dtype"]
+           "literal_addresses_from_tokens", "memory_lookups", "_composite_key_dtype"]
