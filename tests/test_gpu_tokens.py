@@ -47,6 +47,8 @@ def _bits(t):
 def test_literal_addresses_equal_the_reference(ref_model, n_heads, T):
     model, _ = ref_model
     from ravel_lm_b200 import literal_addresses_from_tokens
+    if T == 1 and n_heads >= 3:
+        pytest.skip("the reference's trigram head needs T >= 2 (its prev2 has two columns)")
     g = torch.Generator(device="cuda").manual_seed(T * 10 + n_heads)
     toks = torch.randint(0, 1024, (3, T), generator=g, device="cuda")
     toks[0, ::3] = torch.randint(-(1 << 62), 1 << 62, toks[0, ::3].shape, generator=g, device="cuda")  # wraps
