@@ -248,6 +248,35 @@ int ravel_tape_build_tokens(const int64_t* tokens, int n_literal, int64_t bos_to
                             size_t tape_bytes, void* scratch, size_t scratch_bytes, void* stream);
 
 /*
+ * Latest-k source table from a built tape: src[(b*T + t)*C + c][j] = the flat
+ * payload row ((b*T + t')*C + c) of read (b, t, c)'s j-th latest earlier write,
+ * -1 for an invalid slot (the rows ravel_lm/ravel_memory.py:173-174 gathers).
+ * src is [B*T*C, k] int32.  raddr as for ravel_latestk_fwd_tape.
+ */
+int ravel_latestk_sources(const void* tape, int tape_flags, const void* raddr, int addr_dtype, int64_t B, int64_t T,
+                          int64_t C, int64_t A, int64_t k, int32_t* src, void* stream);
+
+/*
+ * A memory layer's read-out, fused: out[n] = A[n] * W^T with the read rows
+ * A[n] = [payload[src[n, c, j]] for c < C, j < k (zero for -1) | sums[n, c] for
+ * c < C] -- torch.cat of the latest-k values and sums (ravel_lm/model.py:383-385)
+ * followed by fast_linear (:386) -- without A ever being written: a tcgen05
+ * kernel (kind::tf32: TF32 inputs, float32 accumulation) gathers every A tile
+ * into shared memory.  payload [B*T*C, D], sums [B*T, C, D] or NULL (no sum
+ * read), weight [N, K] with K = C*k*D (+ C*D), all float32, D a multiple of 4,
+ * 16-byte aligned.  With x and gate ([B*T, N]) the output is the gate residual
+ * x + sigmoid(gate) * (A * W^T) (ravel_lm/model.py:388), and pre (optional)
+ * receives A * W^T itself.
+ */
+int ravel_gather_gemm(const float* payload, const int32_t* src, const float* sums, int64_t B, int64_t T, int64_t C,
+                      int64_t D, int64_t k, const float* weight, int64_t N, const float* x, const float* gate,
+                      float* out, float* pre, void* stream);
+
+/* The read rows A of ravel_gather_gemm written out ([B*T, K] float32), for its backward. */
+int ravel_gather_rows(const float* payload, const int32_t* src, const float* sums, int64_t B, int64_t T, int64_t C,
+                      int64_t D, int64_t k, float* rows, void* stream);
+
+/*
  * Gate residual of a memory layer, out = x + sigmoid(gate) * fused, elementwise
  * over n elements of float32 or bfloat16 (gate_residual,
  * ravel_lm/triton_block.py:383-387, called at ravel_lm/model.py:388).  Same

@@ -65,6 +65,9 @@ SIGNATURES = {
     "ravel_literal_addresses": (_c_int, [_c_vp, _c_i64, _c_i64, _c_int, _c_i64, _c_i64, _c_vp, _c_vp]),
     "ravel_tape_build_tokens": (_c_int, [_c_vp, _c_int, _c_i64, _c_vp, _c_vp, _c_int, _c_vp] + [_c_i64] * 4 +
                                 [_c_int, _c_vp, _c_vp, _c_sz, _c_vp, _c_sz, _c_vp]),
+    "ravel_latestk_sources": (_c_int, [_c_vp, _c_int, _c_vp, _c_int] + [_c_i64] * 5 + [_c_vp, _c_vp]),
+    "ravel_gather_gemm": (_c_int, [_c_vp, _c_vp, _c_vp] + [_c_i64] * 5 + [_c_vp, _c_i64] + [_c_vp] * 5),
+    "ravel_gather_rows": (_c_int, [_c_vp, _c_vp, _c_vp] + [_c_i64] * 5 + [_c_vp, _c_vp]),
     "ravel_gate_residual_fwd": (_c_int, [_c_vp] * 4 + [_c_i64, _c_int, _c_vp]),
     "ravel_gate_residual_bwd": (_c_int, [_c_vp] * 5 + [_c_i64, _c_int, _c_vp]),
     "ravel_rms_norm_fwd": (_c_int, [_c_vp, _c_vp, ctypes.c_float, _c_vp, _c_vp, _c_i64, _c_i64, _c_int, _c_vp]),

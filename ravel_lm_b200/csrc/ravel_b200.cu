@@ -3,6 +3,8 @@
 // Entry points are declared (and their reference counterparts cited) in
 // include/ravel_b200.h.  This file holds argument validation, the tape and
 // scratch layouts, and the launch plumbing; the kernels live in the headers.
+#include <cudaTypedefs.h>
+
 #include <atomic>
 #include <cstring>
 #include <initializer_list>
@@ -15,6 +17,7 @@
 #include "segsum.cuh"
 #include "cache.cuh"
 #include "glue.cuh"
+#include "gather_gemm.cuh"
 
 namespace ravel {
 namespace {
@@ -1026,11 +1029,116 @@ int elem_vec_ok(int64_t n, int esize, std::initializer_list<const void*> ptrs) {
         if (reinterpret_cast<uintptr_t>(p) % 16 != 0) return 0;
     return 1;
 }
+// ------------------------------------------------------------------ fused gather + fuse Linear
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+int encode_weight_map(CUtensorMap* map, const float* W, int64_t N, int64_t K, int box_rows) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    if (encode == nullptr) {
+        cudaDriverEntryPointQueryResult q;
+        void* fn = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || fn == nullptr)
+            return RAVEL_ERR_CUDA;
+        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 4};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(ravel::GG_BK), static_cast<cuuint32_t>(box_rows)};
+    cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(W), dims, strides, box,
+                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? RAVEL_OK : RAVEL_ERR_CUDA;
+}
+
+int gather_args(ravel::GatherArgs& g, const float* payload, const int32_t* src, const float* sums, int64_t B, int64_t T,
+                int64_t C, int64_t D, int64_t k) {
+    if (B < 0 || T < 0 || C <= 0 || D <= 0 || k <= 0) return RAVEL_ERR_INVALID_ARG;
+    if (D % 4 != 0) return RAVEL_ERR_UNSUPPORTED;  // 16-byte pieces stay inside one slot
+    const int64_t K = C * k * D + (sums ? C * D : 0);
+    if (K > (int64_t{1} << 30) || B * T * C >= 2147483647LL) return RAVEL_ERR_UNSUPPORTED;
+    if (payload == nullptr || src == nullptr) return RAVEL_ERR_INVALID_ARG;
+    if (ravel::addr_bits(payload) % 16 || (sums && ravel::addr_bits(sums) % 16)) return RAVEL_ERR_INVALID_ARG;
+    g.payload = payload; g.src = src; g.sums = sums;
+    g.M = B * T;
+    g.C = static_cast<int>(C); g.k = static_cast<int>(k); g.D = static_cast<int>(D); g.K = static_cast<int>(K);
+    return RAVEL_OK;
+}
 }  // namespace
 
 using namespace ravel;
 
 extern "C" {
+
+int ravel_latestk_sources(const void* tape, int tape_flags, const void* raddr, int addr_dtype, int64_t B, int64_t T,
+                          int64_t C, int64_t A, int64_t k, int32_t* src, void* stream) {
+    if (int e = check_sizes(B, T, C, 0, A)) return e;
+    if (k <= 0) return RAVEL_ERR_INVALID_ARG;
+    if (k > 512) return RAVEL_ERR_UNSUPPORTED;
+    const int64_t N = B * T * C;
+    if (N == 0) return RAVEL_OK;
+    if (tape == nullptr || src == nullptr) return RAVEL_ERR_INVALID_ARG;
+    const TapeLayout tl = tape_layout(B, T, C, A, tape_flags);
+    if (tl.general && raddr == nullptr) return RAVEL_ERR_INVALID_ARG;
+    const TapeView tv = tape_view(tape, tl);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    return with_key(tl.kl.key64, [&](auto kt) -> int {
+        using KeyT = decltype(kt);
+        if (!tl.general) {
+            k_lk_sources_aliased<KeyT><<<grid_cap((N + 255) / 256), 256, 0, st>>>(
+                static_cast<const KeyT*>(tv.keys), B * C, T, C, tl.kl.tbits, static_cast<int>(k), src);
+        } else {
+            LkArgs a = lk_args(tv, tl, raddr, addr_dtype, B, T, C, 1, A, k, RAVEL_F32);
+            k_lk_sources_general<KeyT><<<grid_cap((N * k + 255) / 256), 256, 0, st>>>(a, src);
+        }
+        return check_launch();
+    });
+}
+
+int ravel_gather_rows(const float* payload, const int32_t* src, const float* sums, int64_t B, int64_t T, int64_t C,
+                      int64_t D, int64_t k, float* rows, void* stream) {
+    GatherArgs g;
+    if (int e = gather_args(g, payload, src, sums, B, T, C, D, k)) return e;
+    if (g.M == 0) return RAVEL_OK;
+    if (rows == nullptr || addr_bits(rows) % 16) return RAVEL_ERR_INVALID_ARG;
+    const int64_t pieces = g.M * (g.K / 4);
+    k_gather_rows<<<grid_cap((pieces + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(g, rows);
+    return check_launch();
+}
+
+int ravel_gather_gemm(const float* payload, const int32_t* src, const float* sums, int64_t B, int64_t T, int64_t C,
+                      int64_t D, int64_t k, const float* weight, int64_t N, const float* x, const float* gate,
+                      float* out, float* pre, void* stream) {
+    GemmArgs a;
+    std::memset(&a, 0, sizeof(a));
+    if (int e = gather_args(a.g, payload, src, sums, B, T, C, D, k)) return e;
+    if (N <= 0 || N > (int64_t{1} << 24)) return RAVEL_ERR_INVALID_ARG;
+    if (a.g.M == 0) return RAVEL_OK;
+    if (weight == nullptr || out == nullptr || ((x == nullptr) != (gate == nullptr))) return RAVEL_ERR_INVALID_ARG;
+    if (addr_bits(weight) % 16 || (a.g.K * 4) % 16) return RAVEL_ERR_UNSUPPORTED;  // TMA rows: 16-byte strides
+    for (const void* p : {static_cast<const void*>(out), static_cast<const void*>(pre), static_cast<const void*>(x),
+                          static_cast<const void*>(gate)})
+        if (p != nullptr && addr_bits(p) % 16) return RAVEL_ERR_INVALID_ARG;
+    a.N = static_cast<int>(N);
+    a.out = out; a.pre = pre; a.x = x; a.gate = gate;
+    const int64_t mtiles = (a.g.M + GG_BM - 1) / GG_BM;
+    // one wave of CTAs where possible: 256-column tiles once the token tiles fill the SMs
+    const int bn = N <= 64 ? 64 : ((N <= 128 || mtiles < sm_count()) ? 128 : 256);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    auto go = [&](auto bnc) -> int {
+        constexpr int BN = decltype(bnc)::value;
+        CUtensorMap map;
+        if (int e = encode_weight_map(&map, weight, N, a.g.K, BN)) return e;
+        const size_t smem = gather_gemm_smem<BN>();
+        if (int e = set_smem(k_gather_gemm<BN>, smem)) return e;
+        const dim3 grid(static_cast<unsigned>(mtiles), static_cast<unsigned>((N + BN - 1) / BN));
+        k_gather_gemm<BN><<<grid, GG_THREADS, smem, st>>>(map, a);
+        return check_launch();
+    };
+    if (bn == 64) return go(IC<64>{});
+    if (bn == 128) return go(IC<128>{});
+    return go(IC<256>{});
+}
 
 int ravel_tape_build_tokens(const int64_t* tokens, int n_literal, int64_t bos_token_id, const void* learned_write,
                             const void* learned_read, int learned_dtype, const uint8_t* wmask, int64_t B, int64_t T,
