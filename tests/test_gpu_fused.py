@@ -6,7 +6,8 @@ pieces in float64, within the TF32 tolerance of its inputs (the reference's own
 CUDA ``fast_linear`` is a TF32 Triton dot): |error| <= 5e-3 * max|expected|.
 Its backward (cuBLAS float32 GEMMs plus the operator's own backward kernels)
 must match float64 autograd of the unfused composition within 1e-4 of the
-largest gradient.  Cases cover aliased and general reads, a write mask, k of
+largest gradient (the gate's gradient, a product with the forward's TF32
+result, within the forward's tolerance).  Cases cover aliased and general reads, a write mask, k of
 1-3, with and without the sum read, N below, at and above one tile (64, 128,
 256 columns), token counts that are not a multiple of 128, and a K of 24 (one
 partial 32-float chunk).
@@ -74,15 +75,19 @@ def _check(c, tol_fwd=5e-3, tol_bwd=1e-4):
     ref = {n: (c[n].double().requires_grad_(True) if c[n] is not None else None) for n in ("p", "W", "x", "gate")}
     want = _composed(c, ref["p"], ref["W"], ref["x"], ref["gate"])
     want.backward(c["gy"].double())
+    want = want.detach()
     scale = float(want.abs().max())
     err = float((out.double() - want).abs().max())
     assert err <= tol_fwd * scale, f"forward: max error {err:.3g} vs {tol_fwd} * {scale:.3g}"
     for n in ("p", "W", "x", "gate"):
         if ref[n] is None:
             continue
+        # d gate = gy * (A W^T) * s * (1 - s) carries the forward's TF32 error; the
+        # others come from float32 GEMMs of exact rows
+        tol = tol_fwd if n == "gate" else tol_bwd
         g, gw = leaves[n].grad.double(), ref[n].grad
         e, s = float((g - gw).abs().max()), float(gw.abs().max())
-        assert e <= tol_bwd * s, f"grad {n}: max error {e:.3g} vs {tol_bwd} * {s:.3g}"
+        assert e <= tol * s, f"grad {n}: max error {e:.3g} vs {tol} * {s:.3g}"
 
 
 def test_small_aliased_with_sums():
