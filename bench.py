@@ -547,11 +547,12 @@ def main():
     strong = None
     if world > 1 and not args.no_strong and cfg.cfg == 3:
         strong = run_strong(cfg, dev, rank, world)
-    ref_gpu = cfg1 = None
+    ref_gpu = cfg1 = fused_read = None
     if world == 1 and not args.no_reference_gpu:
         if cfg.backward:
             ref_gpu = run_reference_gpu(cfg, x, dev, steps=5, warmup=args.warmup)
         cfg1 = run_cfg1(dev)
+        fused_read = run_fused_read(dev)
     del x, p, gv, gs
     torch.cuda.empty_cache()
     model = None
@@ -581,7 +582,7 @@ def main():
             "roofline": roofline, "kernels": kernels, "e2e": e2e, "e2e_copy_bound": copy_bound,
             "cpu_baseline": cpu, "cpu_port": port, "decode": decode,
             "general_path": general, "reference_gpu": ref_gpu, "config1": cfg1, "strong_scaling": strong,
-            "config5_model": model, "clocks": clk, "gpu_launches": launches,
+            "config5_model": model, "fused_read_linear": fused_read, "clocks": clk, "gpu_launches": launches,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -947,6 +948,84 @@ def run_cfg1(dev, reps: int = 200) -> dict:
     return out
 
 
+def run_fused_read(dev, reps: int = 20) -> dict:
+    """The memory layer's read-out at configuration 5's layer shapes (8 x 1024 tokens, 8 heads,
+    D 32 fp32, k 2 + sum read, fuse 768 -> 256, gate residual; learned read heads): the unfused
+    chain (latest-k forward, sum forward, cat, cuBLAS Linear, gate residual) against
+    memory_read_linear (the gather inside a tcgen05 GEMM), forward only, per call; and the
+    fused GEMM kernel's own time with its algorithmic FLOPs and bytes."""
+    import torch
+    import ravel_lm_b200._lib as L
+    from ravel_lm_b200 import causal_last_k_lookup, causal_sum_lookup
+    from ravel_lm_b200.fused import memory_read_linear
+    from ravel_lm_b200.ravel_memory import clear_tape_cache
+    from ravel_lm_b200.workloads import CONFIGS, make_inputs
+    cfg = CONFIGS[5]
+    x0 = make_inputs(cfg, seed=1005, device=dev, grads=False)
+    w, r, p = x0["write"], x0["read"], x0["payload"]
+    B, T, C, D, k = cfg.B, cfg.T, cfg.C, cfg.D, cfg.k
+    N, K = 256, C * (k + 1) * D
+    g = torch.Generator(device=dev).manual_seed(77)
+    W = torch.randn(N, K, generator=g, device=dev) * K ** -0.5
+    x = torch.randn(B, T, N, generator=g, device=dev)
+    gate = torch.randn(B, T, N, generator=g, device=dev)
+
+    def unfused():
+        clear_tape_cache()
+        vals, _ = causal_last_k_lookup(w, p, r, address_space=cfg.A, k=k)
+        sums, _ = causal_sum_lookup(w, p, r, address_space=cfg.A)
+        rows = torch.cat([vals.reshape(B, T, -1), sums.reshape(B, T, -1)], -1)
+        return x + torch.sigmoid(gate) * torch.nn.functional.linear(rows, W)
+
+    def fused():
+        clear_tape_cache()
+        return memory_read_linear(w, p, r, W, address_space=cfg.A, k=k, use_sum_read=True, x=x, gate_lin=gate)
+
+    def timed(fn):
+        for _ in range(5):
+            fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) * 1000.0 / reps
+
+    with torch.no_grad():
+        out = {"config": "cfg5 layer: B8 T1024 H8 D32 fp32, k=2 + sum read, fuse 768->256, gate residual",
+               "us_unfused": timed(unfused), "us_fused": timed(fused)}
+        diff = (fused() - unfused()).abs().max().item()
+        recs = []
+
+        def hook(name, thunk):
+            if name != "ravel_gather_gemm":
+                return thunk()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            rc = thunk()
+            e1.record()
+            recs.append((e0, e1))
+            return rc
+
+        L.set_call_hook(hook)
+        for _ in range(reps):
+            fused()
+        torch.cuda.synchronize(dev)
+        L.set_call_hook(None)
+    us = sum(a.elapsed_time(b) for a, b in recs) / len(recs) * 1000.0
+    M = B * T
+    flops = 2.0 * M * N * K
+    # payload rows read once + sums + source table + weight + x, gate, out
+    nbytes = (M * C * D * 4) * 2 + M * C * k * 4 + N * K * 4 + 3 * M * N * 4
+    out.update({"us_gemm_kernel": us, "gemm_tflops": flops / (us * 1e-6) / 1e12,
+                "gemm_gbs": nbytes / (us * 1e-6) / 1e9, "gemm_algorithmic_bytes": nbytes, "gemm_flops": flops,
+                "max_abs_diff_vs_unfused": diff,
+                "precision": "fused: TF32 tensor-core inputs, fp32 accumulation; unfused: cuBLAS fp32"})
+    return out
+
+
 def model_config(RavelConfig):
     """Configuration 5's model: a random-init 6-layer RavelLM with both lookups in every layer."""
     return RavelConfig(vocab_size=1024, block_size=1024, d_model=256, n_layers=6, address_space=1024,
@@ -959,7 +1038,9 @@ def run_model(dev, rank: int, world: int, steps: int = 8, warmup: int = 3) -> di
     8 sequences of 1024 tokens per GPU, with this operator dropped in for ravel_lm.ravel_memory
     (the import of model.py:11) and, for comparison, with the stock operator.  One step =
     forward, backward, the deferred weight gradients (deferred.flush_deferred), a gradient
-    all-reduce over NCCL when world > 1 (data parallel), and an AdamW step."""
+    all-reduce over NCCL when world > 1 (data parallel), and an AdamW step.  ``ours_fused``
+    also replaces every memory layer's forward by ravel_lm_b200.layer.memory_layer_forward
+    (token-hashed tape, read-out GEMM and gate residual on the tensor cores)."""
     import torch
     import ravel_lm_b200._lib as L
     import ravel_lm_b200.ravel_memory as mine
@@ -984,10 +1065,19 @@ def run_model(dev, rank: int, world: int, steps: int = 8, warmup: int = 3) -> di
     x, y = toks[:, :-1].contiguous(), toks[:, 1:].contiguous()
     names = ("causal_last_k_lookup", "causal_sum_lookup", "RavelLayerCache")
     stock = {n: getattr(model_mod, n) for n in names}
+    import types
+
+    from ravel_lm_b200.layer import memory_layer_forward
+    layers = [blk.memory for blk in model.blocks if blk.memory is not None]
 
     def use(impl):
         for n in names:
-            setattr(model_mod, n, getattr(mine, n) if impl == "ours" else stock[n])
+            setattr(model_mod, n, stock[n] if impl == "stock" else getattr(mine, n))
+        for layer in layers:
+            if impl == "ours_fused":
+                layer.forward = types.MethodType(memory_layer_forward, layer)
+            elif "forward" in layer.__dict__:
+                del layer.forward
 
     def step():
         mine.clear_tape_cache()
@@ -1013,7 +1103,7 @@ def run_model(dev, rank: int, world: int, steps: int = 8, warmup: int = 3) -> di
                      "A 1024, payload 32 fp32, last_k 2 + sum read; 8 x 1024 tokens per GPU",
            "parallelism": f"data parallel over {world} GPU(s), NCCL all-reduce of gradients" if world > 1
            else "1 GPU", "global_batch": B * world}
-    for impl in ("ours", "stock"):
+    for impl in ("ours", "ours_fused", "stock"):
         use(impl)
         try:
             for _ in range(warmup):
@@ -1021,7 +1111,7 @@ def run_model(dev, rank: int, world: int, steps: int = 8, warmup: int = 3) -> di
             torch.cuda.synchronize(dev)
             barrier(world)
             ops = []
-            if impl == "ours":
+            if impl != "stock":
                 def hook(name, thunk):
                     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                     e0.record()

@@ -193,3 +193,40 @@ def test_generate_greedy_matches_stock(ref):
     with ours(model_mod):
         mine = model.generate(prompt, max_new_tokens=16, temperature=0.0, use_cache=True)
     assert torch.equal(mine, stock)
+
+
+@contextlib.contextmanager
+def fused_layers(model_mod, model):
+    """Every memory layer's forward replaced by ravel_lm_b200.layer.memory_layer_forward."""
+    import types
+
+    from ravel_lm_b200.layer import memory_layer_forward
+    layers = [b.memory for b in model.blocks if b.memory is not None]
+    with ours(model_mod):
+        for layer in layers:
+            layer.forward = types.MethodType(memory_layer_forward, layer)
+        try:
+            yield
+        finally:
+            for layer in layers:
+                del layer.forward
+
+
+@pytest.mark.parametrize("n_layers,literal,learned", [(1, 4, 4), (3, 8, 0)])
+def test_fused_memory_layer_forward(ref, n_layers, literal, learned):
+    """The layer's read-out on the tensor cores (TF32, as the reference's own CUDA fast_linear):
+    logits and gradients within TF32 tolerance of the stock layer.  One layer with learned
+    heads (their addresses come from the embeddings, identical in both runs), or literal heads
+    only (addresses from the tokens), so that no learned argmax sees the TF32 differences."""
+    model_mod, RavelConfig, deferred = ref
+    torch.manual_seed(4)
+    cfg = cfg5(RavelConfig, n_layers=n_layers, n_literal_heads=literal, n_learned_heads=learned)
+    model = model_mod.RavelLM(cfg).cuda()
+    x, y = _tokens(4, 1024, 1024, seed=12)
+    ref_logits, ref_loss, ref_grads = _step(model, deferred, x, y)
+    with fused_layers(model_mod, model):
+        logits, loss, grads = _step(model, deferred, x, y)
+    _close(logits, ref_logits, 1e-2, "logits")
+    _close(loss, ref_loss, 1e-3, "loss")
+    for n, g in ref_grads.items():
+        _close(grads[n], g, 3e-2, f"grad of {n}")
