@@ -59,8 +59,11 @@ extern "C" {
 #define RAVEL_TAPE_WRITE_MASK 2
 
 /* ---- device-side error bits (ravel_device_error) ------------------------ */
-#define RAVEL_DEVERR_SPIN 1       /* a decoupled-lookback wait hit its iteration limit */
-#define RAVEL_DEVERR_BOUNDS 2     /* an index check failed inside a kernel */
+/* A wait on another block (a scan's look-back, the fused GEMM's pipeline
+ * barriers) hit its poll limit and gave up instead of hanging.  Sizes,
+ * pointers, alignment and workspace are checked on the host before any launch,
+ * so kernels carry no other error bit. */
+#define RAVEL_DEVERR_SPIN 1
 
 /* Bytes of the tape written by a forward call and read by its backward call. */
 size_t ravel_tape_bytes(int64_t B, int64_t T, int64_t C, int64_t A, int tape_flags);
@@ -109,8 +112,10 @@ int ravel_latestk_fwd(const void* waddr, const void* raddr, int addr_dtype, cons
  * Gradient of the latest-k values w.r.t. payloads (the autograd of
  * index_select + mask multiply at ravel_lm/ravel_memory.py:173-175):
  * grad_payload[src] = sum of grad_vals over the valid slots that read src.
- * grad_payload [B,T,C,D] is fully overwritten.  Deterministic for aliased
- * reads without a mask; float32 atomics otherwise.
+ * grad_payload [B,T,C,D] is fully overwritten.  Deterministic (a gather, no
+ * atomics) whenever a payload row is 2^m <= 32 vectors of 16 bytes (any D for
+ * aliased reads without a mask); float atomics for other rows of general or
+ * masked tapes.
  */
 int ravel_latestk_bwd(const void* tape, int tape_flags, const void* raddr, int addr_dtype,
                       const void* grad_vals, int dtype, int64_t B, int64_t T, int64_t C, int64_t D,
@@ -313,6 +318,21 @@ size_t ravel_rms_norm_scratch_bytes(int64_t M, int64_t K);
 int ravel_rms_norm_bwd(const void* x, const void* weight, const void* grad_y, const float* rstd, void* grad_x,
                        void* grad_weight, int64_t M, int64_t K, int dtype, void* scratch, size_t scratch_bytes,
                        void* stream);
+
+/*
+ * Poll limit of every wait on another block, on the current device (default
+ * 2^22 polls, about a second of waiting; 1 .. 2^28).  A copy to device memory:
+ * call it between steps, not while a stream is being captured.
+ */
+int ravel_set_wait_limit(uint32_t polls);
+
+/*
+ * Self-test of the bounded wait: one warp waits on *flag (a device word) with
+ * the wait the scans use.  Given a word nothing sets, the wait gives up after
+ * the poll limit, RAVEL_DEVERR_SPIN appears in ravel_device_error, and the
+ * context stays usable.
+ */
+int ravel_wait_selftest(const uint32_t* flag, void* stream);
 
 /* Copy the device error word (RAVEL_DEVERR_* bits) of the current device into
  * *out after the work queued on `stream`; synchronises that stream. */

@@ -26,7 +26,6 @@ RAVEL_TAPE_GENERAL_READS = 1
 RAVEL_TAPE_WRITE_MASK = 2
 RAVEL_NOALLOC_SCRATCH_BYTES = 32 << 20
 RAVEL_DEVERR_SPIN = 1
-RAVEL_DEVERR_BOUNDS = 2
 
 _c_i64 = ctypes.c_int64
 _c_int = ctypes.c_int
@@ -73,6 +72,8 @@ SIGNATURES = {
     "ravel_rms_norm_fwd": (_c_int, [_c_vp, _c_vp, ctypes.c_float, _c_vp, _c_vp, _c_i64, _c_i64, _c_int, _c_vp]),
     "ravel_rms_norm_scratch_bytes": (_c_sz, [_c_i64, _c_i64]),
     "ravel_rms_norm_bwd": (_c_int, [_c_vp] * 6 + [_c_i64, _c_i64, _c_int, _c_vp, _c_sz, _c_vp]),
+    "ravel_set_wait_limit": (_c_int, [ctypes.c_uint32]),
+    "ravel_wait_selftest": (_c_int, [_c_vp, _c_vp]),
     "ravel_device_error": (_c_int, [ctypes.POINTER(_c_int), _c_vp]),
     "ravel_clear_device_error": (_c_int, [_c_vp]),
     "ravel_kernel_launches": (ctypes.c_uint64, []),

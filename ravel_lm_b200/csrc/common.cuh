@@ -16,6 +16,10 @@ __device__ unsigned int g_error_word = 0u;
 
 __device__ __forceinline__ void flag_error(unsigned int bits) { atomicOr(&g_error_word, bits); }
 
+// Polls a wait on another block's flag may take before it gives up (sets
+// RAVEL_DEVERR_SPIN and returns); one per device, set by ravel_set_wait_limit.
+__device__ unsigned int g_wait_limit = 1u << 22;
+
 // ----------------------------------------------------------------- memory-order helpers
 __device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
     unsigned int v;
@@ -25,6 +29,22 @@ __device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
 
 __device__ __forceinline__ void st_release(unsigned int* p, unsigned int v) {
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Wait until *p (published by another block with st_release) is nonzero and
+// return it; after g_wait_limit polls give up, flag RAVEL_DEVERR_SPIN and
+// return 0.  Every look-back wait of the scans goes through here.
+__device__ __forceinline__ unsigned int wait_flag(const unsigned int* p, unsigned int sleep_ns) {
+    const unsigned int limit = *const_cast<volatile unsigned int*>(&g_wait_limit);
+    unsigned int f, spins = 0;
+    while ((f = ld_acquire(p)) == 0u) {
+        if (++spins > limit) {
+            flag_error(RAVEL_DEVERR_SPIN);
+            return 0u;
+        }
+        __nanosleep(sleep_ns);
+    }
+    return f;
 }
 
 // Streaming (evict-first) 16-byte store: the latest-k outputs are written once
@@ -71,6 +91,10 @@ __device__ __forceinline__ unsigned lanemask_lt() {
     asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
     return m;
 }
+
+// One warp waits on a flag with the scans' own bounded wait (ravel_wait_selftest):
+// given a word nothing sets, the wait gives up and RAVEL_DEVERR_SPIN comes back.
+__global__ void k_wait_selftest(const unsigned int* flag) { (void)wait_flag(flag, 32); }
 
 // ----------------------------------------------------------------- address folding
 // ravel_lm/ravel_memory.py:127-128: .to(key_dtype).remainder(A).  With int32 keys

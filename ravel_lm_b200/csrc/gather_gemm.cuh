@@ -96,7 +96,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 // Bounded wait on an mbarrier phase; false when the bound ran out (or abort is set).
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
-    for (uint32_t it = 0; it < (1u << 24); ++it) {
+    const uint32_t limit = 4u * *const_cast<volatile unsigned int*>(&g_wait_limit);
+    for (uint32_t it = 0; it < limit; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 1023u) == 1023u && *abort) return false;
         if (it > 4096u) __nanosleep(64);

@@ -1070,6 +1070,17 @@ using namespace ravel;
 
 extern "C" {
 
+int ravel_set_wait_limit(uint32_t polls) {
+    if (polls < 1 || polls > (1u << 28)) return RAVEL_ERR_INVALID_ARG;
+    return cudaMemcpyToSymbol(g_wait_limit, &polls, sizeof(polls)) == cudaSuccess ? RAVEL_OK : RAVEL_ERR_CUDA;
+}
+
+int ravel_wait_selftest(const uint32_t* flag, void* stream) {
+    if (flag == nullptr) return RAVEL_ERR_INVALID_ARG;
+    k_wait_selftest<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(flag);
+    return check_launch();
+}
+
 int ravel_latestk_sources(const void* tape, int tape_flags, const void* raddr, int addr_dtype, int64_t B, int64_t T,
                           int64_t C, int64_t A, int64_t k, int32_t* src, void* stream) {
     if (int e = check_sizes(B, T, C, 0, A)) return e;

@@ -11,7 +11,7 @@
 //   * a chunk publishes its aggregate (flag 1) or, once known, its inclusive
 //     prefix (flag 2); a chunk containing a segment start publishes its
 //     inclusive value at once, so look-back stops at the nearest segment start;
-//   * every wait is bounded: after SPIN_LIMIT polls the kernel flags
+//   * every wait is bounded: after g_wait_limit polls the kernel flags
 //     RAVEL_DEVERR_SPIN in the device error word and continues with a zero
 //     carry instead of hanging.
 //
@@ -32,7 +32,6 @@
 namespace ravel {
 
 constexpr int SCAN_THREADS = 256;
-constexpr unsigned SPIN_LIMIT = 1u << 22;
 
 template <typename Acc>
 struct ScanArgs {
@@ -206,17 +205,8 @@ __global__ void __launch_bounds__(SCAN_THREADS) k_segscan(ScanArgs<typename Elem
             for (int col = lane; col < D; col += 32) pagg[col] = Acc(0);
             int64_t j = L - 1;
             while (true) {
-                unsigned f;
-                unsigned spins = 0;
-                bool bail = false;
-                while ((f = ld_acquire(a.flags + j)) == 0u) {
-                    if (++spins > SPIN_LIMIT) { bail = true; break; }
-                    __nanosleep(64);
-                }
-                if (bail) {
-                    if (lane == 0) flag_error(RAVEL_DEVERR_SPIN);
-                    break;
-                }
+                const unsigned f = wait_flag(a.flags + j, 64);
+                if (f == 0u) break;  // gave up: RAVEL_DEVERR_SPIN is set
                 const Acc* src = (f == 2u) ? a.incl + j * D : a.agg + j * D;
                 for (int col = lane; col < D; col += 32) pagg[col] += src[col];
                 if (f == 2u) break;
@@ -358,12 +348,8 @@ __device__ __forceinline__ void windowed_lookback(unsigned* flags, const Acc* ag
         const int64_t idx = j - lane;
         unsigned f = 2u;  // slots before the stream start are never reached
         if (idx >= jmin) {
-            unsigned spins = 0;
-            while ((f = ld_acquire(flags + idx)) == 0u) {
-                if (++spins > SPIN_LIMIT) { f = 3u; break; }
-                __nanosleep(32);
-            }
-            if (f == 3u) flag_error(RAVEL_DEVERR_SPIN);
+            f = wait_flag(flags + idx, 32);
+            if (f == 0u) f = 3u;  // gave up: RAVEL_DEVERR_SPIN is set
         }
         const unsigned term = __ballot_sync(0xffffffffu, f >= 2u);
         int stop = term ? __ffs(term) - 1 : 31;
@@ -914,15 +900,8 @@ __global__ void __launch_bounds__(GS_WARPS * 32) k_range_scan(GsArgs a) {
         for (int q = 0; q < MAXC; ++q) cin[q] = Acc(0);
         if (need) {
             for (int64_t j = tk - 1;; --j) {
-                unsigned f = 0, spins = 0;
-                while ((f = ld_acquire(a.bflags + j)) == 0u) {
-                    if (++spins > SPIN_LIMIT) break;
-                    __nanosleep(64);
-                }
-                if (f == 0u) {
-                    if (lane == 0) flag_error(RAVEL_DEVERR_SPIN);
-                    break;
-                }
+                const unsigned f = wait_flag(a.bflags + j, 64);
+                if (f == 0u) break;  // gave up: RAVEL_DEVERR_SPIN is set
                 const Acc* src = bv + (j * 2 + (f == 2u ? 1 : 0)) * D;
 #pragma unroll
                 for (int q = 0; q < MAXC; ++q) {

@@ -132,3 +132,45 @@ def test_global_fold_leaves_equal_rules_alone():
     assert _global_fold(a, sh, 10, 7) is a
     a32 = a.to(torch.int32)
     assert _global_fold(a32, sh, 10, 7) is a32
+
+
+def _failing_worker(rank, world, port, out_q):
+    """Rank 1 fails before the collective; rank 0's gather must end with an error, not hang."""
+    import datetime
+
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    try:
+        from ravel_lm_b200.sharding import gather_outputs
+        sh = shard_streams(2, 4, world, rank)
+        if rank == 1:
+            raise RuntimeError("injected failure on rank 1")
+        try:
+            gather_outputs(torch.zeros(1, 3, 4, 2), sh)
+            out_q.put("no error")
+        except Exception as exc:  # the process group's timeout or the peer's disconnect
+            out_q.put(type(exc).__name__)
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def test_a_rank_that_fails_before_the_all_gather_is_detected():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(g, 2, port, q)) for g in range(2)]
+    for pr in procs:
+        pr.start()
+    for pr in procs:
+        pr.join(timeout=90)
+    for pr in procs:
+        if pr.is_alive():
+            pr.kill()
+    assert procs[1].exitcode != 0
+    got = q.get(timeout=5)
+    assert got != "no error", "rank 0 must see the failure as an error"
