@@ -8,9 +8,11 @@
 //
 //   * CTAs take chunk tickets from an atomic counter, so every chunk a CTA
 //     waits on already belongs to a running CTA (forward progress);
-//   * a chunk publishes its aggregate (flag 1) or, once known, its inclusive
-//     prefix (flag 2); a chunk containing a segment start publishes its
-//     inclusive value at once, so look-back stops at the nearest segment start;
+//   * a chunk containing a segment start publishes its inclusive value (flag 2),
+//     any other chunk only its aggregate (flag 1); look-back adds aggregates back
+//     to the nearest chunk with a segment start (chunk 0 of every stream is one).
+//     Every successor thus adds the same values in the same order, and the sums
+//     are the same bits from run to run;
 //   * every wait is bounded: after g_wait_limit polls the kernel flags
 //     RAVEL_DEVERR_SPIN in the device error word and continues with a zero
 //     carry instead of hanging.
@@ -214,12 +216,9 @@ __global__ void __launch_bounds__(SCAN_THREADS) k_segscan(ScanArgs<typename Elem
             }
         }
         __syncthreads();
-        if (!chunk_has_start) {
-            for (int col = tid; col < D; col += SCAN_THREADS) a.incl[L * D + col] = pagg[col] + carry[col];
-            __threadfence();
-            __syncthreads();
-            if (tid == 0) st_release(a.flags + L, 2u);
-        }
+        // (a chunk without a segment start never publishes an inclusive value: its
+        // successors always add the same aggregates in the same order, so sums are
+        // the same bits from run to run)
         // apply the look-back carry to positions before the first segment start
         for (uint32_t e = tid; e < static_cast<uint32_t>(first_start * D); e += SCAN_THREADS) {
             uint32_t i, d;
@@ -517,15 +516,8 @@ __global__ void __launch_bounds__(SCANW_WARPS * 32) k_segscan_w(ScanArgs<typenam
 #pragma unroll
             for (int q = 0; q < EL; ++q) cin[q] = Acc(0);
             windowed_lookback<Acc, EL>(a.flags, a.agg, a.incl, L - 1, L - ch, D, lane, active, col, cin);
-            if (!chunk_hs) {
-                if (active) {
-#pragma unroll
-                    for (int q = 0; q < EL; ++q) a.incl[L * D + col + q] = cin[q] + cagg[q];
-                }
-                __threadfence();
-                __syncwarp();
-                if (lane == 0) st_release(a.flags + L, 2u);
-            }
+            // no inclusive value for a chunk without a segment start: a fixed set of
+            // aggregates in a fixed order reaches every successor (reproducible sums)
             if (active) {
 #pragma unroll
                 for (int q = 0; q < EL; ++q) carry[col + q] = cin[q];
@@ -911,16 +903,10 @@ __global__ void __launch_bounds__(GS_WARPS * 32) k_range_scan(GsArgs a) {
                 if (f == 2u || j == tk - cb) break;
             }
         }
-        if (!closed) {
-#pragma unroll
-            for (int q = 0; q < MAXC; ++q) {
-                const uint32_t col = lane + 32u * q;
-                if (col < D) bv[(tk * 2 + 1) * D + col] = cin[q] + bv[(tk * 2) * D + col];
-            }
-            __threadfence();
-            __syncwarp();
-            if (lane == 0) st_release(a.bflags + tk, 2u);
-        }
+        // A block without a segment start publishes only its aggregate (never an
+        // inclusive value once its own look-back is done): every successor then adds
+        // the same aggregates in the same order back to the nearest block holding a
+        // segment start, so the sums are the same bits from run to run.
         // carries: c_0 = cin; c_{j+1} = 0 if lo_{j+1} starts a segment, else piece_j (+ c_j when range j holds no start)
 #pragma unroll
         for (int q = 0; q < MAXC; ++q) {

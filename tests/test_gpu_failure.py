@@ -91,3 +91,24 @@ def test_one_poll_scans_are_exact_or_report(lib, D):
     clear_tape_cache()
     again, _ = causal_sum_lookup(w, p, address_space=3)
     assert torch.equal(again, want) and L.device_error(st) == 0
+
+
+@pytest.mark.parametrize("D,dtype", [(64, torch.bfloat16), (24, torch.float32)])
+def test_scans_are_reproducible_bit_for_bit(lib, D, dtype):
+    """Long segments spanning many blocks: the forward and backward sums of repeated calls
+    are the same bits (no timing-dependent association in the look-back)."""
+    from ravel_lm_b200 import causal_sum_lookup
+    from ravel_lm_b200.ravel_memory import clear_tape_cache
+    g = torch.Generator(device="cuda").manual_seed(5)
+    w = torch.randint(0, 2, (2, 30000, 8), generator=g, device="cuda")
+    p0 = torch.randn(2, 30000, 8, D, generator=g, device="cuda").to(dtype)
+    gs = torch.randn(2, 30000, 8, D, generator=g, device="cuda").to(dtype)
+    outs = []
+    for _ in range(6):
+        clear_tape_cache()
+        p = p0.clone().requires_grad_(True)
+        sums, _ = causal_sum_lookup(w, p, address_space=2)
+        sums.backward(gs)
+        outs.append((sums.detach(), p.grad))
+    for s2, g2 in outs[1:]:
+        assert torch.equal(s2, outs[0][0]) and torch.equal(g2, outs[0][1])
