@@ -72,6 +72,8 @@ def parse():
     ap.add_argument("--batch", type=int, default=None, help="override B per GPU (small profiling cases)")
     ap.add_argument("--ops", choices=["all", "lk", "ss"], default="all",
                     help="ops in a step (profiling a single op; the benchmark runs all)")
+    ap.add_argument("--only", choices=["fused_read", "decode", "config1", "model"], default=None,
+                    help="run one side measurement alone and print its JSON (profiling)")
     return ap.parse_args()
 
 
@@ -438,6 +440,18 @@ def main():
     from ravel_lm_b200.workloads import make_inputs
 
     rank, world, local = dist_setup()
+    if args.only is not None:
+        dev = torch.device("cuda", local)
+        fn = {"fused_read": run_fused_read, "decode": run_decode, "config1": run_cfg1,
+              "model": lambda d: run_model(d, rank, world)}[args.only]
+        res = fn(dev)
+        if rank == 0:
+            print(json.dumps({"only": args.only, "result": res}), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            barrier(world)
+            dist.destroy_process_group()
+        return
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     seed = 1000 + cfg.cfg + 7919 * rank
