@@ -11,15 +11,16 @@
 //   k_lk_sources     the source table: src[r, j] = flat payload row of read r's
 //                    j-th latest earlier write, -1 for an invalid slot (whose
 //                    reference value candidate*0 contributes zero to A * W^T).
-//   k_gather_gemm    one CTA per 128 tokens x BN outputs.  Warps 0-3 gather A
+//   k_gather_gemm    one CTA per 128 tokens x BN outputs.  Warps 0-7 gather A
 //                    tiles (128 rows x 32 floats) with cp.async into the 128-byte
-//                    swizzled K-major layout; warp 4 lane 0 loads the W tiles
+//                    swizzled K-major layout; warp 9 lane 0 loads the W tiles
 //                    (BN rows x 32 floats) by TMA (this GPU's own memory, no
-//                    multicast) and issues tcgen05.mma kind::tf32 (M 128, N BN,
-//                    K 8 per instruction) into a TMEM accumulator; a 4-stage
-//                    mbarrier ring connects them.  Warps 0-3 then read the
-//                    accumulator with tcgen05.ld and store it, optionally as
-//                    x + sigmoid(gate) * acc.  Every wait is bounded: on a
+//                    multicast); warp 8 lane 0 issues tcgen05.mma kind::tf32
+//                    (M 128, N BN, K 8 per instruction) into a TMEM accumulator;
+//                    a 4-stage mbarrier ring connects them.  Warps 0-7 then read
+//                    the accumulator with tcgen05.ld (warps w and w+4 share the
+//                    TMEM lanes of rows 32(w%4).., half the columns each) and
+//                    store it, optionally as x + sigmoid(gate) * acc.  Every wait is bounded: on a
 //                    timeout the kernel sets RAVEL_DEVERR_SPIN, drains its own
 //                    copies, frees its TMEM and returns.
 //   k_gather_rows    the same gather written out as A (the backward's GEMMs).
@@ -209,11 +210,14 @@ __global__ void k_gather_rows(GatherArgs g, float* __restrict__ A) {
 }
 
 // ------------------------------------------------------------------ the fused GEMM
-constexpr int GG_BM = 128;        // tokens per CTA (UMMA M)
-constexpr int GG_BK = 32;         // floats per K chunk: one 128-byte swizzle row
+constexpr int GG_BM = 128;         // tokens per CTA (UMMA M)
+constexpr int GG_BK = 32;          // floats per K chunk: one 128-byte swizzle row
 constexpr int GG_STAGES = 4;
-constexpr int GG_PRODUCERS = 128; // warps 0-3 gather A and run the epilogue
-constexpr int GG_THREADS = GG_PRODUCERS + 32;
+constexpr int GG_PWARPS = 8;       // warps 0-7 gather A, then run the epilogue
+constexpr int GG_PRODUCERS = GG_PWARPS * 32;
+constexpr int GG_MMA_WARP = GG_PWARPS;      // lane 0 issues the MMAs
+constexpr int GG_TMA_WARP = GG_PWARPS + 1;  // lane 0 loads the W tiles
+constexpr int GG_THREADS = GG_PRODUCERS + 64;
 
 struct GemmArgs {
     GatherArgs g;
@@ -229,12 +233,53 @@ constexpr size_t gather_gemm_smem() {
     return 1024 /* alignment slack */ + static_cast<size_t>(GG_STAGES) * (GG_BM + BN) * GG_BK * 4 + 256;
 }
 
+// Epilogue of one 32-column slice of the accumulator: TMEM lanes 32*(warp % 4) ..
+// +31 are this warp's rows.
+template <int BN>
+__device__ __forceinline__ void gg_epilogue_slice(const GemmArgs& a, uint32_t tmem, int warp, int lane, int64_t m0,
+                                                  int n0, int c0) {
+    uint32_t r[32];
+    tmem_ld32(tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + static_cast<uint32_t>(c0), r);
+    const int64_t gm = m0 + (warp & 3) * 32 + lane;
+    if (gm >= a.g.M || n0 + c0 >= a.N) return;
+    const bool vec = (a.N & 3) == 0;  // rows start 16-byte aligned: 4-float stores
+#pragma unroll
+    for (int c = 0; c < 32; c += 4) {
+        const int col = n0 + c0 + c;
+        if (col >= a.N) break;
+        const int64_t o = gm * a.N + col;
+        float v[4] = {__uint_as_float(r[c]), __uint_as_float(r[c + 1]), __uint_as_float(r[c + 2]),
+                      __uint_as_float(r[c + 3])};
+        const int nv = (a.N - col) < 4 ? (a.N - col) : 4;
+        if (vec) {
+            if (a.pre) *reinterpret_cast<float4*>(a.pre + o) = make_float4(v[0], v[1], v[2], v[3]);
+            if (a.x) {
+                const float4 xv = *reinterpret_cast<const float4*>(a.x + o);
+                const float4 gv = *reinterpret_cast<const float4*>(a.gate + o);
+                const float xs[4] = {xv.x, xv.y, xv.z, xv.w}, gs[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    v[e] = __fadd_rn(xs[e], __fmul_rn(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gs[e]))), v[e]));
+            }
+            *reinterpret_cast<float4*>(a.out + o) = make_float4(v[0], v[1], v[2], v[3]);
+        } else {
+            for (int e = 0; e < nv; ++e) {
+                if (a.pre) a.pre[o + e] = v[e];
+                float y = v[e];
+                if (a.x) y = __fadd_rn(a.x[o + e], __fmul_rn(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-a.gate[o + e]))), y));
+                a.out[o + e] = y;
+            }
+        }
+    }
+}
+
 template <int BN>
 __global__ void __launch_bounds__(GG_THREADS, 1) k_gather_gemm(const __grid_constant__ CUtensorMap wmap,
                                                               GemmArgs a) {
-    static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "UMMA N for M = 128");
+    static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "UMMA N for M = 128; two column halves of 32k");
     constexpr uint32_t A_BYTES = GG_BM * GG_BK * 4, B_BYTES = BN * GG_BK * 4;
-    constexpr uint32_t TMEM_COLS = BN <= 32 ? 32 : (BN <= 64 ? 64 : (BN <= 128 ? 128 : 256));
+    constexpr uint32_t TMEM_COLS = BN <= 64 ? 64 : (BN <= 128 ? 128 : 256);
+    constexpr int ROWS_PER_THREAD = GG_BM * 8 / GG_PRODUCERS;  // 8 pieces of 16 bytes per row
     extern __shared__ unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;  // swizzled tiles need 1024-byte alignment
@@ -270,22 +315,46 @@ __global__ void __launch_bounds__(GG_THREADS, 1) k_gather_gemm(const __grid_cons
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp < 4) {
-        // ---------------- A producers: 8 pieces of 16 bytes per thread per chunk
+    if (warp < GG_PWARPS) {
+        // ---------------- A producers.  Thread t owns 16-byte piece pc = t % 8 of rows
+        // t / 8 + 32 i: the piece's slot and offset are worked out once per chunk, and
+        // its rows' source rows are independent loads issued back to back.
+        const int pc = tid & 7, r0 = tid >> 3;
+        const int ck = a.g.C * a.g.k;
         for (int kc = 0; kc < nk; ++kc) {
             const int s = kc % GG_STAGES;
             if (kc >= GG_STAGES && !mbar_wait(bar_empty + 8 * s, ((kc / GG_STAGES) - 1) & 1, abort)) {
                 *abort = 1;
                 break;
             }
+            const int kidx = kc * GG_BK + pc * 4;
+            const bool in_k = kidx < a.g.K;
+            const int slot = in_k ? kidx / a.g.D : 0;
+            const int d = kidx - slot * a.g.D;
+            const bool lk = slot < ck;
+            int32_t srow[ROWS_PER_THREAD];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int idx = tid + GG_PRODUCERS * i;  // 1024 pieces: row idx / 8, piece idx % 8
-                const int r = idx >> 3, pc = idx & 7;
-                bool valid;
-                const float* src = gather_piece(a.g, m0 + r, kc * GG_BK + pc * 4, valid);
-                const uint32_t dst = sA + s * A_BYTES + r * 128 + ((pc ^ (r & 7)) << 4);
-                cp_async16_zfill(dst, src, valid);
+            for (int i = 0; i < ROWS_PER_THREAD; ++i) {
+                const int64_t n = m0 + r0 + 32 * i;
+                srow[i] = (in_k && lk && n < a.g.M) ? __ldg(a.g.src + n * ck + slot) : -1;
+            }
+            const uint32_t stage = sA + s * A_BYTES;
+#pragma unroll
+            for (int i = 0; i < ROWS_PER_THREAD; ++i) {
+                const int r = r0 + 32 * i;
+                const int64_t n = m0 + r;
+                const float* src = a.g.payload;
+                bool valid = false;
+                if (in_k && n < a.g.M) {
+                    if (lk) {
+                        valid = srow[i] >= 0;
+                        if (valid) src = a.g.payload + static_cast<int64_t>(srow[i]) * a.g.D + d;
+                    } else {
+                        valid = true;
+                        src = a.g.sums + (n * a.g.C + (slot - ck)) * static_cast<int64_t>(a.g.D) + d;
+                    }
+                }
+                cp_async16_zfill(stage + r * 128 + ((pc ^ (r & 7)) << 4), src, valid);
             }
             cp_async_commit();
             if (kc >= GG_STAGES - 1) {  // the chunk issued STAGES-1 iterations ago has landed
@@ -300,67 +369,21 @@ __global__ void __launch_bounds__(GG_THREADS, 1) k_gather_gemm(const __grid_cons
             for (int kc = nk - (GG_STAGES - 1) < 0 ? 0 : nk - (GG_STAGES - 1); kc < nk; ++kc)
                 mbar_arrive(bar_full + 8 * (kc % GG_STAGES));
         }
-        // ---------------- epilogue: lane r of warp w holds row 32w + r of the tile
+        // ---------------- epilogue: warps w and w + 4 share TMEM lanes 32*(w%4), each
+        // takes half of the columns
         const bool ok = !*abort && mbar_wait(bar_done, 0, abort);
         tc_fence_after();
         if (!ok) {
             *abort = 1;
         } else {
-            const int row = warp * 32 + lane;
-            const int64_t gm = m0 + row;
-            const bool vec = (a.N & 3) == 0;  // rows start 16-byte aligned: 4-float stores
-            for (int c0 = 0; c0 < BN; c0 += 32) {
-                uint32_t r[32];
-                tmem_ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(c0), r);
-                if (gm >= a.g.M || n0 + c0 >= a.N) continue;
-#pragma unroll
-                for (int c = 0; c < 32; c += 4) {
-                    const int col = n0 + c0 + c;
-                    if (col >= a.N) break;
-                    const int64_t o = gm * a.N + col;
-                    float v[4] = {__uint_as_float(r[c]), __uint_as_float(r[c + 1]), __uint_as_float(r[c + 2]),
-                                  __uint_as_float(r[c + 3])};
-                    const int nv = (a.N - col) < 4 ? (a.N - col) : 4;
-                    if (vec) {
-                        if (a.pre) *reinterpret_cast<float4*>(a.pre + o) = make_float4(v[0], v[1], v[2], v[3]);
-                        if (a.x) {
-                            const float4 xv = *reinterpret_cast<const float4*>(a.x + o);
-                            const float4 gv = *reinterpret_cast<const float4*>(a.gate + o);
-                            const float xs[4] = {xv.x, xv.y, xv.z, xv.w}, gs[4] = {gv.x, gv.y, gv.z, gv.w};
-#pragma unroll
-                            for (int e = 0; e < 4; ++e)
-                                v[e] = __fadd_rn(xs[e], __fmul_rn(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gs[e]))), v[e]));
-                        }
-                        *reinterpret_cast<float4*>(a.out + o) = make_float4(v[0], v[1], v[2], v[3]);
-                    } else {
-                        for (int e = 0; e < nv; ++e) {
-                            if (a.pre) a.pre[o + e] = v[e];
-                            float y = v[e];
-                            if (a.x)
-                                y = __fadd_rn(a.x[o + e],
-                                              __fmul_rn(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-a.gate[o + e]))), y));
-                            a.out[o + e] = y;
-                        }
-                    }
-                }
-            }
+            const int half = warp >> 2;
+            for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 32)
+                gg_epilogue_slice<BN>(a, tmem, warp, lane, m0, n0, c0);
         }
-    } else if (lane == 0) {
-        // ---------------- warp 4: W tiles by TMA, then the MMAs of each chunk
+    } else if (warp == GG_MMA_WARP && lane == 0) {
+        // ---------------- the MMAs of each chunk, as soon as its A and W tiles landed
         constexpr uint32_t IDESC = idesc_tf32(GG_BM, BN);
-        int loaded = 0;
-        for (int kc = 0; kc < nk && !*abort; ++kc) {
-            // keep up to STAGES W tiles in flight ahead of the MMAs
-            for (; loaded < nk && loaded < kc + GG_STAGES; ++loaded) {
-                const int s = loaded % GG_STAGES;
-                if (loaded >= GG_STAGES && !mbar_wait(bar_empty + 8 * s, ((loaded / GG_STAGES) - 1) & 1, abort)) {
-                    *abort = 1;
-                    break;
-                }
-                mbar_arrive_expect_tx(bar_full + 8 * s, B_BYTES);
-                tma_load_2d(sB + s * B_BYTES, &wmap, loaded * GG_BK, n0, bar_full + 8 * s);
-            }
-            if (*abort) break;
+        for (int kc = 0; kc < nk; ++kc) {
             const int s = kc % GG_STAGES;
             if (!mbar_wait(bar_full + 8 * s, (kc / GG_STAGES) & 1, abort)) {
                 *abort = 1;
@@ -376,15 +399,25 @@ __global__ void __launch_bounds__(GG_THREADS, 1) k_gather_gemm(const __grid_cons
             umma_commit(bar_empty + 8 * s);  // frees the stage when these MMAs have read it
         }
         umma_commit(bar_done);  // arrives when every MMA issued above has completed
+    } else if (warp == GG_TMA_WARP && lane == 0) {
+        // ---------------- W tiles by TMA (this GPU's memory, no multicast), STAGES ahead
+        for (int kc = 0; kc < nk; ++kc) {
+            const int s = kc % GG_STAGES;
+            if (kc >= GG_STAGES && !mbar_wait(bar_empty + 8 * s, ((kc / GG_STAGES) - 1) & 1, abort)) {
+                *abort = 1;
+                break;
+            }
+            mbar_arrive_expect_tx(bar_full + 8 * s, B_BYTES);
+            tma_load_2d(sB + s * B_BYTES, &wmap, kc * GG_BK, n0, bar_full + 8 * s);
+        }
         if (*abort) {
-            flag_error(RAVEL_DEVERR_SPIN);
             // tile loads still in flight land within microseconds; give them a bounded
             // while before the CTA's shared memory is released
             for (int i = 0; i < 256; ++i) __nanosleep(4000);
         }
     }
     // ---------------- teardown: the MMAs are complete (done barrier) before TMEM is freed
-    if (warp == 4 && lane == 0 && *abort) (void)mbar_wait(bar_done, 0, abort);
+    if (warp == GG_MMA_WARP && lane == 0 && *abort) (void)mbar_wait(bar_done, 0, abort);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
