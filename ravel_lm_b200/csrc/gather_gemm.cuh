@@ -226,12 +226,19 @@ struct GemmArgs {
     float* pre;            // [M, N] the GEMM result before the gate, or null
     const float* x;        // gate residual: out = x + sigmoid(gate) * acc (both [M, N]) or null
     const float* gate;
+    int ck_smem;           // > 0: the source table of a tile is staged in shared memory
 };
 
+// Dynamic shared memory: the stage ring, barriers, and (when it fits, ck_smem > 0)
+// the tile's source-row table [128][ck] int32.
 template <int BN>
-constexpr size_t gather_gemm_smem() {
-    return 1024 /* alignment slack */ + static_cast<size_t>(GG_STAGES) * (GG_BM + BN) * GG_BK * 4 + 256;
+constexpr size_t gather_gemm_smem(int ck_smem) {
+    return 1024 /* alignment slack */ + static_cast<size_t>(GG_STAGES) * (GG_BM + BN) * GG_BK * 4 + 256 +
+           static_cast<size_t>(ck_smem) * GG_BM * 4;
 }
+
+// sigmoid for the TF32 epilogue: 1 / (1 + e^-x) with the fast exponential
+__device__ __forceinline__ float gg_sigmoid(float x) { return __frcp_rn(1.0f + __expf(-x)); }
 
 // Epilogue of one 32-column slice of the accumulator: TMEM lanes 32*(warp % 4) ..
 // +31 are this warp's rows.
@@ -258,15 +265,14 @@ __device__ __forceinline__ void gg_epilogue_slice(const GemmArgs& a, uint32_t tm
                 const float4 gv = *reinterpret_cast<const float4*>(a.gate + o);
                 const float xs[4] = {xv.x, xv.y, xv.z, xv.w}, gs[4] = {gv.x, gv.y, gv.z, gv.w};
 #pragma unroll
-                for (int e = 0; e < 4; ++e)
-                    v[e] = __fadd_rn(xs[e], __fmul_rn(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gs[e]))), v[e]));
+                for (int e = 0; e < 4; ++e) v[e] = xs[e] + gg_sigmoid(gs[e]) * v[e];
             }
             *reinterpret_cast<float4*>(a.out + o) = make_float4(v[0], v[1], v[2], v[3]);
         } else {
             for (int e = 0; e < nv; ++e) {
                 if (a.pre) a.pre[o + e] = v[e];
                 float y = v[e];
-                if (a.x) y = __fadd_rn(a.x[o + e], __fmul_rn(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-a.gate[o + e]))), y));
+                if (a.x) y = a.x[o + e] + gg_sigmoid(a.gate[o + e]) * y;
                 a.out[o + e] = y;
             }
         }
@@ -288,12 +294,19 @@ __global__ void __launch_bounds__(GG_THREADS, 1) k_gather_gemm(const __grid_cons
     unsigned char* gen = smem_raw + (sbar + 8 * (2 * GG_STAGES + 1) - raw);
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(gen);
     volatile int* abort = reinterpret_cast<volatile int*>(gen + 4);
+    int32_t* ssrc = reinterpret_cast<int32_t*>(gen + 16);  // [128][ck] when a.ck_smem
     const uint32_t bar_full = sbar, bar_empty = sbar + 8 * GG_STAGES, bar_done = sbar + 16 * GG_STAGES;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t m0 = static_cast<int64_t>(blockIdx.x) * GG_BM;
     const int n0 = blockIdx.y * BN;
     const int nk = (a.g.K + GG_BK - 1) / GG_BK;
+    const int ck = a.g.C * a.g.k;
+    if (a.ck_smem && warp < GG_PWARPS) {  // the tile's rows of the source table are contiguous
+        const int64_t rows = (a.g.M - m0) < GG_BM ? (a.g.M - m0) : GG_BM;
+        for (int i = tid; i < GG_BM * ck; i += GG_PRODUCERS)
+            ssrc[i] = i < rows * ck ? __ldg(a.g.src + m0 * ck + i) : -1;
+    }
 
     if (tid == 0) {
         for (int s = 0; s < GG_STAGES; ++s) {
@@ -320,7 +333,6 @@ __global__ void __launch_bounds__(GG_THREADS, 1) k_gather_gemm(const __grid_cons
         // t / 8 + 32 i: the piece's slot and offset are worked out once per chunk, and
         // its rows' source rows are independent loads issued back to back.
         const int pc = tid & 7, r0 = tid >> 3;
-        const int ck = a.g.C * a.g.k;
         for (int kc = 0; kc < nk; ++kc) {
             const int s = kc % GG_STAGES;
             if (kc >= GG_STAGES && !mbar_wait(bar_empty + 8 * s, ((kc / GG_STAGES) - 1) & 1, abort)) {
@@ -336,7 +348,9 @@ __global__ void __launch_bounds__(GG_THREADS, 1) k_gather_gemm(const __grid_cons
 #pragma unroll
             for (int i = 0; i < ROWS_PER_THREAD; ++i) {
                 const int64_t n = m0 + r0 + 32 * i;
-                srow[i] = (in_k && lk && n < a.g.M) ? __ldg(a.g.src + n * ck + slot) : -1;
+                srow[i] = (in_k && lk && n < a.g.M)
+                              ? (a.ck_smem ? ssrc[(r0 + 32 * i) * ck + slot] : __ldg(a.g.src + n * ck + slot))
+                              : -1;
             }
             const uint32_t stage = sA + s * A_BYTES;
 #pragma unroll

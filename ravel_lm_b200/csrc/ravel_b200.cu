@@ -1140,7 +1140,9 @@ int ravel_gather_gemm(const float* payload, const int32_t* src, const float* sum
         constexpr int BN = decltype(bnc)::value;
         CUtensorMap map;
         if (int e = encode_weight_map(&map, weight, N, a.g.K, BN)) return e;
-        const size_t smem = gather_gemm_smem<BN>();
+        const int ck = a.g.C * a.g.k;
+        a.ck_smem = gather_gemm_smem<BN>(ck) <= 227 * 1024 ? ck : 0;  // stage the source table if it fits
+        const size_t smem = gather_gemm_smem<BN>(a.ck_smem);
         if (int e = set_smem(k_gather_gemm<BN>, smem)) return e;
         const dim3 grid(static_cast<unsigned>(mtiles), static_cast<unsigned>((N + BN - 1) / BN));
         k_gather_gemm<BN><<<grid, GG_THREADS, smem, st>>>(map, a);

@@ -58,7 +58,8 @@ class _ReadLinearFn(torch.autograd.Function):
         if use_sum:
             sums, _smask, _t = _segsum_fwd_impl(write, p, read, write_mask, address_space, prebuilt)
         out = torch.empty(B, T, N, dtype=torch.float32, device=device)
-        pre = torch.empty_like(out) if x is not None else None
+        # A W^T before the gate is kept only for the gate's gradient
+        pre = torch.empty_like(out) if (x is not None and ctx.needs_input_grad[6]) else None
         xc = x.contiguous() if x is not None else None
         gc = gate.contiguous() if gate is not None else None
         _lib.call("ravel_gather_gemm", p.data_ptr(), src.data_ptr(), None if sums is None else sums.data_ptr(),
