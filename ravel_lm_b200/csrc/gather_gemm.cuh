@@ -212,7 +212,10 @@ __global__ void k_gather_rows(GatherArgs g, float* __restrict__ A) {
 // ------------------------------------------------------------------ the fused GEMM
 constexpr int GG_BM = 128;         // tokens per CTA (UMMA M)
 constexpr int GG_BK = 32;          // floats per K chunk: one 128-byte swizzle row
-constexpr int GG_STAGES = 4;
+// pipeline depth per column tile: as many stages as fit in shared memory
+// (64 columns: 8 x 24 KB, 128: 6 x 32 KB, 256: 4 x 48 KB)
+template <int BN>
+__host__ __device__ constexpr int gg_stages() { return BN <= 64 ? 8 : (BN <= 128 ? 6 : 4); }
 constexpr int GG_PWARPS = 8;       // warps 0-7 gather A, then run the epilogue
 constexpr int GG_PRODUCERS = GG_PWARPS * 32;
 constexpr int GG_MMA_WARP = GG_PWARPS;      // lane 0 issues the MMAs
@@ -233,7 +236,7 @@ struct GemmArgs {
 // the tile's source-row table [128][ck] int32.
 template <int BN>
 constexpr size_t gather_gemm_smem(int ck_smem) {
-    return 1024 /* alignment slack */ + static_cast<size_t>(GG_STAGES) * (GG_BM + BN) * GG_BK * 4 + 256 +
+    return 1024 /* alignment slack */ + static_cast<size_t>(gg_stages<BN>()) * (GG_BM + BN) * GG_BK * 4 + 256 +
            static_cast<size_t>(ck_smem) * GG_BM * 4;
 }
 
@@ -283,6 +286,7 @@ template <int BN>
 __global__ void __launch_bounds__(GG_THREADS, 1) k_gather_gemm(const __grid_constant__ CUtensorMap wmap,
                                                               GemmArgs a) {
     static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "UMMA N for M = 128; two column halves of 32k");
+    constexpr int GG_STAGES = gg_stages<BN>();
     constexpr uint32_t A_BYTES = GG_BM * GG_BK * 4, B_BYTES = BN * GG_BK * 4;
     constexpr uint32_t TMEM_COLS = BN <= 64 ? 64 : (BN <= 128 ? 128 : 256);
     constexpr int ROWS_PER_THREAD = GG_BM * 8 / GG_PRODUCERS;  // 8 pieces of 16 bytes per row

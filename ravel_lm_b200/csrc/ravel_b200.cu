@@ -1134,7 +1134,11 @@ int ravel_gather_gemm(const float* payload, const int32_t* src, const float* sum
     a.out = out; a.pre = pre; a.x = x; a.gate = gate;
     const int64_t mtiles = (a.g.M + GG_BM - 1) / GG_BM;
     // one wave of CTAs where possible: 256-column tiles once the token tiles fill the SMs
+#ifdef RAVEL_GG_FORCE_BN
+    const int bn = RAVEL_GG_FORCE_BN;  // build-time tuning knob (sweeps)
+#else
     const int bn = N <= 64 ? 64 : ((N <= 128 || mtiles < sm_count()) ? 128 : 256);
+#endif
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     auto go = [&](auto bnc) -> int {
         constexpr int BN = decltype(bnc)::value;
