@@ -114,6 +114,17 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
         : "memory");
 }
+// Four rows (y0..y3) of a 2-D tensor map, `x` elements into each, one box width
+// each, into four consecutive 128-byte rows of shared memory (this GPU's memory,
+// one CTA: no multicast).  A row index past the tensor reads zeros.
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* map, int x, int y0, int y1, int y2,
+                                            int y3, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3), "r"(bar)
+        : "memory");
+}
 __device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, bool valid) {
     const int n = valid ? 16 : 0;
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
@@ -282,8 +293,13 @@ __device__ __forceinline__ void gg_epilogue_slice(const GemmArgs& a, uint32_t tm
     }
 }
 
-template <int BN>
+// GATHER4: A tiles come from TMA gather4 loads of the payload and sums rows (D a
+// multiple of 32: a K chunk lies in one slot), issued by the TMA warp; otherwise the
+// producer warps gather 16-byte pieces with cp.async.
+template <int BN, bool GATHER4>
 __global__ void __launch_bounds__(GG_THREADS, 1) k_gather_gemm(const __grid_constant__ CUtensorMap wmap,
+                                                              const __grid_constant__ CUtensorMap pmap,
+                                                              const __grid_constant__ CUtensorMap smap,
                                                               GemmArgs a) {
     static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "UMMA N for M = 128; two column halves of 32k");
     constexpr int GG_STAGES = gg_stages<BN>();
@@ -314,7 +330,7 @@ __global__ void __launch_bounds__(GG_THREADS, 1) k_gather_gemm(const __grid_cons
 
     if (tid == 0) {
         for (int s = 0; s < GG_STAGES; ++s) {
-            mbar_init(bar_full + 8 * s, GG_PRODUCERS + 1);
+            mbar_init(bar_full + 8 * s, GATHER4 ? 1 : GG_PRODUCERS + 1);
             mbar_init(bar_empty + 8 * s, 1);
         }
         mbar_init(bar_done, 1);
@@ -337,7 +353,7 @@ __global__ void __launch_bounds__(GG_THREADS, 1) k_gather_gemm(const __grid_cons
         // t / 8 + 32 i: the piece's slot and offset are worked out once per chunk, and
         // its rows' source rows are independent loads issued back to back.
         const int pc = tid & 7, r0 = tid >> 3;
-        for (int kc = 0; kc < nk; ++kc) {
+        for (int kc = 0; kc < (GATHER4 ? 0 : nk); ++kc) {
             const int s = kc % GG_STAGES;
             if (kc >= GG_STAGES && !mbar_wait(bar_empty + 8 * s, ((kc / GG_STAGES) - 1) & 1, abort)) {
                 *abort = 1;
@@ -381,15 +397,27 @@ __global__ void __launch_bounds__(GG_THREADS, 1) k_gather_gemm(const __grid_cons
                 mbar_arrive(bar_full + 8 * ((kc - (GG_STAGES - 1)) % GG_STAGES));
             }
         }
-        cp_async_wait<0>();
-        fence_proxy_async_smem();
-        if (!*abort) {
-            for (int kc = nk - (GG_STAGES - 1) < 0 ? 0 : nk - (GG_STAGES - 1); kc < nk; ++kc)
-                mbar_arrive(bar_full + 8 * (kc % GG_STAGES));
+        if (!GATHER4) {
+            cp_async_wait<0>();
+            fence_proxy_async_smem();
+            if (!*abort) {
+                for (int kc = nk - (GG_STAGES - 1) < 0 ? 0 : nk - (GG_STAGES - 1); kc < nk; ++kc)
+                    mbar_arrive(bar_full + 8 * (kc % GG_STAGES));
+            }
         }
         // ---------------- epilogue: warps w and w + 4 share TMEM lanes 32*(w%4), each
-        // takes half of the columns
-        const bool ok = !*abort && mbar_wait(bar_done, 0, abort);
+        // takes half of the columns.  The wait for the last MMA sleeps between polls,
+        // leaving the issue slots to the TMA and MMA warps.
+        bool ok = !*abort;
+        if (ok) {
+            ok = false;
+            const uint32_t limit = 4u * *const_cast<volatile unsigned int*>(&g_wait_limit);
+            for (uint32_t it = 0; it < limit; ++it) {
+                if (mbar_try_wait(bar_done, 0)) { ok = true; break; }
+                if ((it & 255u) == 255u && *abort) break;
+                __nanosleep(256);
+            }
+        }
         tc_fence_after();
         if (!ok) {
             *abort = 1;
@@ -417,16 +445,50 @@ __global__ void __launch_bounds__(GG_THREADS, 1) k_gather_gemm(const __grid_cons
             umma_commit(bar_empty + 8 * s);  // frees the stage when these MMAs have read it
         }
         umma_commit(bar_done);  // arrives when every MMA issued above has completed
-    } else if (warp == GG_TMA_WARP && lane == 0) {
-        // ---------------- W tiles by TMA (this GPU's memory, no multicast), STAGES ahead
+    } else if (warp == GG_TMA_WARP && (GATHER4 || lane == 0)) {
+        // ---------------- W tiles by TMA (this GPU's memory, no multicast), STAGES ahead;
+        // with GATHER4 the warp's lanes also fetch the A tile, 4 rows per gather4
+        const int64_t rows_p = a.g.M * a.g.C;  // payload / sums rows: past them reads zeros
         for (int kc = 0; kc < nk; ++kc) {
             const int s = kc % GG_STAGES;
-            if (kc >= GG_STAGES && !mbar_wait(bar_empty + 8 * s, ((kc / GG_STAGES) - 1) & 1, abort)) {
-                *abort = 1;
+            bool go = true;
+            if (lane == 0) {
+                if (kc >= GG_STAGES && !mbar_wait(bar_empty + 8 * s, ((kc / GG_STAGES) - 1) & 1, abort)) {
+                    *abort = 1;
+                    go = false;
+                } else {
+                    mbar_arrive_expect_tx(bar_full + 8 * s, B_BYTES + (GATHER4 ? A_BYTES : 0u));
+                    tma_load_2d(sB + s * B_BYTES, &wmap, kc * GG_BK, n0, bar_full + 8 * s);
+                }
+            }
+            if (GATHER4) {
+                go = __shfl_sync(0xffffffffu, go, 0);
+                if (!go) break;
+                // chunk kc: slot and column offset (a chunk lies in one slot: D % 32 == 0)
+                const int kidx = kc * GG_BK;
+                const int slot = kidx / a.g.D, d = kidx - slot * a.g.D;
+                const bool lk = slot < ck;
+                int y[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int r = lane * 4 + i;
+                    const int64_t n = m0 + r;
+                    int64_t row = rows_p;  // out of range: zero fill
+                    if (n < a.g.M) {
+                        if (lk) {
+                            const int32_t v = a.ck_smem ? ssrc[r * ck + slot] : __ldg(a.g.src + n * ck + slot);
+                            if (v >= 0) row = v;
+                        } else {
+                            row = n * a.g.C + (slot - ck);
+                        }
+                    }
+                    y[i] = static_cast<int>(row);
+                }
+                tma_gather4(sA + s * A_BYTES + lane * 512, lk ? &pmap : &smap, d, y[0], y[1], y[2], y[3],
+                            bar_full + 8 * s);
+            } else if (!go) {
                 break;
             }
-            mbar_arrive_expect_tx(bar_full + 8 * s, B_BYTES);
-            tma_load_2d(sB + s * B_BYTES, &wmap, kc * GG_BK, n0, bar_full + 8 * s);
         }
         if (*abort) {
             // tile loads still in flight land within microseconds; give them a bounded

@@ -1051,6 +1051,27 @@ int encode_weight_map(CUtensorMap* map, const float* W, int64_t N, int64_t K, in
     return r == CUDA_SUCCESS ? RAVEL_OK : RAVEL_ERR_CUDA;
 }
 
+// Rows of `rows` x D floats (payload or sums) for TMA gather4: boxes of one row x 32 floats.
+int encode_rows_map(CUtensorMap* map, const float* base, int64_t rows, int64_t D) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    if (encode == nullptr) {
+        cudaDriverEntryPointQueryResult q;
+        void* fn = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || fn == nullptr)
+            return RAVEL_ERR_CUDA;
+        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(D) * 4};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(ravel::GG_BK), 1};
+    cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box,
+                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? RAVEL_OK : RAVEL_ERR_CUDA;
+}
+
 int gather_args(ravel::GatherArgs& g, const float* payload, const int32_t* src, const float* sums, int64_t B, int64_t T,
                 int64_t C, int64_t D, int64_t k) {
     if (B < 0 || T < 0 || C <= 0 || D <= 0 || k <= 0) return RAVEL_ERR_INVALID_ARG;
@@ -1140,16 +1161,29 @@ int ravel_gather_gemm(const float* payload, const int32_t* src, const float* sum
     const int bn = N <= 64 ? 64 : ((N <= 128 || mtiles < sm_count()) ? 128 : 256);
 #endif
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // A tiles by TMA gather4 when a K chunk of 32 floats lies inside one slot
+    const bool gather4 = a.g.D % GG_BK == 0;
     auto go = [&](auto bnc) -> int {
         constexpr int BN = decltype(bnc)::value;
-        CUtensorMap map;
+        CUtensorMap map, pmap, smap;
         if (int e = encode_weight_map(&map, weight, N, a.g.K, BN)) return e;
+        std::memset(&pmap, 0, sizeof(pmap));
+        std::memset(&smap, 0, sizeof(smap));
+        if (gather4) {
+            if (int e = encode_rows_map(&pmap, payload, a.g.M * C, D)) return e;
+            if (int e = encode_rows_map(&smap, sums ? sums : payload, a.g.M * C, D)) return e;
+        }
         const int ck = a.g.C * a.g.k;
         a.ck_smem = gather_gemm_smem<BN>(ck) <= 227 * 1024 ? ck : 0;  // stage the source table if it fits
         const size_t smem = gather_gemm_smem<BN>(a.ck_smem);
-        if (int e = set_smem(k_gather_gemm<BN>, smem)) return e;
         const dim3 grid(static_cast<unsigned>(mtiles), static_cast<unsigned>((N + BN - 1) / BN));
-        k_gather_gemm<BN><<<grid, GG_THREADS, smem, st>>>(map, a);
+        if (gather4) {
+            if (int e = set_smem(k_gather_gemm<BN, true>, smem)) return e;
+            k_gather_gemm<BN, true><<<grid, GG_THREADS, smem, st>>>(map, pmap, smap, a);
+        } else {
+            if (int e = set_smem(k_gather_gemm<BN, false>, smem)) return e;
+            k_gather_gemm<BN, false><<<grid, GG_THREADS, smem, st>>>(map, pmap, smap, a);
+        }
         return check_launch();
     };
     if (bn == 64) return go(IC<64>{});
