@@ -1161,8 +1161,15 @@ int ravel_gather_gemm(const float* payload, const int32_t* src, const float* sum
     const int bn = N <= 64 ? 64 : ((N <= 128 || mtiles < sm_count()) ? 128 : 256);
 #endif
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
-    // A tiles by TMA gather4 when a K chunk of 32 floats lies inside one slot
+    // A tiles by TMA gather4 (a K chunk of 32 floats inside one slot) or by the cp.async
+    // producers.  Measured at config-5 layer shapes: gather4 68 us, cp.async 42-46 us --
+    // 768 four-row gathers per CTA keep the TMA unit busy ~170 cycles each -- so
+    // cp.async is the default and gather4 a build-time option.
+#ifdef RAVEL_GG_GATHER4
     const bool gather4 = a.g.D % GG_BK == 0;
+#else
+    const bool gather4 = false;
+#endif
     auto go = [&](auto bnc) -> int {
         constexpr int BN = decltype(bnc)::value;
         CUtensorMap map, pmap, smap;
