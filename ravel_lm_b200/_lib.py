@@ -128,14 +128,20 @@ def check(name: str, status: int) -> None:
     raise RavelError(name, status)
 
 
+_fns: dict = {}
+
+
 def call(name: str, *args) -> None:
     """Call a status-returning entry point, raising on failure."""
-    fn = getattr(load(), name)
+    fn = _fns.get(name)
+    if fn is None:
+        fn = _fns[name] = getattr(load(), name)
     if _call_hook is not None:
         status = _call_hook(name, lambda: fn(*args))
     else:
         status = fn(*args)
-    check(name, status)
+    if status:
+        check(name, status)
 
 
 def set_call_hook(hook: Optional[Callable]) -> None:

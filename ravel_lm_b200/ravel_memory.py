@@ -74,7 +74,9 @@ def _payload_code(t: Tensor) -> int:
 
 
 def _stream(device: torch.device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    """The raw handle of the current CUDA stream of ``device`` (no Stream object is built)."""
+    return torch._C._cuda_getCurrentRawStream(device.index if device.index is not None else
+                                              torch.cuda.current_device())
 
 
 def _require_cuda(*tensors: Optional[Tensor]) -> torch.device:
