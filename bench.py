@@ -284,6 +284,8 @@ def kernel_bytes(cfg) -> dict:
         "ravel_tape_build": N * addr,
         "ravel_latestk_fwd_tape": N * (D * e + k * D * e + k),
         "ravel_latestk_bwd": N * (k * D * e + D * e),
+        # the latest-k gradient added to the sum's: reads that gradient too
+        "ravel_latestk_bwd_accumulate": N * (k * D * e + 2 * D * e),
         "ravel_segsum_fwd_tape": N * (2 * D * e + 1),
         "ravel_segsum_bwd": N * (2 * D * e),
     }
