@@ -8,7 +8,10 @@
 #include <atomic>
 #include <cstring>
 #include <initializer_list>
+#include <map>
 #include <mutex>
+#include <tuple>
+#include <utility>
 #include <type_traits>
 
 #include "common.cuh"
@@ -265,13 +268,46 @@ int check_launch() {
     return e == cudaSuccess ? RAVEL_OK : RAVEL_ERR_CUDA;
 }
 
+// Per-(kernel, device) results of CUDA attribute calls, so that a launch pays for
+// them once per process instead of on every call.
+std::mutex g_attr_mu;
+std::map<std::pair<const void*, int>, size_t> g_smem_set;            // dynamic smem limit raised to
+std::map<std::tuple<const void*, int, int, size_t>, int> g_occupancy;  // blocks per SM
+
+int current_device() {
+    int dev = 0;
+    return cudaGetDevice(&dev) == cudaSuccess ? dev : 0;
+}
+
 template <typename K>
 int set_smem(K kernel, size_t bytes) {
     if (bytes <= 48 * 1024) return RAVEL_OK;
     if (bytes > 227 * 1024) return RAVEL_ERR_UNSUPPORTED;
+    const auto key = std::make_pair(reinterpret_cast<const void*>(kernel), current_device());
+    std::lock_guard<std::mutex> lock(g_attr_mu);
+    auto it = g_smem_set.find(key);
+    if (it != g_smem_set.end() && it->second >= bytes) return RAVEL_OK;
     const cudaError_t e =
         cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
-    return e == cudaSuccess ? RAVEL_OK : RAVEL_ERR_CUDA;
+    if (e != cudaSuccess) return RAVEL_ERR_CUDA;
+    g_smem_set[key] = bytes;
+    return RAVEL_OK;
+}
+
+// cudaOccupancyMaxActiveBlocksPerMultiprocessor, remembered per (kernel, device, block, smem).
+template <typename K>
+int occupancy(K kernel, int threads, size_t smem) {
+    const auto key = std::make_tuple(reinterpret_cast<const void*>(kernel), current_device(), threads, smem);
+    {
+        std::lock_guard<std::mutex> lock(g_attr_mu);
+        auto it = g_occupancy.find(key);
+        if (it != g_occupancy.end()) return it->second;
+    }
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, threads, smem) != cudaSuccess || occ < 1) occ = 1;
+    std::lock_guard<std::mutex> lock(g_attr_mu);
+    g_occupancy[key] = occ;
+    return occ;
 }
 
 uintptr_t addr_bits(const void* p) { return reinterpret_cast<uintptr_t>(p); }
@@ -673,12 +709,7 @@ int launch_segscan(const TapeView& tv, const TapeLayout& tl, int64_t B, int64_t 
             const int64_t bmw_max = gpb * kRlMax / 32 + 2;
             const size_t smem_max = range_scan_smem(VPL, gpb, D, sizeof(Acc), bmw_max);
             if (int e = set_smem(kern, smem_max)) return e;
-            int occ = 0;
-            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, GS_WARPS * 32,
-                                                              range_scan_smem(VPL, gpb, D, sizeof(Acc), 2)) !=
-                    cudaSuccess ||
-                occ < 1)
-                occ = 1;
+            const int occ = occupancy(kern, GS_WARPS * 32, range_scan_smem(VPL, gpb, D, sizeof(Acc), 2));
             // one range per lane group; whole blocks per stream, RAVEL_RS_WAVES waves of blocks
             // Short streams (64-position ranges do not fill one wave): about two
             // blocks per SM, ranges down to RAVEL_RS_RLMIN positions.

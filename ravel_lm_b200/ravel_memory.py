@@ -155,6 +155,7 @@ class _TapeCache:
         self.refs = None
         self.value = None
         self.partner = None  # (payload ref, payload version, latest-k node ref) of the tape's latest-k call
+        self.touched = None  # the key of the entry the last get hit or put made
 
     @staticmethod
     def _key(write, read, mask, A, stream):
@@ -170,6 +171,7 @@ class _TapeCache:
         w, r, m = (ref() if ref is not None else None for ref in self.refs)
         if w is not write or r is not read or m is not mask:
             return None
+        self.touched = self.key
         return self.value
 
     def put(self, write, read, mask, A, stream, value):
@@ -177,10 +179,11 @@ class _TapeCache:
         self.refs = tuple(None if t is None else weakref.ref(t) for t in (write, read, mask))
         self.value = value
         self.partner = None
+        self.touched = self.key
 
-    def note_latest_k(self, write, read, mask, A, stream, payload, node):
-        """Remember the latest-k call that used the cached tape (see ``_SegSumFn.backward``)."""
-        if node is not None and self.get(write, read, mask, A, stream) is not None:
+    def note_latest_k(self, payload, node):
+        """Remember the latest-k call that just used the cached tape (see ``_SegSumFn.backward``)."""
+        if node is not None and self.key is not None and self.touched is self.key:
             self.partner = (weakref.ref(payload), payload._version, weakref.ref(node))
 
     def latest_k_partner(self, write, read, mask, A, stream, payload):
@@ -193,7 +196,7 @@ class _TapeCache:
         return node
 
     def clear(self):
-        self.key = self.refs = self.value = self.partner = None
+        self.key = self.refs = self.value = self.partner = self.touched = None
 
 
 _tape_cache = _TapeCache()
@@ -543,10 +546,10 @@ def causal_last_k_lookup(
     if torch.compiler.is_compiling():
         vals, mask, _tape = _latestk_fwd(write_addresses, payloads, read, write_mask, int(address_space), int(k))
         return vals, mask
+    _tape_cache.touched = None
     vals, mask = _LatestKFn.apply(write_addresses, payloads, read, write_mask, int(address_space), int(k))
     if vals.grad_fn is not None:
-        _tape_cache.note_latest_k(write_addresses, read, write_mask, int(address_space), _stream(payloads.device),
-                                  payloads, vals.grad_fn)
+        _tape_cache.note_latest_k(payloads, vals.grad_fn)
     return vals, mask
 
 
@@ -678,23 +681,43 @@ class RavelLayerCache:
                   _stream(device))
 
     def step(self, read_addresses: Tensor, write_addresses: Tensor, payloads: Tensor) -> Tuple[Tensor, Tensor]:
-        """``read(read_addresses)`` then ``write(write_addresses, payloads)`` in one launch."""
+        """``read(read_addresses)`` then ``write(write_addresses, payloads)`` in one launch.
+
+        Decode calls this once per memory layer and token, so the common case --
+        contiguous CUDA tensors on one device, int64 (or int32) addresses of one
+        type, payloads in the cache's dtype -- takes a short path; anything else
+        goes through the same checks as ``read`` and ``write``.
+        """
+        values, filled = self.values, self.filled
         B, C = read_addresses.shape
         D = payloads.shape[-1]
-        if write_addresses.shape != (B, C) or self.values.shape[:2] != (B, C) or self.values.shape[-1] != D:
+        if write_addresses.shape != (B, C) or values.shape[:2] != (B, C) or values.shape[-1] != D:
             raise ValueError("cache and payload shapes do not match")
-        device = _require_cuda(self.values, self.filled, read_addresses, write_addresses, payloads)
-        self._check_storage()
-        ra, rcode = _addr(read_addresses)
-        wa, wcode = _addr(write_addresses)
-        if rcode != wcode:
-            ra, wa, rcode = ra.to(torch.int64), wa.to(torch.int64), _lib.RAVEL_I64
-        p = payloads.to(self.values.dtype).contiguous()
-        vals = self.values.new_empty(B, C, D)
+        device = values.device
+        adt = read_addresses.dtype
+        fast = (device.type == "cuda" and filled.device == device and read_addresses.device == device
+                and write_addresses.device == device and payloads.device == device
+                and adt in (torch.int64, torch.int32) and write_addresses.dtype == adt
+                and payloads.dtype == values.dtype and filled.dtype == torch.bool and values.is_contiguous()
+                and filled.is_contiguous() and read_addresses.is_contiguous() and write_addresses.is_contiguous()
+                and payloads.is_contiguous())
+        if fast:
+            ra, wa, rcode, p = read_addresses, write_addresses, (
+                _lib.RAVEL_I64 if adt == torch.int64 else _lib.RAVEL_I32), payloads
+            code = _payload_code(values)
+        else:
+            device = _require_cuda(values, filled, read_addresses, write_addresses, payloads)
+            self._check_storage()
+            ra, rcode = _addr(read_addresses)
+            wa, wcode = _addr(write_addresses)
+            if rcode != wcode:
+                ra, wa, rcode = ra.to(torch.int64), wa.to(torch.int64), _lib.RAVEL_I64
+            p = payloads.to(values.dtype).contiguous()
+            code = _payload_code(values)
+        vals = values.new_empty(B, C, D)
         mask = torch.empty(B, C, dtype=torch.bool, device=device)
-        _lib.call("ravel_cache_step", self.values.data_ptr(), self.filled.data_ptr(), ra.data_ptr(), wa.data_ptr(),
-                  rcode, p.data_ptr(), _payload_code(self.values), B, C, self.values.shape[2], D, vals.data_ptr(),
-                  mask.data_ptr(), _stream(device))
+        _lib.call("ravel_cache_step", values.data_ptr(), filled.data_ptr(), ra.data_ptr(), wa.data_ptr(), rcode,
+                  p.data_ptr(), code, B, C, values.shape[2], D, vals.data_ptr(), mask.data_ptr(), _stream(device))
         return vals, mask
 
 
