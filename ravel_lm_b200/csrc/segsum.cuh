@@ -720,7 +720,10 @@ inline size_t range_scan_smem(int vpl, int64_t gpb, int64_t D, size_t acc_bytes,
 }
 
 template <typename KeyT, int DT, bool IN_SORTED, bool OUT_SORTED, bool INCL, int VPL>
-__global__ void __launch_bounds__(GS_WARPS * 32) k_range_scan(GsArgs a) {
+#ifndef RAVEL_GS_MINB
+#define RAVEL_GS_MINB 1  // minimum resident blocks per SM the register allocation must allow
+#endif
+__global__ void __launch_bounds__(GS_WARPS * 32, RAVEL_GS_MINB) k_range_scan(GsArgs a) {
     using E = Elem<DT>;
     using Acc = typename E::Acc;
     using V = typename E::T;
