@@ -371,14 +371,17 @@ def run_decode(dev) -> dict:
 
     # eager: one read + one write launch per step through the API (what model.py:421,424 calls)
     eager_us = timed(lambda i: (cache.read(ra[i]), cache.write(ra[i], pay[i])), steps)
-    # eager: the one-launch step
+    # eager: the one-launch step, with new output tensors and into reused ones
     step_us = timed(lambda i: cache.step(ra[i], ra[i], pay[i]), steps)
+    obuf = (torch.empty(S, H, D, dtype=dt, device=dev), torch.empty(S, H, dtype=torch.bool, device=dev))
+    step_out_us = timed(lambda i: cache.step(ra[i], ra[i], pay[i], out=obuf), steps)
     graph_us = graphed(ra, ra)
     graph_ind_us = graphed(ra, wa)
     step_bytes = S * H * (2 * 8 + 4 * D * 2 + 3)
     out = {"config": "cfg4: 256 streams x 16 heads, A=4096 uniform, D=64 bf16, cache prefilled by 4096 writes",
            "us_per_step_graph": graph_us, "us_per_step_graph_independent_rw": graph_ind_us,
            "us_per_step_eager": eager_us, "us_per_step_eager_one_launch": step_us,
+           "us_per_step_eager_one_launch_reused_out": step_out_us,
            "prefill_us_token_by_token": prefill_tok_us, "prefill_us_bulk": prefill_bulk_us,
            "bytes_per_step": step_bytes, "gbs_graph": step_bytes / (graph_us * 1e-6) / 1e9,
            "target_us": 10.0}
@@ -553,6 +556,7 @@ def main():
     tokens = cfg.tokens * world
     value = tokens / (ms * 1e-3)
 
+    step_graph = run_graph_step(step, dev, world)
     e2e = copy_bound = None
     if not args.no_e2e and cfg.backward:
         e2e = run_e2e(cfg, x, dev, args.e2e_steps, world)
@@ -593,6 +597,7 @@ def main():
             "vs_baseline": None, "dtype": DTYPE_NAMES[str(cfg.dtype)],
             "data": "synthetic", "config": workload_config(cfg, world),
             "tokens_per_sec_per_gpu": value / world,
+            "step_graph": step_graph,
             "step_roofline": {"algorithmic_bytes": step_bytes, "achieved_gbs": step_bytes / (ms * 1e-3) / 1e9,
                               "frac": step_bytes / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], "peak": peaks["hbm_gbs"]},
             "roofline": roofline, "kernels": kernels, "e2e": e2e, "e2e_copy_bound": copy_bound,
@@ -795,6 +800,33 @@ def run_e2e(cfg, x, dev, steps, world):
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps,
             "path": "pinned host -> ravel_lm_b200.causal_last_k_lookup/causal_sum_lookup (+autograd) -> pinned host",
             "overlap": "copies in and out on their own streams; step i+1 host->device overlaps step i device->host"}
+
+
+def run_graph_step(step, dev, world, reps: int = 10) -> dict:
+    """The same step captured once in a CUDA graph and replayed (no host launch work): the
+    kernel-bound step time, which host-bound small configurations hide in eager mode."""
+    import torch
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        step()
+        with torch.cuda.graph(graph, stream=side):
+            step()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = max_over_ranks(e0.elapsed_time(e1) / reps, world)
+    del graph
+    return {"ms_per_step": ms, "replays": reps}
 
 
 def run_copy_bound(e2e: dict, dev, steps: int, world: int) -> dict:

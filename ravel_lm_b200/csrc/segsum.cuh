@@ -720,10 +720,16 @@ inline size_t range_scan_smem(int vpl, int64_t gpb, int64_t D, size_t acc_bytes,
 }
 
 template <typename KeyT, int DT, bool IN_SORTED, bool OUT_SORTED, bool INCL, int VPL>
-#ifndef RAVEL_GS_MINB
-#define RAVEL_GS_MINB 1  // minimum resident blocks per SM the register allocation must allow
+// Build-time knob: RAVEL_GS_MINB = resident blocks per SM the register allocation
+// must allow.  Measured at config 3 (sum forward / backward, us): none 168 / 160,
+// 6 blocks (80 registers) 166 / 158, 8 blocks (64 registers) 168 / 161, 1 block
+// 194 / 185; a 2-block ring 179 / 170, 8 warps per block 206 / 196.
+#ifdef RAVEL_GS_MINB
+#define RAVEL_GS_BOUNDS __launch_bounds__(GS_WARPS * 32, RAVEL_GS_MINB)
+#else
+#define RAVEL_GS_BOUNDS __launch_bounds__(GS_WARPS * 32)
 #endif
-__global__ void __launch_bounds__(GS_WARPS * 32, RAVEL_GS_MINB) k_range_scan(GsArgs a) {
+__global__ void RAVEL_GS_BOUNDS k_range_scan(GsArgs a) {
     using E = Elem<DT>;
     using Acc = typename E::Acc;
     using V = typename E::T;

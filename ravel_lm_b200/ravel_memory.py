@@ -680,13 +680,16 @@ class RavelLayerCache:
                   p.data_ptr(), _payload_code(self.values), B, T, C, A, D, scratch.data_ptr(), scratch.numel(),
                   _stream(device))
 
-    def step(self, read_addresses: Tensor, write_addresses: Tensor, payloads: Tensor) -> Tuple[Tensor, Tensor]:
+    def step(self, read_addresses: Tensor, write_addresses: Tensor, payloads: Tensor,
+             out: Optional[Tuple[Tensor, Tensor]] = None) -> Tuple[Tensor, Tensor]:
         """``read(read_addresses)`` then ``write(write_addresses, payloads)`` in one launch.
 
         Decode calls this once per memory layer and token, so the common case --
         contiguous CUDA tensors on one device, int64 (or int32) addresses of one
         type, payloads in the cache's dtype -- takes a short path; anything else
-        goes through the same checks as ``read`` and ``write``.
+        goes through the same checks as ``read`` and ``write``.  ``out``: a
+        (values [B, C, D], mask [B, C] bool) pair of contiguous tensors to write
+        the read into instead of new ones (a decode loop that reuses its buffers).
         """
         values, filled = self.values, self.filled
         B, C = read_addresses.shape
@@ -714,8 +717,15 @@ class RavelLayerCache:
                 ra, wa, rcode = ra.to(torch.int64), wa.to(torch.int64), _lib.RAVEL_I64
             p = payloads.to(values.dtype).contiguous()
             code = _payload_code(values)
-        vals = values.new_empty(B, C, D)
-        mask = torch.empty(B, C, dtype=torch.bool, device=device)
+        if out is None:
+            vals = values.new_empty(B, C, D)
+            mask = torch.empty(B, C, dtype=torch.bool, device=device)
+        else:
+            vals, mask = out
+            if (vals.shape != (B, C, D) or vals.dtype != values.dtype or mask.shape != (B, C)
+                    or mask.dtype != torch.bool or vals.device != device or mask.device != device
+                    or not (vals.is_contiguous() and mask.is_contiguous())):
+                raise ValueError("out must be contiguous (values [B, C, D] of the cache dtype, mask [B, C] bool)")
         _lib.call("ravel_cache_step", values.data_ptr(), filled.data_ptr(), ra.data_ptr(), wa.data_ptr(), rcode,
                   p.data_ptr(), code, B, C, values.shape[2], D, vals.data_ptr(), mask.data_ptr(), _stream(device))
         return vals, mask

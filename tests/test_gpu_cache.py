@@ -172,3 +172,24 @@ def test_bulk_prefill_then_decode_matches_latest1():
         v, m = cache.step(addr[:, t], addr[:, t], pay[:, t])
         assert torch.equal(m, mask[:, t, :, 0])
         assert torch.equal(v, vals[:, t, :, 0])
+
+
+def test_step_into_reused_outputs():
+    """``step(..., out=...)`` writes the read into the given buffers, equal to a fresh step."""
+    import torch
+    from ravel_lm_b200 import RavelLayerCache
+    g = torch.Generator(device="cuda").manual_seed(12)
+    B, C, A, D = 3, 4, 50, 8
+    c1 = RavelLayerCache.empty(B, C, A, D, device="cuda", dtype=torch.float32)
+    c2 = RavelLayerCache.empty(B, C, A, D, device="cuda", dtype=torch.float32)
+    buf = (torch.empty(B, C, D, device="cuda"), torch.empty(B, C, dtype=torch.bool, device="cuda"))
+    for _ in range(20):
+        ra = torch.randint(0, A, (B, C), generator=g, device="cuda")
+        wa = torch.randint(0, A, (B, C), generator=g, device="cuda")
+        p = torch.randn(B, C, D, generator=g, device="cuda")
+        v1, m1 = c1.step(ra, wa, p)
+        v2, m2 = c2.step(ra, wa, p, out=buf)
+        assert v2 is buf[0] and m2 is buf[1]
+        assert torch.equal(v1, v2) and torch.equal(m1, m2)
+    with pytest.raises(ValueError):
+        c2.step(ra, wa, p, out=(buf[0][:, :2], buf[1]))
