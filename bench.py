@@ -557,10 +557,11 @@ def main():
     value = tokens / (ms * 1e-3)
 
     step_graph = run_graph_step(step, dev, world)
-    e2e = copy_bound = None
+    e2e = copy_bound = e2e_train = None
     if not args.no_e2e and cfg.backward:
         e2e = run_e2e(cfg, x, dev, args.e2e_steps, world)
         copy_bound = run_copy_bound(e2e, dev, args.e2e_steps, world)
+        e2e_train = run_e2e_training(cfg, x, dev, args.e2e_steps, world)
     general = None
     if not args.no_general and cfg.addressing == "zipf" and cfg.backward:
         general = run_general(cfg, x, dev, world)
@@ -601,6 +602,7 @@ def main():
             "step_roofline": {"algorithmic_bytes": step_bytes, "achieved_gbs": step_bytes / (ms * 1e-3) / 1e9,
                               "frac": step_bytes / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], "peak": peaks["hbm_gbs"]},
             "roofline": roofline, "kernels": kernels, "e2e": e2e, "e2e_copy_bound": copy_bound,
+            "e2e_training": e2e_train,
             "cpu_baseline": cpu, "cpu_port": port, "decode": decode,
             "general_path": general, "reference_gpu": ref_gpu, "config1": cfg1, "strong_scaling": strong,
             "config5_model": model, "fused_read_linear": fused_read, "clocks": clk, "gpu_launches": launches,
@@ -827,6 +829,88 @@ def run_graph_step(step, dev, world, reps: int = 10) -> dict:
     ms = max_over_ranks(e0.elapsed_time(e1) / reps, world)
     del graph
     return {"ms_per_step": ms, "replays": reps}
+
+
+def run_e2e_training(cfg, x, dev, steps, world):
+    """A training step of the operator end to end: each step's batch (write addresses and payload)
+    crosses from pinned host memory, the forward outputs are consumed on the device by a fixed
+    probe loss L = <values, G1> + <sums, G2> (G1, G2 device-resident like a next layer's weights;
+    its gradients are exactly G1 and G2, the upstream gradients of the device-timed step), and the
+    loss and the payload gradient -- the step's results for its caller -- cross back."""
+    import torch
+    from ravel_lm_b200 import causal_last_k_lookup, causal_sum_lookup
+    from ravel_lm_b200.ravel_memory import clear_tape_cache
+
+    class ProbeLoss(torch.autograd.Function):
+        @staticmethod
+        def forward(ctx, t, g):
+            ctx.save_for_backward(g)
+            return torch.dot(t.reshape(-1).float(), g.reshape(-1).float()) if t.numel() < (1 << 27) else \
+                sum(torch.dot(a.float(), b.float()) for a, b in zip(t.reshape(-1).split(1 << 26),
+                                                                     g.reshape(-1).split(1 << 26)))
+
+        @staticmethod
+        def backward(ctx, go):
+            (g,) = ctx.saved_tensors
+            return g * go.to(g.dtype), None
+
+    G1, G2 = x["g_vals"], x["g_sums"]
+    host = {"write": x["write"].to("cpu").pin_memory(), "payload": x["payload"].detach().to("cpu").pin_memory()}
+    if x["read"] is not None:
+        host["read"] = x["read"].to("cpu").pin_memory()
+    out_loss = torch.empty(1, dtype=torch.float32).pin_memory()
+    out_grad = torch.empty(tuple(x["payload"].shape), dtype=cfg.dtype).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = out_loss.numel() * 4 + out_grad.numel() * out_grad.element_size()
+    s_in, s_cmp, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def one():
+        with torch.cuda.stream(s_in):
+            w = host["write"].to(dev, non_blocking=True)
+            r = host["read"].to(dev, non_blocking=True) if "read" in host else None
+            p = host["payload"].to(dev, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(s_in)
+        with torch.cuda.stream(s_cmp):
+            s_cmp.wait_event(ev)
+            for t in (w, r, p):
+                if t is not None:
+                    t.record_stream(s_cmp)
+            clear_tape_cache()
+            p.requires_grad_(True)
+            vals, _ = causal_last_k_lookup(w, p, r, address_space=cfg.A, k=cfg.k)
+            sums, _ = causal_sum_lookup(w, p, r, address_space=cfg.A)
+            loss = ProbeLoss.apply(vals, G1) + ProbeLoss.apply(sums, G2)
+            loss.backward()
+            res = (loss.detach().reshape(1), p.grad)
+            ev2 = torch.cuda.Event()
+            ev2.record(s_cmp)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev2)
+            for t in res:
+                t.record_stream(s_out)
+            out_loss.copy_(res[0], non_blocking=True)
+            out_grad.copy_(res[1], non_blocking=True)
+
+    one()
+    torch.cuda.current_stream(dev).wait_stream(s_out)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    cur = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(cur)
+    s_in.wait_stream(cur)
+    for _ in range(steps):
+        one()
+    cur.wait_stream(s_out)
+    e1.record(cur)
+    torch.cuda.synchronize(dev)
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    return {"value": cfg.tokens * world / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps,
+            "path": "pinned host batch (addresses, payload) -> causal_last_k_lookup/causal_sum_lookup -> probe "
+                    "loss <values, G1> + <sums, G2> on the device -> backward -> pinned host loss + payload gradient",
+            "overlap": "copies in and out on their own streams; step i+1 host->device overlaps step i device->host"}
 
 
 def run_copy_bound(e2e: dict, dev, steps: int, world: int) -> dict:
