@@ -344,26 +344,39 @@ int sort_streams(const SortArgs& a0, void* out, void* other, int64_t S, int64_t 
     SortArgs a = a0;
     a.tiles = sp.tiles;
     if (sp.tiles > 1 && sp.tiles <= 8) {
-        // one cluster of `tiles` CTAs per stream, straight into `out`
-        const size_t smem = cluster_sort_smem<1024, 8, KeyT>();
-        if (set_smem(k_cluster_sort<KeyT, 1024, 8>, smem) == RAVEL_OK) {
+        // one cluster of CTAs per stream, straight into `out`: CTAs of CT threads x 8 keys,
+        // as many as the stream needs (2..8)
+        auto try_cluster = [&](auto ctc) -> int {
+            constexpr int CT = decltype(ctc)::value;
+            const int64_t tile = static_cast<int64_t>(CT) * 8;
+            const int64_t ctiles = (T + tile - 1) / tile;
+            if (ctiles < 2 || ctiles > 8) return -1;
+            const size_t smem = cluster_sort_smem<CT, 8, KeyT>();
+            if (set_smem(k_cluster_sort<KeyT, CT, 8>, smem) != RAVEL_OK) return -1;
             SortArgs ca = a;
             ca.keys_out = out;
             cudaLaunchConfig_t cfg = {};
-            cfg.gridDim = dim3(static_cast<unsigned>(S * sp.tiles));
-            cfg.blockDim = dim3(1024);
+            cfg.gridDim = dim3(static_cast<unsigned>(S * ctiles));
+            cfg.blockDim = dim3(CT);
             cfg.dynamicSmemBytes = smem;
             cfg.stream = st;
             cudaLaunchAttribute attr[1];
             attr[0].id = cudaLaunchAttributeClusterDimension;
-            attr[0].val.clusterDim.x = static_cast<unsigned>(sp.tiles);
+            attr[0].val.clusterDim.x = static_cast<unsigned>(ctiles);
             attr[0].val.clusterDim.y = 1;
             attr[0].val.clusterDim.z = 1;
             cfg.attrs = attr;
             cfg.numAttrs = 1;
-            if (cudaLaunchKernelEx(&cfg, k_cluster_sort<KeyT, 1024, 8>, ca) == cudaSuccess) return check_launch();
-            (void)cudaGetLastError();  // not schedulable here: use tiles + merges
-        }
+            if (cudaLaunchKernelEx(&cfg, k_cluster_sort<KeyT, CT, 8>, ca) == cudaSuccess) return check_launch();
+            (void)cudaGetLastError();  // not schedulable here
+            return -1;
+        };
+#ifndef RAVEL_SORT_CT
+#define RAVEL_SORT_CT 1024
+#endif
+        int rc = T <= static_cast<int64_t>(RAVEL_SORT_CT) * 64 ? try_cluster(IC<RAVEL_SORT_CT>{}) : -1;
+        if (rc < 0 && RAVEL_SORT_CT != 1024) rc = try_cluster(IC<1024>{});
+        if (rc >= 0) return rc;  // otherwise: tiles + merges
     }
     void* first = (sp.merge_passes % 2 == 0) ? out : other;
     a.keys_out = first;
