@@ -371,6 +371,10 @@ int sort_streams(const SortArgs& a0, void* out, void* other, int64_t S, int64_t 
             (void)cudaGetLastError();  // not schedulable here
             return -1;
         };
+// Build-time knob: threads of the cluster sort's CTAs for streams that fit 8 of them.
+// Measured at config 3 (T = 32768, tape build, us): 1024 threads (clusters of 4)
+// 71.5, 512 (clusters of 8, two CTAs per SM) 70.9, 256 73.5: the sort does not
+// gain from a second resident CTA.
 #ifndef RAVEL_SORT_CT
 #define RAVEL_SORT_CT 1024
 #endif
