@@ -499,35 +499,21 @@ def main():
     stream = torch.cuda.current_stream(dev).cuda_stream
     assert L.device_error(stream) == 0
 
-    records = defaultdict(list)
-    # events made before the timed region, so that timing each entry point adds
-    # only two event records per call to the host's work
-    pool = [torch.cuda.Event(enable_timing=True) for _ in range(2 * 16 * args.steps)]
-    used = [0]
-
-    def hook(name, thunk):
-        i = used[0]
-        if i + 2 > len(pool):
-            return thunk()
-        used[0] = i + 2
-        e0, e1 = pool[i], pool[i + 1]
-        e0.record()
-        rc = thunk()
-        e1.record()
-        records[name].append((e0, e1))
-        return rc
-
     barrier(world)
     torch.cuda.synchronize(dev)
     launches0 = L.kernel_launches()
-    L.set_call_hook(hook)
+    # every entry point's own GPU time, recorded by the library around its work
+    # (two cudaEventRecord calls per call; nothing on the Python side)
+    L.timing_start(16 * args.steps)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
     for _ in range(args.steps):
         step()
     t1.record()
     torch.cuda.synchronize(dev)
-    L.set_call_hook(None)
+    records = defaultdict(list)
+    for name, t in L.timing_stop():
+        records[name].append(t)
     launches = L.kernel_launches() - launches0
     barrier(world)
     clk = clocks.stop()
@@ -538,8 +524,7 @@ def main():
     peaks = measured_peaks()
     kb = kernel_bytes(cfg)
     kernels = {}
-    for name, evs in records.items():
-        times = [a.elapsed_time(b) for a, b in evs]
+    for name, times in records.items():
         avg_ms = sum(times) / len(times)
         ent = {"launches": len(times), "avg_us": avg_ms * 1000.0, "share": sum(times) / (ms_local * args.steps)}
         if name in kb:
@@ -694,16 +679,6 @@ def run_general(cfg, x, dev, world, steps: int = 5) -> dict:
     r = zipf_ranks(cfg.A, cfg.zipf_s, tuple(w.shape), g)
     p = x["payload"].detach().requires_grad_(True)
     gv, gs = x["g_vals"], x["g_sums"]
-    records = defaultdict(list)
-
-    def hook(name, thunk):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        rc = thunk()
-        e1.record()
-        records[name].append((e0, e1))
-        return rc
-
     def step():
         clear_tape_cache()
         p.grad = None
@@ -714,16 +689,18 @@ def run_general(cfg, x, dev, world, steps: int = 5) -> dict:
     for _ in range(2):
         step()
     torch.cuda.synchronize(dev)
-    L.set_call_hook(hook)
+    L.timing_start(16 * steps)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
     for _ in range(steps):
         step()
     t1.record()
     torch.cuda.synchronize(dev)
-    L.set_call_hook(None)
+    records = defaultdict(list)
+    for name, t in L.timing_stop():
+        records[name].append(t)
     ms = max_over_ranks(t0.elapsed_time(t1) / steps, world)
-    per = {n: sum(a.elapsed_time(b) for a, b in v) / len(v) * 1000.0 for n, v in records.items()}
+    per = {n: sum(v) / len(v) * 1000.0 for n, v in records.items()}
     return {"reads": f"independent Zipf(s={cfg.zipf_s}) reads of the same shape", "ms_per_step": ms,
             "value": cfg.tokens * world / (ms * 1e-3), "unit": "tokens/s", "steps": steps,
             "kernels_us": per}
@@ -1127,24 +1104,12 @@ def run_fused_read(dev, reps: int = 20) -> dict:
         out = {"config": "cfg5 layer: B8 T1024 H8 D32 fp32, k=2 + sum read, fuse 768->256, gate residual",
                "us_unfused": timed(unfused), "us_fused": timed(fused)}
         diff = (fused() - unfused()).abs().max().item()
-        recs = []
-
-        def hook(name, thunk):
-            if name != "ravel_gather_gemm":
-                return thunk()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            rc = thunk()
-            e1.record()
-            recs.append((e0, e1))
-            return rc
-
-        L.set_call_hook(hook)
+        L.timing_start(16 * reps)
         for _ in range(reps):
             fused()
         torch.cuda.synchronize(dev)
-        L.set_call_hook(None)
-    us = sum(a.elapsed_time(b) for a, b in recs) / len(recs) * 1000.0
+        recs = [t for name, t in L.timing_stop() if name == "ravel_gather_gemm"]
+    us = sum(recs) / len(recs) * 1000.0
     M = B * T
     flops = 2.0 * M * N * K
     # payload rows read once + sums + source table + weight + x, gate, out
@@ -1240,34 +1205,26 @@ def run_model(dev, rank: int, world: int, steps: int = 8, warmup: int = 3) -> di
                 step()
             torch.cuda.synchronize(dev)
             barrier(world)
-            ops = []
             if impl != "stock":
-                def hook(name, thunk):
-                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                    e0.record()
-                    rc = thunk()
-                    e1.record()
-                    ops.append((e0, e1))
-                    return rc
-                L.set_call_hook(hook)
+                L.timing_start(64 * steps)
             t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             t0.record()
             for _ in range(steps):
                 loss = step()
             t1.record()
             torch.cuda.synchronize(dev)
-            L.set_call_hook(None)
+            ops = [t for _name, t in L.timing_stop()] if impl != "stock" else []
             ms = max_over_ranks(t0.elapsed_time(t1) / steps, world)
             ent = {"ms_per_step": ms, "value": B * T * world / (ms * 1e-3), "unit": "tokens/s",
                    "loss": float(loss)}
             if ops:
-                op_ms = sum(a.elapsed_time(b) for a, b in ops) / steps
+                op_ms = sum(ops) / steps
                 ent["operator_ms_per_step"] = op_ms
                 ent["operator_share"] = op_ms / (t0.elapsed_time(t1) / steps)
             out[impl] = ent
         finally:
             use("stock")
-            L.set_call_hook(None)
+            L.timing_stop()
     del model, opt
     torch.cuda.empty_cache()
     return out

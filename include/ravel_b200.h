@@ -344,6 +344,21 @@ int ravel_clear_device_error(void* stream);
 /* Number of kernels this library has launched in this process (all devices). */
 uint64_t ravel_kernel_launches(void);
 
+/* ---- per-entry GPU timing (instrumentation; no reference counterpart) ---
+ * ravel_timing_start(n) creates n pairs of CUDA events on the current device
+ * and turns timing on, discarding earlier records.  While it is on, every
+ * compute entry point above records one pair on its stream around the work it
+ * enqueues (none while the stream is being captured into a graph; calls past
+ * the n-th are not recorded).  ravel_timing_stop() turns it off and keeps the
+ * records; ravel_timing_count() is how many were made;
+ * ravel_timing_read(i, &entry, &ms) waits for record i's end event and returns
+ * the entry point's name (a static string) and the milliseconds between the
+ * pair.  Call start/stop while no entry point runs on another thread. */
+int ravel_timing_start(int64_t max_records);
+int ravel_timing_stop(void);
+int64_t ravel_timing_count(void);
+int ravel_timing_read(int64_t i, const char** entry, float* ms);
+
 /* Human-readable name of a status code. */
 const char* ravel_status_string(int status);
 

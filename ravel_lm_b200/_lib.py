@@ -77,15 +77,24 @@ SIGNATURES = {
     "ravel_device_error": (_c_int, [ctypes.POINTER(_c_int), _c_vp]),
     "ravel_clear_device_error": (_c_int, [_c_vp]),
     "ravel_kernel_launches": (ctypes.c_uint64, []),
+    "ravel_timing_start": (_c_int, [_c_i64]),
+    "ravel_timing_stop": (_c_int, []),
+    "ravel_timing_count": (_c_i64, []),
+    "ravel_timing_read": (_c_int, [_c_i64, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(ctypes.c_float)]),
     "ravel_status_string": (ctypes.c_char_p, [_c_int]),
     "ravel_version": (ctypes.c_char_p, []),
 }
 
 _lib: Optional[ctypes.CDLL] = None
 
-# Optional observer of every compute call: fn(name, call) -> result.  bench.py
-# uses it to bracket individual entry points with CUDA events.
+# Optional observer of every compute call: fn(name, call) -> result (used by
+# tests to see which entry points a Python call reaches).  While one is set the
+# per-step paths go through it instead of their direct calls.
 _call_hook: Optional[Callable] = None
+
+# The C++ host extension (``_ravel_host``): the per-step calls of the Python
+# API -- argument checks, output allocation, the C-ABI call -- without ctypes.
+_host = None
 
 
 class RavelError(RuntimeError):
@@ -144,6 +153,32 @@ def call(name: str, *args) -> None:
         check(name, status)
 
 
+def host():
+    """The C++ host extension, next to the library (built with it); raise if it has not been built."""
+    global _host
+    if _host is not None:
+        return _host
+    load()  # the extension links against the library: load it from its own path first
+    try:
+        from . import _ravel_host
+    except ImportError as e:
+        raise RuntimeError("ravel_lm_b200: host extension _ravel_host is not built; run "
+                           "`python -m ravel_lm_b200.build`") from e
+    _host = _ravel_host
+    return _host
+
+
+def run(name: str, fn: Callable, *args):
+    """Call a host-extension function that returns (status, *outputs); raise on failure."""
+    if _call_hook is not None:
+        res = _call_hook(name, lambda: fn(*args))
+    else:
+        res = fn(*args)
+    if res[0]:
+        check(name, res[0])
+    return res
+
+
 def set_call_hook(hook: Optional[Callable]) -> None:
     global _call_hook
     _call_hook = hook
@@ -163,3 +198,23 @@ def kernel_launches() -> int:
 
 def clear_device_error(stream: int) -> None:
     check("ravel_clear_device_error", load().ravel_clear_device_error(stream))
+
+
+def timing_start(max_records: int) -> None:
+    """Record the GPU time of every compute entry point (up to ``max_records`` calls), natively."""
+    check("ravel_timing_start", load().ravel_timing_start(int(max_records)))
+
+
+def timing_stop() -> list:
+    """Stop recording; return [(entry point name, milliseconds)] in call order (waits for the GPU)."""
+    lib = load()
+    check("ravel_timing_stop", lib.ravel_timing_stop())
+    out = []
+    name, ms = ctypes.c_char_p(), ctypes.c_float()
+    for i in range(int(lib.ravel_timing_count())):
+        rc = lib.ravel_timing_read(i, ctypes.byref(name), ctypes.byref(ms))
+        if rc == RAVEL_OK:
+            out.append((name.value.decode(), float(ms.value)))
+        elif rc != RAVEL_ERR_INVALID_ARG:  # a record whose end was never enqueued is skipped
+            check("ravel_timing_read", rc)
+    return out

@@ -13,6 +13,7 @@
 #include <tuple>
 #include <utility>
 #include <type_traits>
+#include <vector>
 
 #include "common.cuh"
 #include "sort.cuh"
@@ -462,7 +463,7 @@ int tape_build_src(const AddrSrc& wsrc, const AddrSrc& rsrc, int32_t* raddr_out,
             ra.nvalid = nullptr;
             ra.mbit = 0;
             if (int e3 = sort_streams<KeyT>(ra, tv.rkeys, other, S, T, st)) return e3;
-            const int64_t per = (2 * T + MR_K - 1) / MR_K + 1;
+            const int64_t per = mr_chunks(T);
             k_merge_ranks<KeyT><<<grid_cap((S * per + 255) / 256), 256, 0, st>>>(
                 static_cast<const KeyT*>(tv.keys), tv.nvalid, static_cast<const KeyT*>(tv.rkeys), S, T, C,
                 tl.kl.tbits, tv.rridx, tv.ridx, tv.bstart);
@@ -1133,7 +1134,65 @@ int gather_args(ravel::GatherArgs& g, const float* payload, const int32_t* src, 
     g.C = static_cast<int>(C); g.k = static_cast<int>(k); g.D = static_cast<int>(D); g.K = static_cast<int>(K);
     return RAVEL_OK;
 }
+// ------------------------------------------------------------------ per-entry GPU timing
+// Off by default.  ravel_timing_start(n) makes n pairs of CUDA events; while it
+// is on, each timed entry point records one pair on its stream around the work
+// it enqueues (nothing while that stream is being captured into a graph), and
+// ravel_timing_read returns the entry's name and the milliseconds between the
+// pair.  One pair per call costs two cudaEventRecord calls of host time, less
+// than timing the call from the caller's language.
+struct EntryTiming {
+    std::atomic<bool> on{false};
+    std::atomic<int64_t> next{0};
+    int64_t cap = 0;
+    int device = -1;
+    std::vector<cudaEvent_t> ev;         // 2 per record
+    std::vector<const char*> name;       // entry point of each record
+    std::vector<unsigned char> closed;   // the end event was recorded
+};
+EntryTiming g_timing;
+
+class EntryTimer {
+  public:
+    EntryTimer(const char* entry, void* stream) : st_(static_cast<cudaStream_t>(stream)) {
+        if (!g_timing.on.load(std::memory_order_acquire)) return;
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(st_, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return;
+        const int64_t i = g_timing.next.fetch_add(1, std::memory_order_relaxed);
+        if (i >= g_timing.cap) return;
+        g_timing.name[i] = entry;
+        if (cudaEventRecord(g_timing.ev[2 * i], st_) == cudaSuccess) slot_ = i;
+    }
+    ~EntryTimer() {
+        if (slot_ >= 0 && cudaEventRecord(g_timing.ev[2 * slot_ + 1], st_) == cudaSuccess) g_timing.closed[slot_] = 1;
+    }
+    EntryTimer(const EntryTimer&) = delete;
+    EntryTimer& operator=(const EntryTimer&) = delete;
+
+  private:
+    cudaStream_t st_;
+    int64_t slot_ = -1;
+};
+
+void timing_release() {
+    if (g_timing.device >= 0) {
+        int cur = 0;
+        const bool switched = cudaGetDevice(&cur) == cudaSuccess && cur != g_timing.device &&
+                              cudaSetDevice(g_timing.device) == cudaSuccess;
+        for (cudaEvent_t e : g_timing.ev) cudaEventDestroy(e);
+        if (switched) cudaSetDevice(cur);
+    }
+    g_timing.ev.clear();
+    g_timing.name.clear();
+    g_timing.closed.clear();
+    g_timing.cap = 0;
+    g_timing.device = -1;
+    g_timing.next.store(0);
+}
 }  // namespace
+
+// one timing record around the rest of the enclosing entry point
+#define RAVEL_TIMED(entry, stream) EntryTimer ravel_entry_timer_(entry, stream)
 
 using namespace ravel;
 
@@ -1152,6 +1211,7 @@ int ravel_wait_selftest(const uint32_t* flag, void* stream) {
 
 int ravel_latestk_sources(const void* tape, int tape_flags, const void* raddr, int addr_dtype, int64_t B, int64_t T,
                           int64_t C, int64_t A, int64_t k, int32_t* src, void* stream) {
+    RAVEL_TIMED("ravel_latestk_sources", stream);
     if (int e = check_sizes(B, T, C, 0, A)) return e;
     if (k <= 0) return RAVEL_ERR_INVALID_ARG;
     if (k > 512) return RAVEL_ERR_UNSUPPORTED;
@@ -1177,6 +1237,7 @@ int ravel_latestk_sources(const void* tape, int tape_flags, const void* raddr, i
 
 int ravel_gather_rows(const float* payload, const int32_t* src, const float* sums, int64_t B, int64_t T, int64_t C,
                       int64_t D, int64_t k, float* rows, void* stream) {
+    RAVEL_TIMED("ravel_gather_rows", stream);
     GatherArgs g;
     if (int e = gather_args(g, payload, src, sums, B, T, C, D, k)) return e;
     if (g.M == 0) return RAVEL_OK;
@@ -1189,6 +1250,7 @@ int ravel_gather_rows(const float* payload, const int32_t* src, const float* sum
 int ravel_gather_gemm(const float* payload, const int32_t* src, const float* sums, int64_t B, int64_t T, int64_t C,
                       int64_t D, int64_t k, const float* weight, int64_t N, const float* x, const float* gate,
                       float* out, float* pre, void* stream) {
+    RAVEL_TIMED("ravel_gather_gemm", stream);
     GemmArgs a;
     std::memset(&a, 0, sizeof(a));
     if (int e = gather_args(a.g, payload, src, sums, B, T, C, D, k)) return e;
@@ -1250,6 +1312,7 @@ int ravel_tape_build_tokens(const int64_t* tokens, int n_literal, int64_t bos_to
                             const void* learned_read, int learned_dtype, const uint8_t* wmask, int64_t B, int64_t T,
                             int64_t C, int64_t A, int tape_flags, int32_t* read_addr_out, void* tape,
                             size_t tape_bytes, void* scratch, size_t scratch_bytes, void* stream) {
+    RAVEL_TIMED("ravel_tape_build_tokens", stream);
     if (n_literal < 0 || n_literal > C) return RAVEL_ERR_INVALID_ARG;
     if (learned_dtype != RAVEL_I32 && learned_dtype != RAVEL_I64) return RAVEL_ERR_INVALID_ARG;
     if (B * T * C == 0) return RAVEL_OK;
@@ -1274,6 +1337,7 @@ int ravel_tape_build_tokens(const int64_t* tokens, int n_literal, int64_t bos_to
 
 int ravel_literal_addresses(const int64_t* tokens, int64_t B, int64_t T, int n_heads, int64_t bos_token_id,
                             int64_t A, int64_t* out, void* stream) {
+    RAVEL_TIMED("ravel_literal_addresses", stream);
     if (B < 0 || T < 0 || n_heads < 0 || A <= 0) return RAVEL_ERR_INVALID_ARG;
     const int64_t n = B * T * n_heads;
     if (n == 0) return RAVEL_OK;
@@ -1285,6 +1349,7 @@ int ravel_literal_addresses(const int64_t* tokens, int64_t B, int64_t T, int n_h
 
 int ravel_gate_residual_fwd(const void* x, const void* gate, const void* fused, void* out, int64_t n, int dtype,
                             void* stream) {
+    RAVEL_TIMED("ravel_gate_residual_fwd", stream);
     if (n < 0) return RAVEL_ERR_INVALID_ARG;
     if (n == 0) return RAVEL_OK;
     if (!x || !gate || !fused || !out) return RAVEL_ERR_INVALID_ARG;
@@ -1301,6 +1366,7 @@ int ravel_gate_residual_fwd(const void* x, const void* gate, const void* fused, 
 
 int ravel_gate_residual_bwd(const void* gate, const void* fused, const void* grad_out, void* grad_gate,
                             void* grad_fused, int64_t n, int dtype, void* stream) {
+    RAVEL_TIMED("ravel_gate_residual_bwd", stream);
     if (n < 0) return RAVEL_ERR_INVALID_ARG;
     if (n == 0) return RAVEL_OK;
     if (!gate || !fused || !grad_out || !grad_gate || !grad_fused) return RAVEL_ERR_INVALID_ARG;
@@ -1322,6 +1388,7 @@ size_t ravel_rms_norm_scratch_bytes(int64_t M, int64_t K) {
 
 int ravel_rms_norm_fwd(const void* x, const void* weight, float eps, void* y, float* rstd, int64_t M, int64_t K,
                        int dtype, void* stream) {
+    RAVEL_TIMED("ravel_rms_norm_fwd", stream);
     if (M < 0 || K <= 0) return RAVEL_ERR_INVALID_ARG;
     if (K > kRmsMaxK) return RAVEL_ERR_UNSUPPORTED;
     if (M == 0) return RAVEL_OK;
@@ -1338,6 +1405,7 @@ int ravel_rms_norm_fwd(const void* x, const void* weight, float eps, void* y, fl
 int ravel_rms_norm_bwd(const void* x, const void* weight, const void* grad_y, const float* rstd, void* grad_x,
                        void* grad_weight, int64_t M, int64_t K, int dtype, void* scratch, size_t scratch_bytes,
                        void* stream) {
+    RAVEL_TIMED("ravel_rms_norm_bwd", stream);
     if (M < 0 || K <= 0) return RAVEL_ERR_INVALID_ARG;
     if (K > kRmsMaxK) return RAVEL_ERR_UNSUPPORTED;
     if (!x || !weight || !grad_y || !rstd || !grad_x || !grad_weight) return RAVEL_ERR_INVALID_ARG;
@@ -1375,6 +1443,7 @@ size_t ravel_scratch_bytes(int64_t B, int64_t T, int64_t C, int64_t D, int64_t A
 int ravel_tape_build(const void* waddr, const void* raddr, int addr_dtype, const uint8_t* wmask, int64_t B,
                      int64_t T, int64_t C, int64_t A, int tape_flags, void* tape, size_t tape_bytes,
                      void* scratch, size_t scratch_bytes, void* stream) {
+    RAVEL_TIMED("ravel_tape_build", stream);
     return tape_build(waddr, raddr, addr_dtype, wmask, B, T, C, A, tape_flags, tape, tape_bytes, scratch,
                       scratch_bytes, static_cast<cudaStream_t>(stream));
 }
@@ -1382,6 +1451,7 @@ int ravel_tape_build(const void* waddr, const void* raddr, int addr_dtype, const
 int ravel_latestk_fwd_tape(const void* tape, int tape_flags, const void* raddr, int addr_dtype,
                            const void* payload, int dtype, int64_t B, int64_t T, int64_t C, int64_t D,
                            int64_t A, int64_t k, void* out_vals, uint8_t* out_mask, void* stream) {
+    RAVEL_TIMED("ravel_latestk_fwd_tape", stream);
     return lk_fwd_tape(tape, tape_flags, raddr, addr_dtype, payload, dtype, B, T, C, D, A, k, out_vals, out_mask,
                        static_cast<cudaStream_t>(stream));
 }
@@ -1390,6 +1460,7 @@ int ravel_latestk_fwd(const void* waddr, const void* raddr, int addr_dtype, cons
                       const void* payload, int dtype, int64_t B, int64_t T, int64_t C, int64_t D, int64_t A,
                       int64_t k, void* out_vals, uint8_t* out_mask, void* tape, size_t tape_bytes,
                       void* scratch, size_t scratch_bytes, void* stream) {
+    RAVEL_TIMED("ravel_latestk_fwd", stream);
     if (raddr == waddr) raddr = nullptr;
     const int flags = (raddr ? RAVEL_TAPE_GENERAL_READS : 0) | (wmask ? RAVEL_TAPE_WRITE_MASK : 0);
     if (k <= 0) return RAVEL_ERR_INVALID_ARG;
@@ -1403,6 +1474,7 @@ int ravel_latestk_fwd(const void* waddr, const void* raddr, int addr_dtype, cons
 int ravel_latestk_bwd(const void* tape, int tape_flags, const void* raddr, int addr_dtype, const void* grad_vals,
                       int dtype, int64_t B, int64_t T, int64_t C, int64_t D, int64_t A, int64_t k,
                       void* grad_payload, void* scratch, size_t scratch_bytes, void* stream) {
+    RAVEL_TIMED("ravel_latestk_bwd", stream);
     return lk_bwd(tape, tape_flags, raddr, addr_dtype, grad_vals, dtype, B, T, C, D, A, k, grad_payload, scratch,
                   scratch_bytes, static_cast<cudaStream_t>(stream));
 }
@@ -1411,6 +1483,7 @@ int ravel_latestk_bwd_accumulate(const void* tape, int tape_flags, const void* r
                                  const void* grad_vals, int dtype, int64_t B, int64_t T, int64_t C, int64_t D,
                                  int64_t A, int64_t k, void* grad_payload, void* scratch, size_t scratch_bytes,
                                  void* stream) {
+    RAVEL_TIMED("ravel_latestk_bwd_accumulate", stream);
     return lk_bwd(tape, tape_flags, raddr, addr_dtype, grad_vals, dtype, B, T, C, D, A, k, grad_payload, scratch,
                   scratch_bytes, static_cast<cudaStream_t>(stream), /*accumulate=*/1);
 }
@@ -1418,6 +1491,7 @@ int ravel_latestk_bwd_accumulate(const void* tape, int tape_flags, const void* r
 int ravel_segsum_fwd_tape(const void* tape, int tape_flags, const void* raddr, int addr_dtype,
                           const void* payload, int dtype, int64_t B, int64_t T, int64_t C, int64_t D, int64_t A,
                           void* out_sums, uint8_t* out_mask, void* scratch, size_t scratch_bytes, void* stream) {
+    RAVEL_TIMED("ravel_segsum_fwd_tape", stream);
     return ss_fwd_tape(tape, tape_flags, raddr, addr_dtype, payload, dtype, B, T, C, D, A, out_sums, out_mask,
                        scratch, scratch_bytes, static_cast<cudaStream_t>(stream));
 }
@@ -1426,6 +1500,7 @@ int ravel_segsum_fwd(const void* waddr, const void* raddr, int addr_dtype, const
                      const void* payload, int dtype, int64_t B, int64_t T, int64_t C, int64_t D, int64_t A,
                      void* out_sums, uint8_t* out_mask, void* tape, size_t tape_bytes, void* scratch,
                      size_t scratch_bytes, void* stream) {
+    RAVEL_TIMED("ravel_segsum_fwd", stream);
     if (raddr == waddr) raddr = nullptr;
     const int flags = (raddr ? RAVEL_TAPE_GENERAL_READS : 0) | (wmask ? RAVEL_TAPE_WRITE_MASK : 0);
     if (int e = tape_build(waddr, raddr, addr_dtype, wmask, B, T, C, A, flags, tape, tape_bytes, scratch,
@@ -1438,6 +1513,7 @@ int ravel_segsum_fwd(const void* waddr, const void* raddr, int addr_dtype, const
 int ravel_segsum_fwd_noalloc(const void* waddr, const void* raddr, int addr_dtype, const uint8_t* wmask,
                              const void* payload, int dtype, int64_t B, int64_t T, int64_t C, int64_t D, int64_t A,
                              void* out_sums, uint8_t* out_mask, void* stream) {
+    RAVEL_TIMED("ravel_segsum_fwd_noalloc", stream);
     if (raddr == waddr) raddr = nullptr;
     const int flags = (raddr ? RAVEL_TAPE_GENERAL_READS : 0) | (wmask ? RAVEL_TAPE_WRITE_MASK : 0);
     if (int e = check_sizes(B, T, C, D, A)) return e;
@@ -1459,12 +1535,14 @@ int ravel_segsum_fwd_noalloc(const void* waddr, const void* raddr, int addr_dtyp
 int ravel_segsum_bwd(const void* tape, int tape_flags, const void* raddr, int addr_dtype, const void* grad_sums,
                      int dtype, int64_t B, int64_t T, int64_t C, int64_t D, int64_t A, void* grad_payload,
                      void* scratch, size_t scratch_bytes, void* stream) {
+    RAVEL_TIMED("ravel_segsum_bwd", stream);
     return ss_bwd(tape, tape_flags, raddr, addr_dtype, grad_sums, dtype, B, T, C, D, A, grad_payload, scratch,
                   scratch_bytes, static_cast<cudaStream_t>(stream));
 }
 
 int ravel_cache_read(const void* values, const uint8_t* filled, const void* addr, int addr_dtype, int dtype,
                      int64_t B, int64_t C, int64_t A, int64_t D, void* out_vals, uint8_t* out_mask, void* stream) {
+    RAVEL_TIMED("ravel_cache_read", stream);
     if (addr == nullptr) return RAVEL_ERR_INVALID_ARG;
     return cache_op(const_cast<void*>(values), const_cast<uint8_t*>(filled), addr, nullptr, addr_dtype, nullptr,
                     dtype, B, C, A, D, out_vals, out_mask, static_cast<cudaStream_t>(stream));
@@ -1472,6 +1550,7 @@ int ravel_cache_read(const void* values, const uint8_t* filled, const void* addr
 
 int ravel_cache_write(void* values, uint8_t* filled, const void* addr, int addr_dtype, const void* payload,
                       int dtype, int64_t B, int64_t C, int64_t A, int64_t D, void* stream) {
+    RAVEL_TIMED("ravel_cache_write", stream);
     if (addr == nullptr) return RAVEL_ERR_INVALID_ARG;
     return cache_op(values, filled, nullptr, addr, addr_dtype, payload, dtype, B, C, A, D, nullptr, nullptr,
                     static_cast<cudaStream_t>(stream));
@@ -1480,6 +1559,7 @@ int ravel_cache_write(void* values, uint8_t* filled, const void* addr, int addr_
 int ravel_cache_step(void* values, uint8_t* filled, const void* raddr, const void* waddr, int addr_dtype,
                      const void* payload, int dtype, int64_t B, int64_t C, int64_t A, int64_t D, void* out_vals,
                      uint8_t* out_mask, void* stream) {
+    RAVEL_TIMED("ravel_cache_step", stream);
     if (raddr == nullptr || waddr == nullptr) return RAVEL_ERR_INVALID_ARG;
     return cache_op(values, filled, raddr, waddr, addr_dtype, payload, dtype, B, C, A, D, out_vals, out_mask,
                     static_cast<cudaStream_t>(stream));
@@ -1493,6 +1573,7 @@ size_t ravel_cache_prefill_scratch_bytes(int64_t B, int64_t T, int64_t C, int64_
 int ravel_cache_prefill(void* values, uint8_t* filled, const void* addr, int addr_dtype, const void* payload,
                         int dtype, int64_t B, int64_t T, int64_t C, int64_t A, int64_t D, void* scratch,
                         size_t scratch_bytes, void* stream) {
+    RAVEL_TIMED("ravel_cache_prefill", stream);
     return cache_prefill(values, filled, addr, addr_dtype, payload, dtype, B, T, C, A, D, scratch, scratch_bytes,
                          static_cast<cudaStream_t>(stream));
 }
@@ -1514,6 +1595,49 @@ int ravel_clear_device_error(void* stream) {
 }
 
 uint64_t ravel_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int ravel_timing_start(int64_t max_records) {
+    if (max_records <= 0 || max_records > (int64_t{1} << 20)) return RAVEL_ERR_INVALID_ARG;
+    g_timing.on.store(false);
+    timing_release();
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return RAVEL_ERR_CUDA;
+    g_timing.device = dev;
+    g_timing.ev.reserve(static_cast<size_t>(2 * max_records));
+    for (int64_t i = 0; i < 2 * max_records; ++i) {
+        cudaEvent_t e;
+        if (cudaEventCreate(&e) != cudaSuccess) {
+            timing_release();
+            return RAVEL_ERR_CUDA;
+        }
+        g_timing.ev.push_back(e);
+    }
+    g_timing.name.assign(static_cast<size_t>(max_records), nullptr);
+    g_timing.closed.assign(static_cast<size_t>(max_records), 0);
+    g_timing.cap = max_records;
+    g_timing.next.store(0);
+    g_timing.on.store(true, std::memory_order_release);
+    return RAVEL_OK;
+}
+
+int ravel_timing_stop(void) {
+    g_timing.on.store(false, std::memory_order_release);
+    return RAVEL_OK;
+}
+
+int64_t ravel_timing_count(void) {
+    const int64_t n = g_timing.next.load();
+    return n < g_timing.cap ? n : g_timing.cap;
+}
+
+int ravel_timing_read(int64_t i, const char** entry, float* ms) {
+    if (entry == nullptr || ms == nullptr || i < 0 || i >= ravel_timing_count()) return RAVEL_ERR_INVALID_ARG;
+    if (g_timing.name[i] == nullptr || !g_timing.closed[i]) return RAVEL_ERR_INVALID_ARG;
+    if (cudaEventSynchronize(g_timing.ev[2 * i + 1]) != cudaSuccess) return RAVEL_ERR_CUDA;
+    if (cudaEventElapsedTime(ms, g_timing.ev[2 * i], g_timing.ev[2 * i + 1]) != cudaSuccess) return RAVEL_ERR_CUDA;
+    *entry = g_timing.name[i];
+    return RAVEL_OK;
+}
 
 const char* ravel_status_string(int status) {
     switch (status) {

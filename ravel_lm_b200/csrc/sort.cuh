@@ -398,14 +398,19 @@ __global__ void k_stream_offsets(const int* __restrict__ nvalid, int64_t* __rest
 // the stream: the latest valid write strictly below it), and bstart[j + 1] for
 // write j is the number of reads merged before it.  Each thread merges MR_K
 // consecutive elements of the merged order from its merge-path co-rank (a binary
-// search on its diagonal); bstart[0] = 0 and bstart[n + 1 .. T + 1] = T.
+// search on its diagonal); bstart[0] = 0 and bstart[n + 1 .. T + 1] = T, the
+// latter spread over MR_K-entry tail chunks so a heavy write mask (n << T) does
+// not leave one thread storing T entries.
 constexpr int MR_K = 16;
+// chunks per stream: the longest merge (2T elements), then the T + 2 bstart entries
+__host__ __device__ inline int64_t mr_merge_chunks(int64_t T) { return (2 * T + MR_K - 1) / MR_K; }
+__host__ __device__ inline int64_t mr_chunks(int64_t T) { return mr_merge_chunks(T) + (T + 2 + MR_K - 1) / MR_K; }
 template <typename KeyT>
 __global__ void __launch_bounds__(256) k_merge_ranks(const KeyT* wkeys, const int* nvalid, const KeyT* rkeys,
                                                    int64_t S, int64_t T, int64_t C, int tbits, int32_t* rridx,
                                                    int32_t* ridx, int32_t* bstart) {
     const KeyT tmask = (static_cast<KeyT>(1) << tbits) - 1;
-    const int64_t per = (2 * T + MR_K - 1) / MR_K + 1;  // chunks of the longest merge, plus one for the tail
+    const int64_t per = mr_chunks(T), merge = mr_merge_chunks(T);
     for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < S * per;
          e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         const int64_t s = e / per, chunk = e - s * per;
@@ -414,9 +419,13 @@ __global__ void __launch_bounds__(256) k_merge_ranks(const KeyT* wkeys, const in
         const KeyT* R = rkeys + s * T;
         int32_t* bs = bstart + s * (T + 2);
         const int64_t M = n + T;
-        if (chunk == per - 1) {  // bstart[0] and the entries past the last valid write
-            bs[0] = 0;
-            for (int64_t j = n + 1; j <= T + 1; ++j) bs[j] = static_cast<int32_t>(T);
+        if (chunk >= merge) {  // bstart[0] and the entries past the last valid write
+            const int64_t j0 = (chunk - merge) * MR_K;
+            const int64_t j1 = j0 + MR_K < T + 2 ? j0 + MR_K : T + 2;
+            for (int64_t j = j0; j < j1; ++j) {
+                if (j == 0) bs[0] = 0;
+                else if (j > n) bs[j] = static_cast<int32_t>(T);
+            }
             continue;
         }
         const int64_t d = chunk * MR_K;

@@ -123,6 +123,11 @@ def _ptr(t: Optional[Tensor]) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
 
+def _host():
+    """The C++ host extension (per-step calls without ctypes); raises if it is not built."""
+    return _lib._host or _lib.host()
+
+
 @functools.lru_cache(maxsize=256)
 def tape_bytes(B: int, T: int, C: int, A: int, flags: int) -> int:
     return int(_lib.load().ravel_tape_bytes(B, T, C, A, flags))
@@ -229,10 +234,8 @@ def _build_tape(write: Tensor, read: Optional[Tensor], write_mask: Optional[Tens
     m = None
     if write_mask is not None:
         m = write_mask.to(torch.bool).contiguous()
-    tape = torch.empty(tape_bytes(B, T, C, A, flags), dtype=torch.uint8, device=device)
-    scratch = torch.empty(scratch_bytes(B, T, C, D, A, k, dcode, flags), dtype=torch.uint8, device=device)
-    _lib.call("ravel_tape_build", w.data_ptr(), r.data_ptr() if read is not None else None, code, _ptr(m),
-              B, T, C, A, flags, tape.data_ptr(), tape.numel(), scratch.data_ptr(), scratch.numel(), st)
+    _, tape, scratch = _lib.run("ravel_tape_build", _host().tape_build, w, r if read is not None else None, code, m,
+                                A, flags, D, k, dcode)
     _tape_cache.put(write, read, write_mask, A, st, (tape, r, code))
     return tape, scratch, r, code, flags
 
@@ -260,14 +263,11 @@ def _latestk_fwd_impl(write: Tensor, payload: Tensor, read: Optional[Tensor], wr
     B, T, C = write.shape if prebuilt is None else prebuilt.shape
     D = payload.shape[-1]
     device = _require_cuda(write, payload, read, write_mask)
-    vals = payload.new_empty(B, T, C, k, D)
-    mask = torch.empty(B, T, C, k, dtype=torch.bool, device=device)
     tape, _scratch, r, code, flags = _tape_of(write, read, write_mask, address_space, D, k, _payload_code(payload),
                                               device, prebuilt)
     p = payload.contiguous()
-    _lib.call("ravel_latestk_fwd_tape", tape.data_ptr(), flags, r.data_ptr() if flags else None, code,
-              p.data_ptr(), _payload_code(p), B, T, C, D, address_space, k, vals.data_ptr(), mask.data_ptr(),
-              _stream(device))
+    _, vals, mask = _lib.run("ravel_latestk_fwd_tape", _host().latestk_fwd, tape, flags, r if flags else None, code,
+                             p, B, T, C, address_space, k)
     return vals, mask, tape
 
 
@@ -293,19 +293,16 @@ def _latestk_bwd_impl(tape: Tensor, grad_vals: Tensor, raddr: Tensor, flags: int
     D = grad_vals.shape[-1]
     device = _require_cuda(tape, grad_vals)
     g = grad_vals.contiguous()
-    if accumulate_into is None:
-        grad, entry = torch.empty(B, T, C, D, dtype=g.dtype, device=device), "ravel_latestk_bwd"
-    else:
-        grad, entry = accumulate_into, "ravel_latestk_bwd_accumulate"
-        if grad.dtype != g.dtype or grad.shape != (B, T, C, D) or not grad.is_contiguous():
+    _payload_code(g)
+    entry = "ravel_latestk_bwd"
+    if accumulate_into is not None:
+        entry = "ravel_latestk_bwd_accumulate"
+        a = accumulate_into
+        if a.dtype != g.dtype or a.shape != (B, T, C, D) or not a.is_contiguous() or a.device != device:
             raise RuntimeError("accumulation target must be a contiguous [B, T, C, D] tensor of the gradient dtype")
-    scratch = torch.empty(scratch_bytes(B, T, C, D, address_space, k, _payload_code(g), flags),
-                          dtype=torch.uint8, device=device)
     r, code = _addr(raddr)
-    _lib.call(entry, tape.data_ptr(), flags, r.data_ptr() if flags else None, code,
-              g.data_ptr(), _payload_code(g), B, T, C, D, address_space, k, grad.data_ptr(), scratch.data_ptr(),
-              scratch.numel(), _stream(device))
-    return grad
+    return _lib.run(entry, _host().latestk_bwd, tape, flags, r if flags else None, code, g, B, T, C, address_space, k,
+                    accumulate_into)[1]
 
 
 @torch.library.custom_op("ravel_b200::latestk_bwd", mutates_args=())
@@ -346,14 +343,11 @@ def _segsum_fwd_impl(write: Tensor, payload: Tensor, read: Optional[Tensor], wri
     B, T, C = write.shape if prebuilt is None else prebuilt.shape
     D = payload.shape[-1]
     device = _require_cuda(write, payload, read, write_mask)
-    sums = payload.new_empty(B, T, C, D)
-    mask = torch.empty(B, T, C, dtype=torch.bool, device=device)
     tape, scratch, r, code, flags = _tape_of(write, read, write_mask, address_space, D, 1, _payload_code(payload),
                                              device, prebuilt)
     p = payload.contiguous()
-    _lib.call("ravel_segsum_fwd_tape", tape.data_ptr(), flags, r.data_ptr() if flags else None, code,
-              p.data_ptr(), _payload_code(p), B, T, C, D, address_space, sums.data_ptr(), mask.data_ptr(),
-              scratch.data_ptr(), scratch.numel(), _stream(device))
+    _, sums, mask = _lib.run("ravel_segsum_fwd_tape", _host().segsum_fwd, tape, flags, r if flags else None, code, p,
+                             scratch, B, T, C, address_space)
     return sums, mask, tape
 
 
@@ -376,16 +370,12 @@ def _segsum_fwd_fake(write, payload, read, write_mask, address_space):
 def _segsum_bwd_impl(tape: Tensor, grad_sums: Tensor, raddr: Tensor, flags: int, B: int, T: int, C: int,
                      address_space: int) -> Tensor:
     D = grad_sums.shape[-1]
-    device = _require_cuda(tape, grad_sums)
+    _require_cuda(tape, grad_sums)
     g = grad_sums.contiguous()
-    grad = torch.empty(B, T, C, D, dtype=g.dtype, device=device)
-    scratch = torch.empty(scratch_bytes(B, T, C, D, address_space, 1, _payload_code(g), flags),
-                          dtype=torch.uint8, device=device)
+    _payload_code(g)
     r, code = _addr(raddr)
-    _lib.call("ravel_segsum_bwd", tape.data_ptr(), flags, r.data_ptr() if flags else None, code,
-              g.data_ptr(), _payload_code(g), B, T, C, D, address_space, grad.data_ptr(), scratch.data_ptr(),
-              scratch.numel(), _stream(device))
-    return grad
+    return _lib.run("ravel_segsum_bwd", _host().segsum_bwd, tape, flags, r if flags else None, code, g, B, T, C,
+                    address_space)[1]
 
 
 @torch.library.custom_op("ravel_b200::segsum_bwd", mutates_args=())
@@ -686,37 +676,35 @@ class RavelLayerCache:
 
         Decode calls this once per memory layer and token, so the common case --
         contiguous CUDA tensors on one device, int64 (or int32) addresses of one
-        type, payloads in the cache's dtype -- takes a short path; anything else
-        goes through the same checks as ``read`` and ``write``.  ``out``: a
-        (values [B, C, D], mask [B, C] bool) pair of contiguous tensors to write
-        the read into instead of new ones (a decode loop that reuses its buffers).
+        type, payloads in the cache's dtype -- is checked and launched by one
+        call into the C++ host extension; anything else goes through the same
+        checks as ``read`` and ``write``.  ``out``: a (values [B, C, D], mask
+        [B, C] bool) pair of contiguous tensors to write the read into instead of
+        new ones (a decode loop that reuses its buffers).
         """
         values, filled = self.values, self.filled
+        if _lib._call_hook is None and isinstance(read_addresses, Tensor) and isinstance(write_addresses, Tensor) \
+                and isinstance(payloads, Tensor):
+            # the common case, checked, allocated and launched in C++ (None: anything else)
+            res = (_lib._host or _lib.host()).cache_step(values, filled, read_addresses, write_addresses, payloads, out)
+            if res.__class__ is tuple:
+                return res
+            if res is not None:
+                _lib.check("ravel_cache_step", res)
         B, C = read_addresses.shape
         D = payloads.shape[-1]
         if write_addresses.shape != (B, C) or values.shape[:2] != (B, C) or values.shape[-1] != D:
             raise ValueError("cache and payload shapes do not match")
-        device = values.device
-        adt = read_addresses.dtype
-        fast = (device.type == "cuda" and filled.device == device and read_addresses.device == device
-                and write_addresses.device == device and payloads.device == device
-                and adt in (torch.int64, torch.int32) and write_addresses.dtype == adt
-                and payloads.dtype == values.dtype and filled.dtype == torch.bool and values.is_contiguous()
-                and filled.is_contiguous() and read_addresses.is_contiguous() and write_addresses.is_contiguous()
-                and payloads.is_contiguous())
-        if fast:
-            ra, wa, rcode, p = read_addresses, write_addresses, (
-                _lib.RAVEL_I64 if adt == torch.int64 else _lib.RAVEL_I32), payloads
-            code = _payload_code(values)
-        else:
-            device = _require_cuda(values, filled, read_addresses, write_addresses, payloads)
-            self._check_storage()
-            ra, rcode = _addr(read_addresses)
-            wa, wcode = _addr(write_addresses)
-            if rcode != wcode:
-                ra, wa, rcode = ra.to(torch.int64), wa.to(torch.int64), _lib.RAVEL_I64
-            p = payloads.to(values.dtype).contiguous()
-            code = _payload_code(values)
+        if payloads.shape[:2] != (B, C):
+            raise ValueError("cache and payload shapes do not match")
+        device = _require_cuda(values, filled, read_addresses, write_addresses, payloads)
+        self._check_storage()
+        ra, rcode = _addr(read_addresses)
+        wa, wcode = _addr(write_addresses)
+        if rcode != wcode:
+            ra, wa, rcode = ra.to(torch.int64), wa.to(torch.int64), _lib.RAVEL_I64
+        p = payloads.to(values.dtype).contiguous()
+        code = _payload_code(values)
         if out is None:
             vals = values.new_empty(B, C, D)
             mask = torch.empty(B, C, dtype=torch.bool, device=device)

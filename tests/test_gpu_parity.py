@@ -122,6 +122,9 @@ CASES = [
     ("d48_f64_el2", 1, 1700, 2, 48, 30, 2, torch.float64, False, True, "uniform"),
     ("general_bf16_d64_vec", 2, 3000, 4, 64, 500, 4, torch.bfloat16, True, True, "zipf1.05"),
     ("general_f16_d32_vec", 2, 2000, 3, 32, 300, 3, torch.float16, True, False, "uniform"),
+    # a mask keeping 3% of the positions: the bucket starts past the last valid write fill
+    # most of each stream's tail
+    ("general_sparse_mask", 2, 33000, 2, 16, 300, 3, torch.float32, True, 0.03, "uniform"),
 ]
 
 
@@ -143,7 +146,7 @@ def test_seeded_vs_oracle(oracle_mod, case):
     gen = torch.Generator().manual_seed(zlib.crc32(name.encode()))
     w = _gen_addresses(gen, dist, (B, T, C), A)
     r = _gen_addresses(gen, dist, (B, T, C), A) if reads else None
-    m = (torch.rand(B, T, generator=gen) < 0.7) if mask else None
+    m = (torch.rand(B, T, generator=gen) < (0.7 if mask is True else mask)) if mask else None
     if m is not None and B > 1:
         m[1] = False  # an all-masked batch row: empty streams inside the tape
     p = torch.randn(B, T, C, D, generator=gen).to(dt)

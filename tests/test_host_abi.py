@@ -102,6 +102,25 @@ def test_cache_validation_and_no_cpu_path():
         c.prefill(torch.zeros(2, 5, 3, dtype=torch.long), torch.zeros(2, 4, 3, 4))
     with pytest.raises(RuntimeError, match="CUDA tensors only"):
         c.prefill(torch.zeros(2, 5, 3, dtype=torch.long), torch.zeros(2, 5, 3, 4))
+    # step: the C++ fast path declines CPU tensors and the checked path raises
+    a = torch.zeros(2, 3, dtype=torch.long)
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        c.step(a, a, torch.zeros(2, 3, 4))
+    with pytest.raises(ValueError, match="do not match"):
+        c.step(a, a, torch.zeros(2, 2, 4))
+
+
+def test_host_extension_loads_and_timing_api_without_a_gpu():
+    import ravel_lm_b200._lib as L
+    h = L.host()
+    for name in ("cache_step", "tape_build", "latestk_fwd", "segsum_fwd", "segsum_bwd", "latestk_bwd"):
+        assert callable(getattr(h, name)), name
+    # the extension links to the very library ctypes loaded (one copy of its counters)
+    lib = L.load()
+    assert lib.ravel_timing_start(0) == L.RAVEL_ERR_INVALID_ARG
+    assert lib.ravel_timing_stop() == L.RAVEL_OK
+    assert lib.ravel_timing_count() == 0
+    assert L.timing_stop() == []
 
 
 def test_composite_key_dtype_matches_reference_golden():
