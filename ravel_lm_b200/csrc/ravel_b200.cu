@@ -336,16 +336,27 @@ int key32_of(int64_t B, int64_t T, int64_t C, int64_t A) {
 }
 
 // ------------------------------------------------------------------ tape build
-// Sort every stream's events (the keys sort_key builds) into `out`: one cluster
-// per stream for 2-8 tiles, else tiles sorted in shared memory and merged
-// through `other` (ping-pong, S*T keys).
+// Sort every stream's events (the keys sort_key builds) into `out0`: one cluster
+// per stream for 2-8 tiles, one CTA per stream for one tile, else tiles sorted in
+// shared memory and merged through `other` (ping-pong, S*T keys).  With `a1`
+// (a general tape's reads) the second sort into `out1` shares the launch of the
+// first when a stream takes one cluster or one CTA; streams that need merge
+// passes sort one after the other.
 template <typename KeyT>
-int sort_streams(const SortArgs& a0, void* out, void* other, int64_t S, int64_t T, cudaStream_t st) {
+int sort_streams(const SortArgs& a0, void* out0, const SortArgs* a1, void* out1, void* other, int64_t S, int64_t T,
+                 cudaStream_t st) {
     const SortPlan sp = sort_plan(T);
-    SortArgs a = a0;
-    a.tiles = sp.tiles;
+    const int64_t nsort = a1 != nullptr ? 2 : 1;
+    SortPair p;
+    p.a[0] = a0;
+    p.a[0].tiles = sp.tiles;
+    p.a[0].keys_out = out0;
+    p.a[1] = a1 != nullptr ? *a1 : a0;
+    p.a[1].tiles = sp.tiles;
+    p.a[1].keys_out = a1 != nullptr ? out1 : out0;
+    p.first = S;
     if (sp.tiles > 1 && sp.tiles <= 8) {
-        // one cluster of CTAs per stream, straight into `out`: CTAs of CT threads x 8 keys,
+        // one cluster of CTAs per stream, straight into the output: CTAs of CT threads x 8 keys,
         // as many as the stream needs (2..8)
         auto try_cluster = [&](auto ctc) -> int {
             constexpr int CT = decltype(ctc)::value;
@@ -354,10 +365,8 @@ int sort_streams(const SortArgs& a0, void* out, void* other, int64_t S, int64_t 
             if (ctiles < 2 || ctiles > 8) return -1;
             const size_t smem = cluster_sort_smem<CT, 8, KeyT>();
             if (set_smem(k_cluster_sort<KeyT, CT, 8>, smem) != RAVEL_OK) return -1;
-            SortArgs ca = a;
-            ca.keys_out = out;
             cudaLaunchConfig_t cfg = {};
-            cfg.gridDim = dim3(static_cast<unsigned>(S * ctiles));
+            cfg.gridDim = dim3(static_cast<unsigned>(nsort * S * ctiles));
             cfg.blockDim = dim3(CT);
             cfg.dynamicSmemBytes = smem;
             cfg.stream = st;
@@ -368,7 +377,7 @@ int sort_streams(const SortArgs& a0, void* out, void* other, int64_t S, int64_t 
             attr[0].val.clusterDim.z = 1;
             cfg.attrs = attr;
             cfg.numAttrs = 1;
-            if (cudaLaunchKernelEx(&cfg, k_cluster_sort<KeyT, CT, 8>, ca) == cudaSuccess) return check_launch();
+            if (cudaLaunchKernelEx(&cfg, k_cluster_sort<KeyT, CT, 8>, p) == cudaSuccess) return check_launch();
             (void)cudaGetLastError();  // not schedulable here
             return -1;
         };
@@ -383,14 +392,19 @@ int sort_streams(const SortArgs& a0, void* out, void* other, int64_t S, int64_t 
         if (rc < 0 && RAVEL_SORT_CT != 1024) rc = try_cluster(IC<1024>{});
         if (rc >= 0) return rc;  // otherwise: tiles + merges
     }
-    void* first = (sp.merge_passes % 2 == 0) ? out : other;
-    a.keys_out = first;
-    const int64_t grid = S * sp.tiles;
+    if (sp.tiles > 1 && a1 != nullptr) {  // the two sorts share the merge scratch: one after the other
+        if (int e = sort_streams<KeyT>(a0, out0, nullptr, nullptr, other, S, T, st)) return e;
+        return sort_streams<KeyT>(*a1, out1, nullptr, nullptr, other, S, T, st);
+    }
+    void* first = (sp.merge_passes % 2 == 0) ? out0 : other;
+    p.a[0].keys_out = first;
+    p.first = S * sp.tiles;
+    const int64_t grid = nsort * S * sp.tiles;
     auto launch = [&](auto th) -> int {
         constexpr int TH = decltype(th)::value;
         const size_t smem = tile_sort_smem<TH, 8, KeyT>();
         if (int e = set_smem(k_tile_sort<KeyT, TH, 8>, smem)) return e;
-        k_tile_sort<KeyT, TH, 8><<<static_cast<unsigned>(grid), TH, smem, st>>>(a);
+        k_tile_sort<KeyT, TH, 8><<<static_cast<unsigned>(grid), TH, smem, st>>>(p);
         return check_launch();
     };
     int e = RAVEL_OK;
@@ -407,7 +421,7 @@ int sort_streams(const SortArgs& a0, void* out, void* other, int64_t S, int64_t 
     int64_t run = static_cast<int64_t>(sp.threads) * 8;
     const int64_t cps = (T + MERGE_OUT - 1) / MERGE_OUT;
     for (int pass = 0; pass < sp.merge_passes; ++pass) {
-        KeyT* dst = (src == static_cast<const KeyT*>(out)) ? static_cast<KeyT*>(other) : static_cast<KeyT*>(out);
+        KeyT* dst = (src == static_cast<const KeyT*>(out0)) ? static_cast<KeyT*>(other) : static_cast<KeyT*>(out0);
         k_merge<KeyT><<<static_cast<unsigned>(S * cps), MERGE_THREADS, 0, st>>>(src, dst, T, run, cps);
         if (int e2 = check_launch()) return e2;
         src = dst;
@@ -450,26 +464,22 @@ int tape_build_src(const AddrSrc& wsrc, const AddrSrc& rsrc, int32_t* raddr_out,
     void* other = static_cast<char*>(scratch) + sl.off_sort;
     int rc = with_key(tl.kl.key64, [&](auto kt) -> int {
         using KeyT = decltype(kt);
-        if (int e = sort_streams<KeyT>(a, tv.keys, other, S, T, st)) return e;
-        if (tl.general) {
-            k_stream_offsets<<<1, 1024, 0, st>>>(tv.nvalid, tv.soff, S, T);
-            if (int e2 = check_launch()) return e2;
-            // read tape: the reads sorted like the writes (by address, t), then ranked
-            // against the sorted writes; the rank is each read's latest earlier write
-            SortArgs ra = a;
-            ra.src = (flags & RAVEL_TAPE_GENERAL_READS) ? rsrc : wsrc;
-            ra.addr_out = (flags & RAVEL_TAPE_GENERAL_READS) ? raddr_out : nullptr;
-            ra.wmask = nullptr;
-            ra.nvalid = nullptr;
-            ra.mbit = 0;
-            if (int e3 = sort_streams<KeyT>(ra, tv.rkeys, other, S, T, st)) return e3;
-            const int64_t per = mr_chunks(T);
-            k_merge_ranks<KeyT><<<grid_cap((S * per + 255) / 256), 256, 0, st>>>(
-                static_cast<const KeyT*>(tv.keys), tv.nvalid, static_cast<const KeyT*>(tv.rkeys), S, T, C,
-                tl.kl.tbits, tv.rridx, tv.ridx, tv.bstart);
-            if (int e3 = check_launch()) return e3;
-        }
-        return RAVEL_OK;
+        if (!tl.general) return sort_streams<KeyT>(a, tv.keys, nullptr, nullptr, other, S, T, st);
+        // read tape: the reads sorted like the writes (by address, t) -- in the writes'
+        // launch -- then ranked against the sorted writes (the rank is each read's
+        // latest earlier write); the merge kernel also writes the stream offsets
+        SortArgs ra = a;
+        ra.src = (flags & RAVEL_TAPE_GENERAL_READS) ? rsrc : wsrc;
+        ra.addr_out = (flags & RAVEL_TAPE_GENERAL_READS) ? raddr_out : nullptr;
+        ra.wmask = nullptr;
+        ra.nvalid = nullptr;
+        ra.mbit = 0;
+        if (int e = sort_streams<KeyT>(a, tv.keys, &ra, tv.rkeys, other, S, T, st)) return e;
+        const int64_t per = mr_chunks(T);
+        k_merge_ranks<KeyT><<<grid_cap((S * per + 255) / 256), 256, 0, st>>>(
+            static_cast<const KeyT*>(tv.keys), tv.nvalid, static_cast<const KeyT*>(tv.rkeys), S, T, C,
+            tl.kl.tbits, tv.rridx, tv.ridx, tv.bstart, tv.soff);
+        return check_launch();
     });
     return rc;
 }
@@ -977,7 +987,7 @@ int cache_prefill(void* values, uint8_t* filled, const void* addr, int addr_dtyp
     const int vb = row_bytes > 0 ? pick_vec_bytes(row_bytes, addr_bits(values) | addr_bits(payload)) : 2;
     return with_key(pl.kl.key64, [&](auto kt) -> int {
         using KeyT = decltype(kt);
-        if (int e = sort_streams<KeyT>(a, sc + pl.off_keys, sc + pl.off_other, S, T, st)) return e;
+        if (int e = sort_streams<KeyT>(a, sc + pl.off_keys, nullptr, nullptr, sc + pl.off_other, S, T, st)) return e;
         return with_vb(vb, [&](auto vbc) -> int {
             constexpr int VB = decltype(vbc)::value;
             k_cache_prefill<KeyT, VB><<<grid_cap((S * T + 255) / 256), 256, 0, st>>>(

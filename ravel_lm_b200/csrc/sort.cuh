@@ -14,10 +14,12 @@
 //                 warp, warp-private digit histograms and a block-wide scan.
 //   k_merge       merge-path merge of sorted runs for streams longer than a
 //                 tile (log2(tiles) passes, global memory ping-pong).
-//   k_merge_ranks general tapes: the reads sorted like the writes, then merged
-//                 with the sorted writes; each read's rank = searchsorted(right=
-//                 True)-1 of ravel_memory.py:159, restricted to the stream, and
-//                 each write's first read ranked at or after it.
+//   k_merge_ranks general tapes: the reads sorted like the writes (in the
+//                 writes' launch), then merged with the sorted writes; each
+//                 read's rank = searchsorted(right=True)-1 of
+//                 ravel_memory.py:159, restricted to the stream, and each
+//                 write's first read ranked at or after it; block 0 also writes
+//                 the per-stream offsets of the valid writes.
 #pragma once
 
 #include <cooperative_groups.h>
@@ -37,6 +39,14 @@ struct SortArgs {
     void* keys_out;        // [S][T]
     int* nvalid;           // [S], pre-zeroed, or null when there is no mask
     int clamp;             // addresses clamped to [0, A-1] (decode cache) instead of wrapped
+};
+
+// Two sorts in one launch: the blocks (tile sort) or clusters (cluster sort)
+// below `first` sort a[0], the rest a[1] -- a general tape's writes and reads,
+// which are independent.  A single sort sets `first` to the whole grid.
+struct SortPair {
+    SortArgs a[2];
+    int64_t first;
 };
 
 // Sort key of event (b, c, t) (stream s = b*C + c): (invalid bit | address)
@@ -59,7 +69,7 @@ __device__ __forceinline__ KeyT sort_key(const SortArgs& a, int64_t b, int64_t c
 }
 
 template <typename KeyT, int THREADS, int ITEMS>
-__global__ void __launch_bounds__(THREADS) k_tile_sort(SortArgs a) {
+__global__ void __launch_bounds__(THREADS) k_tile_sort(const __grid_constant__ SortPair p) {
     constexpr int TILE = THREADS * ITEMS;
     constexpr int NW = THREADS / 32;
     extern __shared__ __align__(16) unsigned char smem[];
@@ -68,9 +78,11 @@ __global__ void __launch_bounds__(THREADS) k_tile_sort(SortArgs a) {
     uint16_t* whist = reinterpret_cast<uint16_t*>(kb + TILE);
     uint32_t* dbase = reinterpret_cast<uint32_t*>(whist + NW * 256);
 
+    const int which = static_cast<int64_t>(blockIdx.x) >= p.first ? 1 : 0;
+    const SortArgs& a = p.a[which];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t C = a.C, T = a.T;
-    int64_t blk = blockIdx.x;
+    int64_t blk = static_cast<int64_t>(blockIdx.x) - (which ? p.first : 0);
     // c varies fastest so that the C streams of one (b, tile) read the same
     // address sectors back to back (addresses are [B, T, C]).
     const int64_t c = blk % C;
@@ -168,7 +180,7 @@ __global__ void __launch_bounds__(THREADS) k_tile_sort(SortArgs a) {
 // [r*8192, (r+1)*8192) of the stream: no global round trips, no merge passes.
 // Used for streams of 2..8 tiles (T <= 65536); cluster size = tiles.
 template <typename KeyT, int THREADS, int ITEMS>
-__global__ void __launch_bounds__(THREADS) k_cluster_sort(SortArgs a) {
+__global__ void __launch_bounds__(THREADS) k_cluster_sort(const __grid_constant__ SortPair p) {
     namespace cg = cooperative_groups;
     constexpr int TILE = THREADS * ITEMS;
     constexpr int NW = THREADS / 32;
@@ -183,9 +195,12 @@ __global__ void __launch_bounds__(THREADS) k_cluster_sort(SortArgs a) {
     cg::cluster_group cluster = cg::this_cluster();
     const int crank = static_cast<int>(cluster.block_rank());
     const int csize = static_cast<int>(cluster.num_blocks());
+    const int64_t cl = blockIdx.x / csize;  // cluster = stream of one of the two sorts
+    const int which = cl >= p.first ? 1 : 0;
+    const SortArgs& a = p.a[which];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t C = a.C, T = a.T;
-    const int64_t s = blockIdx.x / csize;
+    const int64_t s = cl - (which ? p.first : 0);
     const int64_t b = s / C, c = s % C;
     const int64_t t0 = static_cast<int64_t>(crank) * TILE;
 
@@ -353,8 +368,9 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_merge(const KeyT* __restrict_
 
 // Exclusive prefix of the per-stream valid-write counts: soff[s] = writes of the
 // streams before s in the reference's global sorted order; soff[S] = total.
-__global__ void k_stream_offsets(const int* __restrict__ nvalid, int64_t* __restrict__ soff, int64_t S,
-                                 int64_t T) {
+// Run by one whole block (any multiple of 32 threads).
+__device__ void stream_offsets_block(const int* __restrict__ nvalid, int64_t* __restrict__ soff, int64_t S,
+                                     int64_t T) {
     __shared__ int64_t carry;
     if (threadIdx.x == 0) carry = 0;
     __syncthreads();
@@ -400,7 +416,8 @@ __global__ void k_stream_offsets(const int* __restrict__ nvalid, int64_t* __rest
 // consecutive elements of the merged order from its merge-path co-rank (a binary
 // search on its diagonal); bstart[0] = 0 and bstart[n + 1 .. T + 1] = T, the
 // latter spread over MR_K-entry tail chunks so a heavy write mask (n << T) does
-// not leave one thread storing T entries.
+// not leave one thread storing T entries.  Block 0 first writes the stream
+// offsets (stream_offsets_block), which this launch's merges do not read.
 constexpr int MR_K = 16;
 // chunks per stream: the longest merge (2T elements), then the T + 2 bstart entries
 __host__ __device__ inline int64_t mr_merge_chunks(int64_t T) { return (2 * T + MR_K - 1) / MR_K; }
@@ -408,7 +425,8 @@ __host__ __device__ inline int64_t mr_chunks(int64_t T) { return mr_merge_chunks
 template <typename KeyT>
 __global__ void __launch_bounds__(256) k_merge_ranks(const KeyT* wkeys, const int* nvalid, const KeyT* rkeys,
                                                    int64_t S, int64_t T, int64_t C, int tbits, int32_t* rridx,
-                                                   int32_t* ridx, int32_t* bstart) {
+                                                   int32_t* ridx, int32_t* bstart, int64_t* soff) {
+    if (blockIdx.x == 0) stream_offsets_block(nvalid, soff, S, T);
     const KeyT tmask = (static_cast<KeyT>(1) << tbits) - 1;
     const int64_t per = mr_chunks(T), merge = mr_merge_chunks(T);
     for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < S * per;
