@@ -72,7 +72,7 @@ def parse():
     ap.add_argument("--batch", type=int, default=None, help="override B per GPU (small profiling cases)")
     ap.add_argument("--ops", choices=["all", "lk", "ss"], default="all",
                     help="ops in a step (profiling a single op; the benchmark runs all)")
-    ap.add_argument("--only", choices=["fused_read", "decode", "config1", "model"], default=None,
+    ap.add_argument("--only", choices=["fused_read", "decode", "config1", "config5_op", "model"], default=None,
                     help="run one side measurement alone and print its JSON (profiling)")
     return ap.parse_args()
 
@@ -447,7 +447,7 @@ def main():
     rank, world, local = dist_setup()
     if args.only is not None:
         dev = torch.device("cuda", local)
-        fn = {"fused_read": run_fused_read, "decode": run_decode, "config1": run_cfg1,
+        fn = {"fused_read": run_fused_read, "decode": run_decode, "config1": run_cfg1, "config5_op": run_cfg5_op,
               "model": lambda d: run_model(d, rank, world)}[args.only]
         res = fn(dev)
         if rank == 0:
@@ -559,6 +559,7 @@ def main():
             ref_gpu = run_reference_gpu(cfg, x, dev, steps=5, warmup=args.warmup)
         cfg1 = run_cfg1(dev)
         fused_read = run_fused_read(dev)
+    cfg5_op = run_cfg5_op(dev) if world == 1 and args.config != 5 else None
     del x, p, gv, gs
     torch.cuda.empty_cache()
     model = None
@@ -590,7 +591,8 @@ def main():
             "e2e_training": e2e_train,
             "cpu_baseline": cpu, "cpu_port": port, "decode": decode,
             "general_path": general, "reference_gpu": ref_gpu, "config1": cfg1, "strong_scaling": strong,
-            "config5_model": model, "fused_read_linear": fused_read, "clocks": clk, "gpu_launches": launches,
+            "config5_op": cfg5_op, "config5_model": model, "fused_read_linear": fused_read, "clocks": clk,
+            "gpu_launches": launches,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -1053,6 +1055,56 @@ def run_cfg1(dev, reps: int = 200) -> dict:
         finally:
             tl1._HAS_TRITON = old
     return out
+
+
+def run_cfg5_op(dev, steps: int = 50) -> dict:
+    """Configuration 5's operator step (latest-k k=2 + sum, forward + backward, learned read heads
+    apart from the writes, B8 T1024 H8 D32 fp32) through the public API: eager ms per step with
+    nothing else on the host, each entry point's GPU time (recorded by the library), and the same
+    step replayed from a CUDA graph.  The small shape that host work, not HBM, decides."""
+    import torch
+    import ravel_lm_b200._lib as L
+    from collections import defaultdict
+    from ravel_lm_b200 import causal_last_k_lookup, causal_sum_lookup
+    from ravel_lm_b200.ravel_memory import clear_tape_cache
+    from ravel_lm_b200.workloads import CONFIGS, make_inputs
+    cfg = CONFIGS[5]
+    x = make_inputs(cfg, device=dev)
+    w, r = x["write"], x["read"]
+    p = x["payload"].detach().requires_grad_(True)
+    gv, gs = x["g_vals"], x["g_sums"]
+
+    def step():
+        clear_tape_cache()
+        p.grad = None
+        v, _ = causal_last_k_lookup(w, p, r, address_space=cfg.A, k=cfg.k)
+        s_, _ = causal_sum_lookup(w, p, r, address_space=cfg.A)
+        torch.autograd.backward([v, s_], [gv, gs])
+
+    def timed(n):
+        for _ in range(10):
+            step()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            step()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / n
+
+    ms = timed(steps)
+    L.timing_start(16 * steps)
+    ms_timed = timed(steps)
+    per = defaultdict(list)
+    for name, t in L.timing_stop()[-5 * steps:]:
+        per[name].append(t)
+    graph = run_graph_step(step, dev, 1, reps=steps)
+    return {"config": "cfg5 operator: B8 T1024 H8 D32 fp32, k=2 + sum, learned reads apart from writes, fwd + bwd",
+            "ms_per_step_eager": ms, "tokens_per_s_eager": cfg.tokens / (ms * 1e-3),
+            "ms_per_step_eager_entry_timing": ms_timed,
+            "entry_us": {n: sum(v) / len(v) * 1000.0 for n, v in per.items()},
+            "ms_per_step_graph": graph["ms_per_step"], "target_ms_eager": 0.2}
 
 
 def run_fused_read(dev, reps: int = 20) -> dict:
