@@ -187,6 +187,14 @@ RangePlan range_plan(int64_t S, int64_t T, int64_t slots, int64_t rl_max = int64
 #endif
 static_assert(RAVEL_RS_RLMIN >= 16 && RAVEL_RS_RLMIN <= 64 && RAVEL_RS_RLMIN % 8 == 0, "range length floor");
 int64_t max_ranges(int64_t T) { return T > 0 ? (T + RAVEL_RS_RLMIN - 1) / RAVEL_RS_RLMIN : 1; }
+// Build-time knob: rows of at least this many 16-byte vectors give each lane of the
+// range scan two vectors (half the lanes per row, twice the ranges per warp).
+// Measured at config 3 (128-byte rows, 8 vectors): one vector per lane 170.6 /
+// 160.0 us (sum forward / backward), two 223.4 / 211.3 us.
+#ifndef RAVEL_RS_VPL2_NVEC
+#define RAVEL_RS_VPL2_NVEC 64
+#endif
+static_assert(RAVEL_RS_VPL2_NVEC >= 2 && RAVEL_RS_VPL2_NVEC <= 64, "two vectors per lane need two per row");
 
 int sm_count() {
     static int n = 0;
@@ -709,7 +717,7 @@ int launch_segscan(const TapeView& tv, const TapeLayout& tl, int64_t B, int64_t 
     const int64_t nvec = (D * static_cast<int64_t>(in_es)) % 16 == 0 ? D * static_cast<int64_t>(in_es) / 16 : 0;
     int vpl = 0, lshift = 0;
     if (nvec > 0 && (nvec & (nvec - 1)) == 0 && nvec <= 64) {
-        vpl = nvec == 64 ? 2 : 1;
+        vpl = nvec >= RAVEL_RS_VPL2_NVEC ? 2 : 1;
         const int64_t L = nvec / vpl;
         while ((int64_t{1} << lshift) < L) ++lshift;
     }

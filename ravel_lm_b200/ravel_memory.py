@@ -79,20 +79,25 @@ def _stream(device: torch.device) -> int:
                                               torch.cuda.current_device())
 
 
+def _capturing() -> bool:
+    """Whether the current CUDA stream is being captured into a graph (torch's own query)."""
+    return torch._C._cuda_isCurrentStreamCapturing()
+
+
 def _require_cuda(*tensors: Optional[Tensor]) -> torch.device:
-    dev = None
+    first = None
     for t in tensors:
         if t is None:
             continue
-        if t.device.type != "cuda":
+        if not t.is_cuda:
             raise RuntimeError(
                 f"ravel_lm_b200 runs on CUDA tensors only (got a {t.device.type} tensor); "
                 "there is no CPU fallback")
-        if dev is None:
-            dev = t.device
-        elif t.device != dev:
-            raise RuntimeError(f"tensors are on different devices: {dev} and {t.device}")
-    return dev
+        if first is None:
+            first = t
+        elif t.get_device() != first.get_device():
+            raise RuntimeError(f"tensors are on different devices: {first.device} and {t.device}")
+    return None if first is None else first.device
 
 
 def _aliases(read: Optional[Tensor], write: Tensor) -> bool:
@@ -106,8 +111,10 @@ def _aliases(read: Optional[Tensor], write: Tensor) -> bool:
         return True
     if torch.compiler.is_compiling():
         return False
+    if read.data_ptr() != write.data_ptr():  # the common case of distinct reads: one comparison
+        return False
     return (read.dtype == write.dtype and read.shape == write.shape and read.stride() == write.stride()
-            and read.device == write.device and read.data_ptr() == write.data_ptr())
+            and read.device == write.device)
 
 
 def _flags(read: Optional[Tensor], write_mask: Optional[Tensor]) -> int:
@@ -166,7 +173,7 @@ class _TapeCache:
     def _key(write, read, mask, A, stream):
         return (A, _flags(read, mask), tuple(write.shape), write.dtype, write.device, stream, write._version,
                 None if read is None else (read.dtype, read._version),
-                None if mask is None else (mask.dtype, mask._version), torch.cuda.is_current_stream_capturing())
+                None if mask is None else (mask.dtype, mask._version), _capturing())
 
     def get(self, write, read, mask, A, stream):
         if self.key is None:

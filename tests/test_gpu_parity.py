@@ -125,6 +125,12 @@ CASES = [
     # a mask keeping 3% of the positions: the bucket starts past the last valid write fill
     # most of each stream's tail
     ("general_sparse_mask", 2, 33000, 2, 16, 300, 3, torch.float32, True, 0.03, "uniform"),
+    # 1 KB rows: the range scan's two-vectors-per-lane form (payload rows, or float accumulator rows
+    # of the general path)
+    ("d256_f32_1kb_rows", 1, 3000, 2, 256, 50, 2, torch.float32, False, False, "uniform"),
+    ("d512_bf16_1kb_rows_mask", 1, 1200, 2, 512, 30, 2, torch.bfloat16, False, True, "uniform"),
+    ("d128_f64_1kb_general", 1, 1500, 2, 128, 40, 2, torch.float64, True, True, "uniform"),
+    ("d256_bf16_general_acc_1kb", 1, 2000, 2, 256, 60, 2, torch.bfloat16, True, False, "uniform"),
 ]
 
 
