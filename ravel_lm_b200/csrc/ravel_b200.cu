@@ -32,7 +32,7 @@ struct TapeLayout {
     int general;            // reads use the search path
     int has_mask;
     size_t key_bytes;
-    size_t off_keys, off_nvalid, off_soff, off_ridx, off_rkeys, off_rridx, off_bstart, total;
+    size_t off_keys, off_nvalid, off_soff, off_ridx, off_rkeys, off_rridx, off_bstart, off_mkeys, off_mrole, total;
 };
 
 TapeLayout tape_layout(int64_t B, int64_t T, int64_t C, int64_t A, int flags) {
@@ -49,7 +49,9 @@ TapeLayout tape_layout(int64_t B, int64_t T, int64_t C, int64_t A, int flags) {
     t.off_rkeys = t.off_ridx + (t.general ? align_up(N * 4) : 0);
     t.off_rridx = t.off_rkeys + (t.general ? align_up(S * static_cast<size_t>(T) * t.key_bytes) : 0);
     t.off_bstart = t.off_rridx + (t.general ? align_up(S * static_cast<size_t>(T) * 4) : 0);
-    t.total = t.off_bstart + (t.general ? align_up(S * static_cast<size_t>(T + 2) * 4) : 0);
+    t.off_mkeys = t.off_bstart + (t.general ? align_up(S * static_cast<size_t>(T + 2) * 4) : 0);
+    t.off_mrole = t.off_mkeys + (t.general ? align_up(S * static_cast<size_t>(2 * T) * t.key_bytes) : 0);
+    t.total = t.off_mrole + (t.general ? align_up(S * static_cast<size_t>(2 * T)) : 0);
     return t;
 }
 
@@ -61,6 +63,9 @@ struct TapeView {
     void* rkeys;       // general tapes: [S][T] read keys sorted by (address, t), write key width
     int32_t* rridx;    // general tapes: [S][T] latest valid write below each sorted read, -1 if none
     int32_t* bstart;   // general tapes: [S][T+2] first sorted read of each rridx value + 1
+    void* mkeys;       // general tapes: [S][2T] the valid writes and the reads merged (a read first on equal keys)
+    uint8_t* mrole;    // general tapes: [S][2T] bit 0: a write; bit 1: a read whose latest earlier
+                       // valid write has its address (the sum lookup's mask)
 };
 
 TapeView tape_view(const void* tape, const TapeLayout& t) {
@@ -73,6 +78,8 @@ TapeView tape_view(const void* tape, const TapeLayout& t) {
     v.rkeys = t.general ? static_cast<void*>(base + t.off_rkeys) : nullptr;
     v.rridx = t.general ? reinterpret_cast<int32_t*>(base + t.off_rridx) : nullptr;
     v.bstart = t.general ? reinterpret_cast<int32_t*>(base + t.off_bstart) : nullptr;
+    v.mkeys = t.general ? static_cast<void*>(base + t.off_mkeys) : nullptr;
+    v.mrole = t.general ? reinterpret_cast<uint8_t*>(base + t.off_mrole) : nullptr;
     return v;
 }
 
@@ -224,8 +231,9 @@ ScratchLayout scratch_layout(int64_t B, int64_t T, int64_t C, int64_t D, int64_t
     l.off_ticket = l.off_flags + align_up(nch * 4);
     l.off_agg = l.off_ticket + 256;
     l.off_incl = l.off_agg + align_up(nch * static_cast<size_t>(D) * ab);
-    // range-scan blocks hold at least GS_WARPS ranges
-    const size_t nb = S * static_cast<size_t>((max_ranges(T) + GS_WARPS - 1) / GS_WARPS);
+    // range-scan blocks hold at least GS_WARPS ranges; general tapes' merged scans walk up to 2T positions
+    const int64_t Tm = t.general ? 2 * T : T;
+    const size_t nb = S * static_cast<size_t>((max_ranges(Tm) + GS_WARPS - 1) / GS_WARPS);
     l.off_bflags = l.off_incl + align_up(nch * static_cast<size_t>(D) * ab);
     l.off_bval = l.off_bflags + align_up((nb + 1) * 4);
     l.off_big = l.off_bval + align_up(nb * 2 * static_cast<size_t>(D) * ab);
@@ -486,7 +494,7 @@ int tape_build_src(const AddrSrc& wsrc, const AddrSrc& rsrc, int32_t* raddr_out,
         const int64_t per = mr_chunks(T);
         k_merge_ranks<KeyT><<<grid_cap((S * per + 255) / 256), 256, 0, st>>>(
             static_cast<const KeyT*>(tv.keys), tv.nvalid, static_cast<const KeyT*>(tv.rkeys), S, T, C,
-            tl.kl.tbits, tv.rridx, tv.ridx, tv.bstart, tv.soff);
+            tl.kl.tbits, tv.rridx, tv.ridx, tv.bstart, tv.soff, static_cast<KeyT*>(tv.mkeys), tv.mrole);
         return check_launch();
     });
     return rc;
@@ -693,7 +701,8 @@ int lk_bwd(const void* tape, int flags, const void* raddr, int addr_dtype, const
 template <typename KeyT, int DT>
 int launch_segscan(const TapeView& tv, const TapeLayout& tl, int64_t B, int64_t T, int64_t C, int64_t D,
                    const void* in, int in_sorted, void* out, int out_sorted, uint8_t* out_mask, int inclusive,
-                   int reverse, void* scratch, const ScratchLayout& sl, cudaStream_t st) {
+                   int reverse, void* scratch, const ScratchLayout& sl, cudaStream_t st, int merged = 0,
+                   int load_role = 0) {
     using Acc = typename Elem<DT>::Acc;
     const ScanPlan sp = scan_plan(T, D, DT);
     ScanArgs<Acc> a;
@@ -722,10 +731,19 @@ int launch_segscan(const TapeView& tv, const TapeLayout& tl, int64_t B, int64_t 
         while ((int64_t{1} << lshift) < L) ++lshift;
     }
     const size_t ovec = (16 / in_es) * out_es;  // output bytes per 16-byte input vector
+    // merged scans (a general tape's writes and reads in one sequence, see k_range_scan):
+    // row indices must leave bits 29 and 30 of the scan's row word free
+    if (merged && !(vpl && addr_bits(in) % 16 == 0 && addr_bits(out) % ovec == 0 && B * T * C < (int64_t{1} << 29) &&
+                    tv.mkeys != nullptr && !in_sorted && !out_sorted))
+        return -1;  // not this kernel's shape: the caller takes the two-pass form
     if (vpl && addr_bits(in) % 16 == 0 && addr_bits(out) % ovec == 0) {
+        const int64_t Tm = merged ? 2 * T : T;  // positions per stream of the scanned sequence
         GsArgs ga;
         ga.S = B * C;
-        ga.keys = tv.keys;
+        ga.keys = merged ? tv.mkeys : tv.keys;
+        ga.role = merged ? tv.mrole : nullptr;
+        ga.Ts = Tm;
+        ga.load_role = load_role;
         ga.nvalid = tv.nvalid;
         ga.T = T; ga.C = C;
         ga.D = static_cast<uint32_t>(D);
@@ -738,8 +756,9 @@ int launch_segscan(const TapeView& tv, const TapeLayout& tl, int64_t B, int64_t 
             constexpr int VPL = decltype(vplc)::value;
             constexpr bool IS = decltype(inc)::value != 0;
             constexpr bool OS = decltype(outc)::value != 0;
-            auto kern = inclusive ? k_range_scan<KeyT, DT, IS, OS, true, VPL>
-                                  : k_range_scan<KeyT, DT, IS, OS, false, VPL>;
+            auto kern = merged ? k_range_scan<KeyT, DT, false, false, false, VPL, true>
+                               : (inclusive ? k_range_scan<KeyT, DT, IS, OS, true, VPL, false>
+                                            : k_range_scan<KeyT, DT, IS, OS, false, VPL, false>);
             const int64_t gpb = GS_WARPS * (int64_t{32} >> lshift);
             constexpr int64_t kRlMax = 1024;
             const int64_t bmw_max = gpb * kRlMax / 32 + 2;
@@ -750,11 +769,11 @@ int launch_segscan(const TapeView& tv, const TapeLayout& tl, int64_t B, int64_t 
             // Short streams (64-position ranges do not fill one wave): about two
             // blocks per SM, ranges down to RAVEL_RS_RLMIN positions.
             const int64_t S = B * C > 0 ? B * C : 1;
-            const int64_t blocks64 = S * (((T + 63) / 64 + gpb - 1) / gpb);
+            const int64_t blocks64 = S * (((Tm + 63) / 64 + gpb - 1) / gpb);
             const bool short_streams = blocks64 < static_cast<int64_t>(occ) * sm_count();
             int64_t bps = short_streams ? 2 * sm_count() / S : static_cast<int64_t>(occ) * sm_count() * RAVEL_RS_WAVES / S;
             if (bps < 1) bps = 1;
-            const RangePlan rp = range_plan(1, T, bps * gpb, kRlMax, short_streams ? RAVEL_RS_RLMIN : 64);
+            const RangePlan rp = range_plan(1, Tm, bps * gpb, kRlMax, short_streams ? RAVEL_RS_RLMIN : 64);
             ga.R = rp.R;
             ga.RL = rp.RL;
             ga.snap = static_cast<int>(rp.RL / 2 < GS_SNAP ? rp.RL / 2 : GS_SNAP);
@@ -853,6 +872,14 @@ int ss_fwd_tape(const void* tape, int flags, const void* raddr, int addr_dtype, 
                 return launch_segscan<KeyT, DT>(tv, tl, B, T, C, D, payload, 0, out_sums, 0, out_mask,
                                                 /*inclusive=*/0, /*reverse=*/0, scratch, sl, st);
             }
+            // one scan over the merged sequence of valid writes and reads: writes add their
+            // payload rows, reads store the running sum and the mask the merge decided
+            if (D > 0) {
+                const int rc = launch_segscan<KeyT, DT>(tv, tl, B, T, C, D, payload, 0, out_sums, 0, out_mask, 0, 0,
+                                                        scratch, sl, st, /*merged=*/1, /*load_role=*/1);
+                if (rc >= 0) return rc;
+            }
+            // other row shapes: an inclusive scan of the writes, then a gather per read
             void* tapebuf = static_cast<char*>(scratch) + sl.off_big;
             if (int e = launch_segscan<KeyT, DT>(tv, tl, B, T, C, D, payload, 0, tapebuf, 1, nullptr, 1, 0,
                                                  scratch, sl, st))
@@ -903,6 +930,13 @@ int ss_bwd(const void* tape, int flags, const void* raddr, int addr_dtype, const
             if (tl.has_mask &&
                 cudaMemsetAsync(grad_payload, 0, static_cast<size_t>(N) * D * elem_bytes(DT), st) != cudaSuccess)
                 return RAVEL_ERR_CUDA;
+            // the merged sequence scanned from its end: reads add their gradient rows, every
+            // valid write stores the running sum of the reads after it (masked writes stay 0)
+            {
+                const int rc = launch_segscan<KeyT, DT>(tv, tl, B, T, C, D, grad_sums, 0, grad_payload, 0, nullptr, 0,
+                                                        1, scratch, sl, st, /*merged=*/1, /*load_role=*/0);
+                if (rc >= 0) return rc;
+            }
             // rows of 2^m <= 32 vectors: a reverse inclusive scan of the read
             // gradients over the read tape (suffix sums per address, payload dtype,
             // in accbuf), then each write copies the suffix at its first read

@@ -710,6 +710,11 @@ struct GsArgs {
     int bmw;               // segment-start bitmap words per block
     unsigned* bflags;      // [S*CB] look-back states, then the ticket counter; zeroed before launch
     void* bval;            // Acc [S*CB][2][D]: block aggregate, block inclusive carry
+    // merged scans (general tapes): the stream's valid writes and all its reads in one
+    // sequence; only positions of role `load_role` read a row, only the others store one
+    const uint8_t* role;   // [S][Ts]: bit 0 a write, bit 1 a read with an earlier write of its address
+    int64_t Ts;            // keys (and roles) per stream in `keys`
+    int load_role;
 };
 
 inline size_t range_scan_smem(int vpl, int64_t gpb, int64_t D, size_t acc_bytes, int64_t bmw) {
@@ -719,7 +724,7 @@ inline size_t range_scan_smem(int vpl, int64_t gpb, int64_t D, size_t acc_bytes,
     return b;
 }
 
-template <typename KeyT, int DT, bool IN_SORTED, bool OUT_SORTED, bool INCL, int VPL>
+template <typename KeyT, int DT, bool IN_SORTED, bool OUT_SORTED, bool INCL, int VPL, bool MERGED>
 // Build-time knob: RAVEL_GS_MINB = resident blocks per SM the register allocation
 // must allow.  Measured at config 3 (sum forward / backward, us): none 168 / 160,
 // 6 blocks (80 registers) 166 / 158, 8 blocks (64 registers) 168 / 161, 1 block
@@ -759,7 +764,9 @@ __global__ void RAVEL_GS_BOUNDS k_range_scan(GsArgs a) {
     __syncthreads();
     const int64_t tk = s_tk;
     const int64_t s = tk / a.CB, cb = tk - s * a.CB;
-    const int32_t n_s = a.nvalid ? a.nvalid[s] : static_cast<int32_t>(a.T);
+    // merged: the stream's valid writes and its T reads
+    const int32_t n_s = (a.nvalid ? a.nvalid[s] : static_cast<int32_t>(a.T)) + (MERGED ? static_cast<int32_t>(a.T) : 0);
+    const int64_t Ts = MERGED ? a.Ts : a.T;
     const int64_t r0 = cb * GPB;
     const int nr = static_cast<int>(a.R - r0 < GPB ? a.R - r0 : GPB);
     const int32_t RL = static_cast<int32_t>(a.RL);
@@ -767,7 +774,9 @@ __global__ void RAVEL_GS_BOUNDS k_range_scan(GsArgs a) {
     if (nr <= 0 || X0 >= n_s) return;  // whole block: the empty tail of the stream
 
     const int32_t dir = a.reverse ? -1 : 1;
-    const KeyT* kbase = static_cast<const KeyT*>(a.keys) + s * a.T + (a.reverse ? n_s - 1 : 0);
+    const KeyT* kbase = static_cast<const KeyT*>(a.keys) + s * Ts + (a.reverse ? n_s - 1 : 0);
+    const uint8_t* rbase = MERGED ? a.role + s * Ts + (a.reverse ? n_s - 1 : 0) : nullptr;
+    const uint8_t lrole = static_cast<uint8_t>(a.load_role);
     const uint32_t tix0 = static_cast<uint32_t>(s * a.T) + static_cast<uint32_t>(a.reverse ? n_s - 1 : 0);
     // 1. segment starts of scan positions [X0, X0 + 32 bmw)
     for (int w = warp; w < a.bmw; w += GS_WARPS) {
@@ -842,8 +851,12 @@ __global__ void RAVEL_GS_BOUNDS k_range_scan(GsArgs a) {
 #pragma unroll
         for (int q = 0; q < NE; ++q) acc[q] = Acc(0);
         KeyT kn[PU];
+        bool ld[PU];  // the position reads a row (merged: only positions of the loading role)
 #pragma unroll
-        for (int u = 0; u < PU; ++u) kn[u] = u < n ? kbase[dir * (p0 + u)] : KeyT(0);
+        for (int u = 0; u < PU; ++u) {
+            kn[u] = u < n ? kbase[dir * (p0 + u)] : KeyT(0);
+            ld[u] = u < n && (!MERGED || (rbase[dir * (p0 + u)] & 1) == lrole);
+        }
         for (int32_t i0 = 0; i0 < nmax; i0 += PU) {
             uint4 w[PU][VPL];
 #pragma unroll
@@ -852,13 +865,14 @@ __global__ void RAVEL_GS_BOUNDS k_range_scan(GsArgs a) {
                 const uint32_t row = row_in(p0 + i, kn[u]);
 #pragma unroll
                 for (int v = 0; v < VPL; ++v)
-                    w[u][v] = i < n ? ld_nc_v4(in + static_cast<uint64_t>(row) * rbi + v * L * 16u)
+                    w[u][v] = ld[u] ? ld_nc_v4(in + static_cast<uint64_t>(row) * rbi + v * L * 16u)
                                     : make_uint4(0u, 0u, 0u, 0u);
             }
 #pragma unroll
             for (int u = 0; u < PU; ++u) {
                 const int32_t i = i0 + PU + u;
                 kn[u] = i < n ? kbase[dir * (p0 + i)] : KeyT(0);
+                ld[u] = i < n && (!MERGED || (rbase[dir * (p0 + i)] & 1) == lrole);
             }
 #pragma unroll
             for (int u = 0; u < PU; ++u)
@@ -953,15 +967,20 @@ __global__ void RAVEL_GS_BOUNDS k_range_scan(GsArgs a) {
     const int32_t nb = (len + GS_U - 1) / GS_U;
     const uint32_t lane_slot = static_cast<uint32_t>(lane);
 
-    auto load_keys = [&](int32_t b, KeyT (&k)[GS_U]) {
+    // merged scans: each position's role byte beside its key
+    auto load_keys = [&](int32_t b, KeyT (&k)[GS_U], uint8_t (&r)[GS_U]) {
 #pragma unroll
         for (int u = 0; u < GS_U; ++u) {
             const int32_t i = b * GS_U + u;
-            if (i < len) k[u] = kbase[dir * (i + (i < nA ? offA : offB))];
+            if (i < len) {
+                const int32_t sp = i + (i < nA ? offA : offB);
+                k[u] = kbase[dir * sp];
+                if (MERGED) r[u] = rbase[dir * sp];
+            }
         }
     };
     KeyT klast = KeyT(0);  // key of the row staged last
-    auto stage = [&](int32_t b, const KeyT (&kb)[GS_U]) {
+    auto stage = [&](int32_t b, const KeyT (&kb)[GS_U], const uint8_t (&rb)[GS_U]) {
         if (b < nb) {
             const uint32_t slot0 = static_cast<uint32_t>(b % GS_Q) * GS_U;
 #pragma unroll
@@ -981,12 +1000,25 @@ __global__ void RAVEL_GS_BOUNDS k_range_scan(GsArgs a) {
                         rin = rout = rows_of(k & tmask);
                     }
                     const uint32_t slot = (slot0 + u) * 32 + lane_slot;
+                    // merged: a loading position stores nothing (bit 30), the others read nothing;
+                    // bit 29 carries a storing read's mask
+                    const bool loads = !MERGED || (rb[u] & 1) == lrole;
+                    if (loads) {
 #pragma unroll
-                    for (int v = 0; v < VPL; ++v)
-                        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(ring + (slot * VPL + v) * 16),
-                                     "l"(in + static_cast<uint64_t>(rin) * rbi + v * L * 16u)
-                                     : "memory");
-                    asm volatile("st.shared.u32 [%0], %1;" ::"r"(meta + slot * 4), "r"(rout | (st ? 0x80000000u : 0u))
+                        for (int v = 0; v < VPL; ++v)
+                            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(ring + (slot * VPL + v) * 16),
+                                         "l"(in + static_cast<uint64_t>(rin) * rbi + v * L * 16u)
+                                         : "memory");
+                    } else {
+#pragma unroll
+                        for (int v = 0; v < VPL; ++v)
+                            asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(ring + (slot * VPL + v) * 16),
+                                         "r"(0u)
+                                         : "memory");
+                    }
+                    const uint32_t mflags = MERGED ? ((loads ? 0x40000000u : 0u) | ((rb[u] & 2) ? 0x20000000u : 0u)) : 0u;
+                    asm volatile("st.shared.u32 [%0], %1;" ::"r"(meta + slot * 4),
+                                 "r"(rout | mflags | (st ? 0x80000000u : 0u))
                                  : "memory");
                 }
             }
@@ -1012,7 +1044,8 @@ __global__ void RAVEL_GS_BOUNDS k_range_scan(GsArgs a) {
                 uint32_t mw;
                 asm volatile("ld.shared.u32 %0, [%1];" : "=r"(mw) : "r"(meta + slot * 4));
                 const bool st = static_cast<int32_t>(mw) < 0;
-                const uint32_t orow = mw & 0x7fffffffu;
+                const bool store = !MERGED || (mw & 0x40000000u) == 0u;
+                const uint32_t orow = mw & (MERGED ? 0x1fffffffu : 0x7fffffffu);
 #pragma unroll
                 for (int v = 0; v < VPL; ++v) {
                     const RawWords<16> x = lds_words<16>(ring + (slot * VPL + v) * 16);
@@ -1025,29 +1058,37 @@ __global__ void RAVEL_GS_BOUNDS k_range_scan(GsArgs a) {
                         if (INCL) { c += f[e]; o[e] = c; }
                         else { o[e] = c; c += f[e]; }
                     }
-                    st_frag<OutT, EL>(reinterpret_cast<OutT*>(out + static_cast<uint64_t>(orow) * rbo +
-                                                              v * L * static_cast<uint32_t>(EL * sizeof(OutT))),
-                                      pack<OutT, Acc, EL>(o));
+                    if (store)
+                        st_frag<OutT, EL>(reinterpret_cast<OutT*>(out + static_cast<uint64_t>(orow) * rbo +
+                                                                  v * L * static_cast<uint32_t>(EL * sizeof(OutT))),
+                                          pack<OutT, Acc, EL>(o));
                 }
-                if (omask != nullptr) omask[orow] = st ? 0 : 1;
+                if (MERGED) {
+                    if (omask != nullptr && store) omask[orow] = (mw & 0x20000000u) ? 1 : 0;
+                } else if (omask != nullptr) {
+                    omask[orow] = st ? 0 : 1;
+                }
             }
         }
     };
     KeyT k0[GS_U], k1[GS_U];
+    uint8_t r0v[GS_U], r1v[GS_U];
+#pragma unroll
+    for (int u = 0; u < GS_U; ++u) r0v[u] = r1v[u] = 0;
 #pragma unroll
     for (int b = 0; b < GS_Q - 1; ++b) {
-        load_keys(b, k0);
-        stage(b, k0);
+        load_keys(b, k0, r0v);
+        stage(b, k0, r0v);
     }
-    load_keys(GS_Q - 1, k0);
-    load_keys(GS_Q, k1);
+    load_keys(GS_Q - 1, k0, r0v);
+    load_keys(GS_Q, k1, r1v);
     for (int32_t b = 0; b < nb; b += 2) {
-        stage(b + GS_Q - 1, k0);
-        load_keys(b + GS_Q + 1, k0);
+        stage(b + GS_Q - 1, k0, r0v);
+        load_keys(b + GS_Q + 1, k0, r0v);
         process(b);
         if (b + 1 < nb) {
-            stage(b + GS_Q, k1);
-            load_keys(b + GS_Q + 2, k1);
+            stage(b + GS_Q, k1, r1v);
+            load_keys(b + GS_Q + 2, k1, r1v);
             process(b + 1);
         }
     }

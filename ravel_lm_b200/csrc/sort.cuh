@@ -417,7 +417,9 @@ __device__ void stream_offsets_block(const int* __restrict__ nvalid, int64_t* __
 // search on its diagonal); bstart[0] = 0 and bstart[n + 1 .. T + 1] = T, the
 // latter spread over MR_K-entry tail chunks so a heavy write mask (n << T) does
 // not leave one thread storing T entries.  Block 0 first writes the stream
-// offsets (stream_offsets_block), which this launch's merges do not read.
+// offsets (stream_offsets_block), which this launch's merges do not read.  The
+// merged order itself is kept (mkeys, and mrole: bit 0 a write, bit 1 a read
+// whose latest earlier write has its address) for the sum lookup's scans.
 constexpr int MR_K = 16;
 // chunks per stream: the longest merge (2T elements), then the T + 2 bstart entries
 __host__ __device__ inline int64_t mr_merge_chunks(int64_t T) { return (2 * T + MR_K - 1) / MR_K; }
@@ -425,51 +427,85 @@ __host__ __device__ inline int64_t mr_chunks(int64_t T) { return mr_merge_chunks
 template <typename KeyT>
 __global__ void __launch_bounds__(256) k_merge_ranks(const KeyT* wkeys, const int* nvalid, const KeyT* rkeys,
                                                    int64_t S, int64_t T, int64_t C, int tbits, int32_t* rridx,
-                                                   int32_t* ridx, int32_t* bstart, int64_t* soff) {
+                                                   int32_t* ridx, int32_t* bstart, int64_t* soff, KeyT* mkeys,
+                                                   uint8_t* mrole) {
+    // the merged keys and roles a warp produces (32 chunks of MR_K positions), staged so
+    // that they leave in runs of 32 consecutive positions instead of one per lane
+    __shared__ KeyT sk[8][32 * MR_K];
+    __shared__ uint8_t sr[8][32 * MR_K];
     if (blockIdx.x == 0) stream_offsets_block(nvalid, soff, S, T);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const KeyT tmask = (static_cast<KeyT>(1) << tbits) - 1;
-    const int64_t per = mr_chunks(T), merge = mr_merge_chunks(T);
-    for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < S * per;
-         e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t s = e / per, chunk = e - s * per;
-        const int64_t n = nvalid ? nvalid[s] : T;
-        const KeyT* W = wkeys + s * T;
-        const KeyT* R = rkeys + s * T;
-        int32_t* bs = bstart + s * (T + 2);
-        const int64_t M = n + T;
-        if (chunk >= merge) {  // bstart[0] and the entries past the last valid write
-            const int64_t j0 = (chunk - merge) * MR_K;
-            const int64_t j1 = j0 + MR_K < T + 2 ? j0 + MR_K : T + 2;
-            for (int64_t j = j0; j < j1; ++j) {
-                if (j == 0) bs[0] = 0;
-                else if (j > n) bs[j] = static_cast<int32_t>(T);
+    const int64_t per = mr_chunks(T), merge = mr_merge_chunks(T), total = S * per;
+    // whole warps iterate together (the staging below is warp-wide)
+    for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + warp * 32; base < total;
+         base += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t e = base + lane;
+        int64_t s = 0, d = 0;
+        int cnt = 0;  // merged positions [d, d + cnt) of stream s staged by this lane
+        if (e < total) {
+            s = e / per;
+            const int64_t chunk = e - s * per;
+            const int64_t n = nvalid ? nvalid[s] : T;
+            const KeyT* W = wkeys + s * T;
+            const KeyT* R = rkeys + s * T;
+            int32_t* bs = bstart + s * (T + 2);
+            const int64_t M = n + T;
+            if (chunk >= merge) {  // bstart[0] and the entries past the last valid write
+                const int64_t j0 = (chunk - merge) * MR_K;
+                const int64_t j1 = j0 + MR_K < T + 2 ? j0 + MR_K : T + 2;
+                for (int64_t j = j0; j < j1; ++j) {
+                    if (j == 0) bs[0] = 0;
+                    else if (j > n) bs[j] = static_cast<int32_t>(T);
+                }
+            } else if (chunk * MR_K < M) {
+                d = chunk * MR_K;
+                // co-rank: the largest i (reads among the first d merged) with R[i-1] <= W[d-i]
+                int64_t lo = d - n > 0 ? d - n : 0, hi = d < T ? d : T;
+                while (lo < hi) {
+                    const int64_t mid = (lo + hi + 1) >> 1;
+                    const int64_t j = d - mid;
+                    if (j >= n || R[mid - 1] <= W[j]) lo = mid;
+                    else hi = mid - 1;
+                }
+                int64_t i = lo, j = d - lo;
+                const int64_t b = s / C, c = s - b * C;
+                const int64_t dend = d + MR_K < M ? d + MR_K : M;
+                cnt = static_cast<int>(dend - d);
+                for (int64_t x = d; x < dend; ++x) {
+                    const int o = lane * MR_K + static_cast<int>(x - d);
+                    if (i < T && (j >= n || R[i] <= W[j])) {
+                        const KeyT q = R[i];
+                        const int64_t r = (b * T + static_cast<int64_t>(q & tmask)) * C + c;
+                        rridx[s * T + i] = static_cast<int32_t>(j - 1);
+                        ridx[r] = static_cast<int32_t>(j - 1);
+                        sk[warp][o] = q;
+                        // bit 1: the latest earlier write is of the read's own address (the sum lookup's mask)
+                        sr[warp][o] = (j > 0 && (W[j - 1] >> tbits) == (q >> tbits)) ? 2 : 0;
+                        ++i;
+                    } else {
+                        bs[j + 1] = static_cast<int32_t>(i);
+                        sk[warp][o] = W[j];
+                        sr[warp][o] = 1;
+                        ++j;
+                    }
+                }
             }
-            continue;
         }
-        const int64_t d = chunk * MR_K;
-        if (d >= M) continue;
-        // co-rank: the largest i (reads among the first d merged) with R[i-1] <= W[d-i]
-        int64_t lo = d - n > 0 ? d - n : 0, hi = d < T ? d : T;
-        while (lo < hi) {
-            const int64_t mid = (lo + hi + 1) >> 1;
-            const int64_t j = d - mid;
-            if (j >= n || R[mid - 1] <= W[j]) lo = mid;
-            else hi = mid - 1;
-        }
-        int64_t i = lo, j = d - lo;
-        const int64_t b = s / C, c = s - b * C;
-        const int64_t dend = d + MR_K < M ? d + MR_K : M;
-        for (int64_t x = d; x < dend; ++x) {
-            if (i < T && (j >= n || R[i] <= W[j])) {
-                const KeyT q = R[i];
-                rridx[s * T + i] = static_cast<int32_t>(j - 1);
-                ridx[(b * T + static_cast<int64_t>(q & tmask)) * C + c] = static_cast<int32_t>(j - 1);
-                ++i;
-            } else {
-                bs[j + 1] = static_cast<int32_t>(i);
-                ++j;
+        __syncwarp();
+        // staged position q belongs to lane q / MR_K, MR_K of them per lane
+#pragma unroll 4
+        for (int k = 0; k < MR_K; ++k) {
+            const int q = k * 32 + lane, owner = q / MR_K, off = q % MR_K;
+            const int oc = __shfl_sync(0xffffffffu, cnt, owner);
+            const int64_t os = __shfl_sync(0xffffffffu, s, owner);
+            const int64_t od = __shfl_sync(0xffffffffu, d, owner);
+            if (off < oc) {
+                mkeys[os * 2 * T + od + off] = sk[warp][q];
+                mrole[os * 2 * T + od + off] = sr[warp][q];
             }
         }
+        __syncwarp();
     }
 }
 
