@@ -1268,7 +1268,7 @@ def run_model(dev, rank: int, world: int, steps: int = 8, warmup: int = 3) -> di
             ops = [t for _name, t in L.timing_stop()] if impl != "stock" else []
             ms = max_over_ranks(t0.elapsed_time(t1) / steps, world)
             ent = {"ms_per_step": ms, "value": B * T * world / (ms * 1e-3), "unit": "tokens/s",
-                   "loss": float(loss)}
+                   "loss": float(loss.detach())}
             if ops:
                 op_ms = sum(ops) / steps
                 ent["operator_ms_per_step"] = op_ms
