@@ -72,7 +72,7 @@ def parse():
     ap.add_argument("--batch", type=int, default=None, help="override B per GPU (small profiling cases)")
     ap.add_argument("--ops", choices=["all", "lk", "ss"], default="all",
                     help="ops in a step (profiling a single op; the benchmark runs all)")
-    ap.add_argument("--only", choices=["fused_read", "decode", "config1", "config5_op", "model"], default=None,
+    ap.add_argument("--only", choices=["fused_read", "decode", "config1", "config5_op", "general", "model"], default=None,
                     help="run one side measurement alone and print its JSON (profiling)")
     return ap.parse_args()
 
@@ -448,6 +448,8 @@ def main():
     if args.only is not None:
         dev = torch.device("cuda", local)
         fn = {"fused_read": run_fused_read, "decode": run_decode, "config1": run_cfg1, "config5_op": run_cfg5_op,
+              "general": lambda d: run_general(cfg, make_inputs(cfg, seed=1000 + cfg.cfg, device=d), d, world,
+                                               steps=args.steps),
               "model": lambda d: run_model(d, rank, world)}[args.only]
         res = fn(dev)
         if rank == 0:
