@@ -498,6 +498,117 @@ __global__ void __launch_bounds__(256) k_lk_bwd_gather(LkArgs a, const KeyT* rke
     }
 }
 
+// The same backward over chunks of the write tape: a CTA owns P consecutive
+// sorted writes of one stream and first stages, with coalesced loads, their
+// keys and the k after them, their bucket starts, and -- when the run of the
+// read tape their buckets cover holds at most rcap reads -- those reads' keys
+// and latest writes.  Each lane group then sums one write's gradient rows as
+// k_lk_bwd_gather does, with no dependent global load before the gradient
+// gathers (a chunk with a longer read run reads its read keys from global
+// memory).  Same sums in the same order as k_lk_bwd_gather.
+template <typename KeyT, int DT, int VB>
+__global__ void __launch_bounds__(256) k_lk_bwd_chunk(LkArgs a, const KeyT* rkeys, const int32_t* rridx,
+                                                      const int32_t* bstart, int lshift, int rcap) {
+    using E = Elem<DT>;
+    using Acc = typename E::Acc;
+    using V = typename E::T;
+    constexpr int EPV = VB / static_cast<int>(sizeof(V));
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int P = a.P, k = static_cast<int>(a.k);
+    const int64_t T = a.T, D = a.D;
+    const int64_t s = blockIdx.x / a.nchunks;
+    const int64_t q0 = (blockIdx.x % a.nchunks) * P;
+    const int np = static_cast<int>((T - q0) < P ? (T - q0) : P);
+    const int64_t n_s = a.nvalid ? a.nvalid[s] : T;
+    KeyT* sk = reinterpret_cast<KeyT*>(smem);                              // [P + k] keys q0 ..
+    int32_t* sb = reinterpret_cast<int32_t*>(sk + P + k);                  // [P + k + 1] bstart[q0 + 1 + m]
+    KeyT* srk = reinterpret_cast<KeyT*>(sb + ((P + k + 2) & ~1));          // [rcap] read keys of the run
+    int32_t* srr = reinterpret_cast<int32_t*>(srk + rcap);                 // [rcap] their latest writes
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const KeyT* wk = static_cast<const KeyT*>(a.keys) + s * T;
+    const int32_t* bs = bstart + s * (T + 2);
+    const KeyT* rk = rkeys + s * T;
+    const int32_t* rr = rridx + s * T;
+    for (int m = tid; m < np + k; m += 256) sk[m] = q0 + m < T ? wk[q0 + m] : KeyT(0);
+    for (int m = tid; m <= np + k; m += 256) {
+        const int64_t idx = q0 + 1 + m;
+        sb[m] = bs[idx < T + 1 ? idx : T + 1];
+    }
+    __syncthreads();
+    const int32_t ilo = sb[0], ihi = sb[np - 1 + k];  // the reads whose latest write is q0 .. q0+np-1+k-1
+    const bool staged = ihi - ilo <= rcap;
+    if (staged) {
+        for (int e = tid; e < ihi - ilo; e += 256) {
+            srk[e] = rk[ilo + e];
+            srr[e] = rr[ilo + e];
+        }
+    }
+    __syncthreads();
+    const uint32_t L = 1u << lshift;
+    const uint32_t grp = static_cast<uint32_t>(lane) >> lshift, lig = static_cast<uint32_t>(lane) & (L - 1);
+    const int gpb = 8 * (32 >> lshift);
+    const KeyT tmask = (static_cast<KeyT>(1) << a.tbits) - 1;
+    const V* grad = static_cast<const V*>(a.grad);
+    V* out = static_cast<V*>(a.out);
+    const RowMap rows_of(s, T, a.C);
+    for (int qq = warp * (32 >> lshift) + static_cast<int>(grp); qq < np; qq += gpb) {
+        const int64_t q = q0 + qq;
+        const KeyT kq = sk[qq];
+        const uint64_t orow = static_cast<uint64_t>(rows_of(kq & tmask));
+        Acc acc[EPV];
+#pragma unroll
+        for (int e = 0; e < EPV; ++e) acc[e] = Acc(0);
+        if (a.accumulate) {
+            const uint4 prev = ld_vec<VB>(out + orow * D + lig * EPV);
+            const V* pv0 = reinterpret_cast<const V*>(&prev);
+#pragma unroll
+            for (int e = 0; e < EPV; ++e) acc[e] = E::to_acc(pv0[e]);
+        }
+        if (q < n_s) {
+            // slots j < jmax keep write q+j in q's segment
+            const KeyT aq = kq >> a.tbits;
+            int jmax = 0;
+            while (jmax < k && q + jmax < n_s && (sk[qq + jmax] >> a.tbits) == aq) ++jmax;
+            const int32_t i0 = sb[qq], i1 = sb[qq + jmax];
+            for (int32_t i = i0; i < i1; i += 4) {
+                uint32_t rrow[4];
+                int jj[4];
+                bool use[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const bool in = i + u < i1;
+                    const KeyT key = !in ? KeyT(0) : (staged ? srk[i + u - ilo] : rk[i + u]);
+                    const int32_t rank = !in ? 0 : (staged ? srr[i + u - ilo] : rr[i + u]);
+                    rrow[u] = rows_of(key & tmask);
+                    jj[u] = static_cast<int>(rank - q);
+                    use[u] = in && (key >> a.tbits) == aq;
+                }
+                uint4 x[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    x[u] = use[u] ? ldg_vec<VB>(grad + (static_cast<uint64_t>(rrow[u]) * k + jj[u]) * D + lig * EPV)
+                                  : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const V* xv = reinterpret_cast<const V*>(&x[u]);
+#pragma unroll
+                    for (int e = 0; e < EPV; ++e) acc[e] += E::to_acc(xv[e]);
+                }
+            }
+        }
+        uint4 o = make_uint4(0u, 0u, 0u, 0u);
+        V* ov = reinterpret_cast<V*>(&o);
+#pragma unroll
+        for (int e = 0; e < EPV; ++e) ov[e] = E::from_acc(acc[e]);
+        st_vec<VB>(out + orow * D + lig * EPV, o);
+    }
+}
+
+inline size_t lk_bwd_chunk_smem(int P, int64_t k, int rcap, size_t key_bytes) {
+    return (static_cast<size_t>(P) + static_cast<size_t>(k)) * key_bytes +
+           (static_cast<size_t>(P) + static_cast<size_t>(k) + 2) * 4 + static_cast<size_t>(rcap) * (key_bytes + 4) + 16;
+}
+
 // Convert a float accumulator [n] to the payload dtype (added to `out` when accumulating).
 template <int DT>
 __global__ void k_acc_to_dtype(const float* __restrict__ acc, typename Elem<DT>::T* __restrict__ out, int64_t n,

@@ -491,8 +491,9 @@ int tape_build_src(const AddrSrc& wsrc, const AddrSrc& rsrc, int32_t* raddr_out,
         ra.nvalid = nullptr;
         ra.mbit = 0;
         if (int e = sort_streams<KeyT>(a, tv.keys, &ra, tv.rkeys, other, S, T, st)) return e;
-        const int64_t per = mr_chunks(T);
-        k_merge_ranks<KeyT><<<grid_cap((S * per + 255) / 256), 256, 0, st>>>(
+        const int64_t mgrid = S * mr_tiles(T, MergeTile<KeyT>::TILE) + S * mr_tail_blocks(T);
+        if (mgrid > 2147483647LL) return RAVEL_ERR_UNSUPPORTED;
+        k_merge_ranks<KeyT><<<static_cast<unsigned>(mgrid), 256, 0, st>>>(
             static_cast<const KeyT*>(tv.keys), tv.nvalid, static_cast<const KeyT*>(tv.rkeys), S, T, C,
             tl.kl.tbits, tv.rridx, tv.ridx, tv.bstart, tv.soff, static_cast<KeyT*>(tv.mkeys), tv.mrole);
         return check_launch();
@@ -594,6 +595,11 @@ int lk_fwd_tape(const void* tape, int flags, const void* raddr, int addr_dtype, 
     });
 }
 
+// Build-time knob: 0 keeps the general latest-k backward on the per-write gather (k_lk_bwd_gather).
+#ifndef RAVEL_LK_BWD_CHUNK
+#define RAVEL_LK_BWD_CHUNK 1
+#endif
+
 int lk_bwd(const void* tape, int flags, const void* raddr, int addr_dtype, const void* grad_vals, int dtype,
            int64_t B, int64_t T, int64_t C, int64_t D, int64_t A, int64_t k, void* grad_payload, void* scratch,
            size_t scratch_bytes, cudaStream_t st, int accumulate = 0) {
@@ -654,6 +660,16 @@ int lk_bwd(const void* tape, int flags, const void* raddr, int addr_dtype, const
                         constexpr int VB = decltype(vbc)::value;
                         if constexpr (!vb_ok<DT, VB>()) {
                             return RAVEL_ERR_INVALID_ARG;
+                        } else if (RAVEL_LK_BWD_CHUNK && k <= 64) {
+                            // chunks of the write tape with their keys, bucket starts and read run staged
+                            constexpr int kRcap = 1024;
+                            a.P = 4 * 8 * (32 >> lsh);
+                            a.nchunks = (T + a.P - 1) / a.P;
+                            const size_t smem = lk_bwd_chunk_smem(a.P, k, kRcap, sizeof(KeyT));
+                            if (int e = set_smem(k_lk_bwd_chunk<KeyT, DT, VB>, smem)) return e;
+                            k_lk_bwd_chunk<KeyT, DT, VB><<<static_cast<unsigned>(B * C * a.nchunks), 256, smem, st>>>(
+                                a, static_cast<const KeyT*>(tv.rkeys), tv.rridx, tv.bstart, lsh, kRcap);
+                            return check_launch();
                         } else {
                             k_lk_bwd_gather<KeyT, DT, VB><<<grid_cap((warps * 32 + 255) / 256), 256, 0, st>>>(
                                 a, static_cast<const KeyT*>(tv.rkeys), tv.rridx, tv.bstart, lsh);

@@ -412,100 +412,126 @@ __device__ void stream_offsets_block(const int* __restrict__ nvalid, int64_t* __
 // of equal key.  A read's rank is then the number of writes merged before it,
 // minus one (searchsorted(right=True)-1 of ravel_memory.py:159, restricted to
 // the stream: the latest valid write strictly below it), and bstart[j + 1] for
-// write j is the number of reads merged before it.  Each thread merges MR_K
-// consecutive elements of the merged order from its merge-path co-rank (a binary
-// search on its diagonal); bstart[0] = 0 and bstart[n + 1 .. T + 1] = T, the
-// latter spread over MR_K-entry tail chunks so a heavy write mask (n << T) does
-// not leave one thread storing T entries.  Block 0 first writes the stream
-// offsets (stream_offsets_block), which this launch's merges do not read.  The
-// merged order itself is kept (mkeys, and mrole: bit 0 a write, bit 1 a read
-// whose latest earlier write has its address) for the sum lookup's scans.
-constexpr int MR_K = 16;
-// chunks per stream: the longest merge (2T elements), then the T + 2 bstart entries
-__host__ __device__ inline int64_t mr_merge_chunks(int64_t T) { return (2 * T + MR_K - 1) / MR_K; }
-__host__ __device__ inline int64_t mr_chunks(int64_t T) { return mr_merge_chunks(T) + (T + 2 + MR_K - 1) / MR_K; }
+// write j is the number of reads merged before it.
+//
+// Merge path in two levels: a CTA owns MergeTile::TILE consecutive positions of
+// one stream's merged order; two threads find the tile's co-ranks on its two
+// diagonals (binary searches in global memory), the CTA loads the tile's reads
+// and writes (plus the write before them) into shared memory with coalesced
+// loads, and each thread finds its own co-rank in shared memory and merges
+// MergeTile::E positions from there.  The merged order itself is staged and
+// stored in coalesced runs (mkeys, and mrole: bit 0 a write, bit 1 a read whose
+// latest earlier write has its address) for the sum lookup's scans.  CTAs past
+// the tiles fill bstart[0] = 0 and bstart[n + 1 .. T + 1] = T, 4 entries a
+// thread, so a heavy write mask (n << T) leaves no thread with T stores.  CTA 0
+// first writes the stream offsets (stream_offsets_block), which this launch's
+// merges do not read.
+template <typename KeyT> struct MergeTile {
+    static constexpr int E = sizeof(KeyT) == 4 ? 8 : 4;  // merged positions per thread
+    static constexpr int TILE = 256 * E;                  // per CTA (static shared memory < 48 KB)
+};
+constexpr int MR_TAIL = 1024;  // bstart entries per tail CTA
+__host__ __device__ inline int64_t mr_tiles(int64_t T, int tile) { return (2 * T + tile - 1) / tile; }
+__host__ __device__ inline int64_t mr_tail_blocks(int64_t T) { return (T + 2 + MR_TAIL - 1) / MR_TAIL; }
+
 template <typename KeyT>
 __global__ void __launch_bounds__(256) k_merge_ranks(const KeyT* wkeys, const int* nvalid, const KeyT* rkeys,
                                                    int64_t S, int64_t T, int64_t C, int tbits, int32_t* rridx,
                                                    int32_t* ridx, int32_t* bstart, int64_t* soff, KeyT* mkeys,
                                                    uint8_t* mrole) {
-    // the merged keys and roles a warp produces (32 chunks of MR_K positions), staged so
-    // that they leave in runs of 32 consecutive positions instead of one per lane
-    __shared__ KeyT sk[8][32 * MR_K];
-    __shared__ uint8_t sr[8][32 * MR_K];
+    constexpr int E = MergeTile<KeyT>::E, TILE = MergeTile<KeyT>::TILE;
+    __shared__ KeyT sR[TILE];      // the tile's reads
+    __shared__ KeyT sW[TILE + 1];  // the write before the tile's writes, then its writes
+    __shared__ KeyT sk[TILE];      // merged keys of the tile
+    __shared__ uint8_t sr[TILE];   // their roles
+    __shared__ int64_t s_co[2];
     if (blockIdx.x == 0) stream_offsets_block(nvalid, soff, S, T);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const KeyT tmask = (static_cast<KeyT>(1) << tbits) - 1;
-    const int64_t per = mr_chunks(T), merge = mr_merge_chunks(T), total = S * per;
-    // whole warps iterate together (the staging below is warp-wide)
-    for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + warp * 32; base < total;
-         base += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t e = base + lane;
-        int64_t s = 0, d = 0;
-        int cnt = 0;  // merged positions [d, d + cnt) of stream s staged by this lane
-        if (e < total) {
-            s = e / per;
-            const int64_t chunk = e - s * per;
-            const int64_t n = nvalid ? nvalid[s] : T;
-            const KeyT* W = wkeys + s * T;
-            const KeyT* R = rkeys + s * T;
-            int32_t* bs = bstart + s * (T + 2);
-            const int64_t M = n + T;
-            if (chunk >= merge) {  // bstart[0] and the entries past the last valid write
-                const int64_t j0 = (chunk - merge) * MR_K;
-                const int64_t j1 = j0 + MR_K < T + 2 ? j0 + MR_K : T + 2;
-                for (int64_t j = j0; j < j1; ++j) {
-                    if (j == 0) bs[0] = 0;
-                    else if (j > n) bs[j] = static_cast<int32_t>(T);
-                }
-            } else if (chunk * MR_K < M) {
-                d = chunk * MR_K;
-                // co-rank: the largest i (reads among the first d merged) with R[i-1] <= W[d-i]
-                int64_t lo = d - n > 0 ? d - n : 0, hi = d < T ? d : T;
-                while (lo < hi) {
-                    const int64_t mid = (lo + hi + 1) >> 1;
-                    const int64_t j = d - mid;
-                    if (j >= n || R[mid - 1] <= W[j]) lo = mid;
-                    else hi = mid - 1;
-                }
-                int64_t i = lo, j = d - lo;
-                const int64_t b = s / C, c = s - b * C;
-                const int64_t dend = d + MR_K < M ? d + MR_K : M;
-                cnt = static_cast<int>(dend - d);
-                for (int64_t x = d; x < dend; ++x) {
-                    const int o = lane * MR_K + static_cast<int>(x - d);
-                    if (i < T && (j >= n || R[i] <= W[j])) {
-                        const KeyT q = R[i];
-                        const int64_t r = (b * T + static_cast<int64_t>(q & tmask)) * C + c;
-                        rridx[s * T + i] = static_cast<int32_t>(j - 1);
-                        ridx[r] = static_cast<int32_t>(j - 1);
-                        sk[warp][o] = q;
-                        // bit 1: the latest earlier write is of the read's own address (the sum lookup's mask)
-                        sr[warp][o] = (j > 0 && (W[j - 1] >> tbits) == (q >> tbits)) ? 2 : 0;
-                        ++i;
-                    } else {
-                        bs[j + 1] = static_cast<int32_t>(i);
-                        sk[warp][o] = W[j];
-                        sr[warp][o] = 1;
-                        ++j;
-                    }
-                }
+    const int tid = threadIdx.x;
+    const int64_t tiles = mr_tiles(T, TILE);
+    const int64_t bid = blockIdx.x;
+    if (bid >= S * tiles) {  // bstart[0] and the entries past the last valid write
+        const int64_t b2 = bid - S * tiles, tb = mr_tail_blocks(T);
+        const int64_t s = b2 / tb, jb = (b2 - s * tb) * MR_TAIL;
+        if (s >= S) return;
+        const int64_t n = nvalid ? nvalid[s] : T;
+        int32_t* bs = bstart + s * (T + 2);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t j = jb + tid * 4 + u;
+            if (j > T + 1) break;
+            if (j == 0) bs[0] = 0;
+            else if (j > n) bs[j] = static_cast<int32_t>(T);
+        }
+        return;
+    }
+    const int64_t s = bid / tiles, tile = bid - s * tiles;
+    const int64_t n = nvalid ? nvalid[s] : T;
+    const int64_t M = n + T;
+    const int64_t d0 = tile * TILE;
+    if (d0 >= M) return;
+    const int64_t d1 = d0 + TILE < M ? d0 + TILE : M;
+    const KeyT* W = wkeys + s * T;
+    const KeyT* R = rkeys + s * T;
+    if (tid < 2) {
+        // co-rank: the largest i (reads among the first d merged) with R[i-1] <= W[d-i]
+        const int64_t d = tid ? d1 : d0;
+        int64_t lo = d - n > 0 ? d - n : 0, hi = d < T ? d : T;
+        while (lo < hi) {
+            const int64_t mid = (lo + hi + 1) >> 1;
+            const int64_t j = d - mid;
+            if (j >= n || R[mid - 1] <= W[j]) lo = mid;
+            else hi = mid - 1;
+        }
+        s_co[tid] = lo;
+    }
+    __syncthreads();
+    const int64_t i0 = s_co[0], j0 = d0 - i0;
+    const int nr = static_cast<int>(s_co[1] - i0), nw = static_cast<int>((d1 - s_co[1]) - j0);
+    for (int e = tid; e < nr; e += 256) sR[e] = R[i0 + e];
+    for (int e = tid; e <= nw; e += 256) sW[e] = (e > 0 || j0 > 0) ? W[j0 - 1 + e] : KeyT(0);
+    __syncthreads();
+    const int len = static_cast<int>(d1 - d0);
+    const int e0 = tid * E;
+    if (e0 < len) {
+        // this thread's co-rank inside the tile (a write past the tile's writes counts as +inf:
+        // every read of the tile precedes it)
+        int lo = e0 - nw > 0 ? e0 - nw : 0, hi = e0 < nr ? e0 : nr;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            const int jr = e0 - mid;
+            if (jr >= nw || sR[mid - 1] <= sW[1 + jr]) lo = mid;
+            else hi = mid - 1;
+        }
+        int i = lo, jr = e0 - lo;
+        const int e1 = e0 + E < len ? e0 + E : len;
+        const KeyT tmask = (static_cast<KeyT>(1) << tbits) - 1;
+        const int64_t b = s / C, c = s - b * C;
+        int32_t* bs = bstart + s * (T + 2);
+        for (int e = e0; e < e1; ++e) {
+            const int64_t jg = j0 + jr;
+            if (i < nr && (jr >= nw || sR[i] <= sW[1 + jr])) {
+                const KeyT q = sR[i];
+                const int64_t ig = i0 + i;
+                rridx[s * T + ig] = static_cast<int32_t>(jg - 1);
+                ridx[(b * T + static_cast<int64_t>(q & tmask)) * C + c] = static_cast<int32_t>(jg - 1);
+                sk[e] = q;
+                // bit 1: the latest earlier write is of the read's own address (the sum lookup's mask)
+                sr[e] = (jg > 0 && (sW[jr] >> tbits) == (q >> tbits)) ? 2 : 0;
+                ++i;
+            } else {
+                bs[jg + 1] = static_cast<int32_t>(i0 + i);
+                sk[e] = sW[1 + jr];
+                sr[e] = 1;
+                ++jr;
             }
         }
-        __syncwarp();
-        // staged position q belongs to lane q / MR_K, MR_K of them per lane
-#pragma unroll 4
-        for (int k = 0; k < MR_K; ++k) {
-            const int q = k * 32 + lane, owner = q / MR_K, off = q % MR_K;
-            const int oc = __shfl_sync(0xffffffffu, cnt, owner);
-            const int64_t os = __shfl_sync(0xffffffffu, s, owner);
-            const int64_t od = __shfl_sync(0xffffffffu, d, owner);
-            if (off < oc) {
-                mkeys[os * 2 * T + od + off] = sk[warp][q];
-                mrole[os * 2 * T + od + off] = sr[warp][q];
-            }
-        }
-        __syncwarp();
+    }
+    __syncthreads();
+    KeyT* mk = mkeys + s * 2 * T + d0;
+    uint8_t* mr = mrole + s * 2 * T + d0;
+    for (int e = tid; e < len; e += 256) {
+        mk[e] = sk[e];
+        mr[e] = sr[e];
     }
 }
 
