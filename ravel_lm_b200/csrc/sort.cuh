@@ -472,17 +472,31 @@ __global__ void __launch_bounds__(256) k_merge_ranks(const KeyT* wkeys, const in
     const int64_t d1 = d0 + TILE < M ? d0 + TILE : M;
     const KeyT* W = wkeys + s * T;
     const KeyT* R = rkeys + s * T;
-    if (tid < 2) {
+    if (tid < 64) {
         // co-rank: the largest i (reads among the first d merged) with R[i-1] <= W[d-i]
-        const int64_t d = tid ? d1 : d0;
+        // (true for every i up to it, false after), warp 0 for d0 and warp 1 for d1, each
+        // lane probing one of 32 points of the remaining interval per round
+        const int lane = tid & 31;
+        const int64_t d = tid < 32 ? d0 : d1;
         int64_t lo = d - n > 0 ? d - n : 0, hi = d < T ? d : T;
         while (lo < hi) {
-            const int64_t mid = (lo + hi + 1) >> 1;
+            const int64_t span = hi - lo;
+            const int64_t step = (span + 31) / 32;
+            const int64_t mid = lo + (lane + 1) * step < hi ? lo + (lane + 1) * step : hi;
             const int64_t j = d - mid;
-            if (j >= n || R[mid - 1] <= W[j]) lo = mid;
-            else hi = mid - 1;
+            const bool ok = j >= n || R[mid - 1] <= W[j];
+            const unsigned yes = __ballot_sync(0xffffffffu, ok);
+            const unsigned no = __ballot_sync(0xffffffffu, !ok);
+            // probes rise with the lane: the last true one and the first false one bound the answer
+            const int lt = yes ? 31 - __clz(yes) : -1;
+            const int lf = no ? __ffs(no) - 1 : 32;
+            const int64_t nlo = lt >= 0 ? (lo + (lt + 1) * step < hi ? lo + (lt + 1) * step : hi) : lo;
+            const int64_t nhi = lf < 32 ? (lo + (lf + 1) * step < hi ? lo + (lf + 1) * step : hi) - 1 : hi;
+            lo = nlo;
+            hi = nhi;
+            if (step == 1) break;
         }
-        s_co[tid] = lo;
+        if (lane == 0) s_co[tid >> 5] = lo;
     }
     __syncthreads();
     const int64_t i0 = s_co[0], j0 = d0 - i0;
