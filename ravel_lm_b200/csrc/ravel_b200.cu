@@ -192,6 +192,13 @@ RangePlan range_plan(int64_t S, int64_t T, int64_t slots, int64_t rl_max = int64
 #ifndef RAVEL_RS_RLMIN
 #define RAVEL_RS_RLMIN 16
 #endif
+// Blocks per SM for short streams (their ranges shrink down to RAVEL_RS_RLMIN
+// positions).  Measured at config 5's merged sum scans (2048 positions per
+// stream, us forward / backward): 2 blocks 27.9 / 28.2, 4 blocks 24.3 / 23.7,
+// 8 blocks (16-position ranges) 21.7 / 22.1.
+#ifndef RAVEL_RS_SHORT_BPS
+#define RAVEL_RS_SHORT_BPS 8
+#endif
 static_assert(RAVEL_RS_RLMIN >= 16 && RAVEL_RS_RLMIN <= 64 && RAVEL_RS_RLMIN % 8 == 0, "range length floor");
 int64_t max_ranges(int64_t T) { return T > 0 ? (T + RAVEL_RS_RLMIN - 1) / RAVEL_RS_RLMIN : 1; }
 // Build-time knob: rows of at least this many 16-byte vectors give each lane of the
@@ -782,12 +789,13 @@ int launch_segscan(const TapeView& tv, const TapeLayout& tl, int64_t B, int64_t 
             if (int e = set_smem(kern, smem_max)) return e;
             const int occ = occupancy(kern, GS_WARPS * 32, range_scan_smem(VPL, gpb, D, sizeof(Acc), 2));
             // one range per lane group; whole blocks per stream, RAVEL_RS_WAVES waves of blocks
-            // Short streams (64-position ranges do not fill one wave): about two
-            // blocks per SM, ranges down to RAVEL_RS_RLMIN positions.
+            // Short streams (64-position ranges do not fill one wave): about
+            // RAVEL_RS_SHORT_BPS blocks per SM, ranges down to RAVEL_RS_RLMIN positions.
             const int64_t S = B * C > 0 ? B * C : 1;
             const int64_t blocks64 = S * (((Tm + 63) / 64 + gpb - 1) / gpb);
             const bool short_streams = blocks64 < static_cast<int64_t>(occ) * sm_count();
-            int64_t bps = short_streams ? 2 * sm_count() / S : static_cast<int64_t>(occ) * sm_count() * RAVEL_RS_WAVES / S;
+            int64_t bps = short_streams ? RAVEL_RS_SHORT_BPS * sm_count() / S
+                                        : static_cast<int64_t>(occ) * sm_count() * RAVEL_RS_WAVES / S;
             if (bps < 1) bps = 1;
             const RangePlan rp = range_plan(1, Tm, bps * gpb, kRlMax, short_streams ? RAVEL_RS_RLMIN : 64);
             ga.R = rp.R;
