@@ -86,17 +86,29 @@ TapeView tape_view(const void* tape, const TapeLayout& t) {
 // tile sort configuration for a stream length T
 struct SortPlan {
     int threads;
+    int items;  // keys per thread
     int64_t tiles;
     int merge_passes;
 };
 
+// Build-time knob: keys per thread of the tile sort for streams that fit one CTA at
+// that count (8 otherwise; more threads with fewer keys each shorten the ranking).
+// Measured at config 5 (T = 1024, writes and reads in one launch; step replayed
+// from a CUDA graph, ms): 8 keys 0.0726, 4 keys 0.0686, 2 keys 0.0685.
+#ifndef RAVEL_SORT_SHORT_ITEMS
+#define RAVEL_SORT_SHORT_ITEMS 4
+#endif
+static_assert(RAVEL_SORT_SHORT_ITEMS == 2 || RAVEL_SORT_SHORT_ITEMS == 4 || RAVEL_SORT_SHORT_ITEMS == 8,
+              "keys per thread");
+
 SortPlan sort_plan(int64_t T) {
     SortPlan p;
     const int64_t tile_cap = 8192;
+    p.items = T <= 1024 * RAVEL_SORT_SHORT_ITEMS ? RAVEL_SORT_SHORT_ITEMS : 8;
     int threads = 32;
-    while (threads < 1024 && static_cast<int64_t>(threads) * 8 < T) threads *= 2;
+    while (threads < 1024 && static_cast<int64_t>(threads) * p.items < T) threads *= 2;
     p.threads = threads;
-    const int64_t tile = static_cast<int64_t>(threads) * 8;
+    const int64_t tile = static_cast<int64_t>(threads) * p.items;
     p.tiles = T <= tile ? 1 : (T + tile_cap - 1) / tile_cap;
     p.merge_passes = 0;
     while ((int64_t(1) << p.merge_passes) < p.tiles) ++p.merge_passes;
@@ -423,22 +435,27 @@ int sort_streams(const SortArgs& a0, void* out0, const SortArgs* a1, void* out1,
     p.a[0].keys_out = first;
     p.first = S * sp.tiles;
     const int64_t grid = nsort * S * sp.tiles;
-    auto launch = [&](auto th) -> int {
+    auto launch = [&](auto th, auto it) -> int {
         constexpr int TH = decltype(th)::value;
-        const size_t smem = tile_sort_smem<TH, 8, KeyT>();
-        if (int e = set_smem(k_tile_sort<KeyT, TH, 8>, smem)) return e;
-        k_tile_sort<KeyT, TH, 8><<<static_cast<unsigned>(grid), TH, smem, st>>>(p);
+        constexpr int IT = decltype(it)::value;
+        const size_t smem = tile_sort_smem<TH, IT, KeyT>();
+        if (int e = set_smem(k_tile_sort<KeyT, TH, IT>, smem)) return e;
+        k_tile_sort<KeyT, TH, IT><<<static_cast<unsigned>(grid), TH, smem, st>>>(p);
         return check_launch();
     };
+    auto by_threads = [&](auto it) -> int {
+        switch (sp.threads) {
+            case 32: return launch(IC<32>{}, it);
+            case 64: return launch(IC<64>{}, it);
+            case 128: return launch(IC<128>{}, it);
+            case 256: return launch(IC<256>{}, it);
+            case 512: return launch(IC<512>{}, it);
+            default: return launch(IC<1024>{}, it);
+        }
+    };
     int e = RAVEL_OK;
-    switch (sp.threads) {
-        case 32: e = launch(IC<32>{}); break;
-        case 64: e = launch(IC<64>{}); break;
-        case 128: e = launch(IC<128>{}); break;
-        case 256: e = launch(IC<256>{}); break;
-        case 512: e = launch(IC<512>{}); break;
-        default: e = launch(IC<1024>{}); break;
-    }
+    if (RAVEL_SORT_SHORT_ITEMS != 8 && sp.items == RAVEL_SORT_SHORT_ITEMS) e = by_threads(IC<RAVEL_SORT_SHORT_ITEMS>{});
+    else e = by_threads(IC<8>{});
     if (e) return e;
     const KeyT* src = static_cast<const KeyT*>(first);
     int64_t run = static_cast<int64_t>(sp.threads) * 8;
