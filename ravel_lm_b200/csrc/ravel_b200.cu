@@ -563,6 +563,14 @@ LkArgs lk_args(const TapeView& tv, const TapeLayout& tl, const void* raddr, int 
     return a;
 }
 
+// Build-time knob: (read, slot) pairs per CTA of the general latest-k forward (at most 512).
+// Measured (us, general forward at config 5 / config 3 with independent reads): 512 pairs
+// 14.7 / 535, 256 pairs 13.9 / 562, 128 pairs 13.5 / 650.
+#ifndef RAVEL_LK_GEN_SLOTS
+#define RAVEL_LK_GEN_SLOTS 512
+#endif
+static_assert(RAVEL_LK_GEN_SLOTS >= 1 && RAVEL_LK_GEN_SLOTS <= 512, "the kernel's slot arrays hold 512");
+
 int lk_fwd_tape(const void* tape, int flags, const void* raddr, int addr_dtype, const void* payload, int dtype,
                 int64_t B, int64_t T, int64_t C, int64_t D, int64_t A, int64_t k, void* out_vals,
                 uint8_t* out_mask, cudaStream_t st) {
@@ -609,7 +617,7 @@ int lk_fwd_tape(const void* tape, int flags, const void* raddr, int addr_dtype, 
                         if (int e = set_smem(k_lk_fwd_fast<KeyT, DT, VB>, smem)) return e;
                         k_lk_fwd_fast<KeyT, DT, VB><<<static_cast<unsigned>(S * a.nchunks), 256, smem, st>>>(a);
                     } else {
-                        const int64_t rpc = 512 / k;
+                        const int64_t rpc = (RAVEL_LK_GEN_SLOTS / k) > 0 ? RAVEL_LK_GEN_SLOTS / k : 1;
                         k_lk_fwd_general<KeyT, DT, VB><<<static_cast<unsigned>((N + rpc - 1) / rpc), 256, 0, st>>>(a, rpc);
                     }
                     return check_launch();
