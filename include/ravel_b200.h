@@ -112,10 +112,9 @@ int ravel_latestk_fwd(const void* waddr, const void* raddr, int addr_dtype, cons
  * Gradient of the latest-k values w.r.t. payloads (the autograd of
  * index_select + mask multiply at ravel_lm/ravel_memory.py:173-175):
  * grad_payload[src] = sum of grad_vals over the valid slots that read src.
- * grad_payload [B,T,C,D] is fully overwritten.  Deterministic (a gather, no
- * atomics) whenever a payload row is 2^m <= 32 vectors of 16 bytes (any D for
- * aliased reads without a mask); float atomics for other rows of general or
- * masked tapes.
+ * grad_payload [B,T,C,D] is fully overwritten.  Deterministic for every row
+ * shape: a gather, no atomics (one lane per 16-byte vector when a row is 2^m
+ * <= 32 vectors, else one warp per write over the row's elements).
  */
 int ravel_latestk_bwd(const void* tape, int tape_flags, const void* raddr, int addr_dtype,
                       const void* grad_vals, int dtype, int64_t B, int64_t T, int64_t C, int64_t D,

@@ -342,67 +342,6 @@ __global__ void __launch_bounds__(256) k_lk_fwd_general(LkArgs a, int64_t reads_
     }
 }
 
-// ------------------------------------------------------------------ general backward
-// atomicAdd of grad_vals into an accumulator [N, D] (float, or double for
-// float64); the accumulator is the output itself for float32 / float64.
-template <typename KeyT, int DT>
-__global__ void __launch_bounds__(256) k_lk_bwd_general(LkArgs a, int64_t reads_per_cta, int vshift) {
-    using E = Elem<DT>;
-    using Acc = typename E::Acc;
-    using V = typename E::T;
-    __shared__ int64_t srow[512];
-    const int k = static_cast<int>(a.k);
-    const int64_t N = a.B * a.T * a.C;
-    const int64_t r0 = blockIdx.x * reads_per_cta;
-    const int nr = static_cast<int>((N - r0) < reads_per_cta ? (N - r0) : reads_per_cta);
-    const int ns = nr * k;
-    for (int e = threadIdx.x; e < ns; e += 256) {
-        int64_t row; bool valid;
-        general_candidate<KeyT>(a, r0 + e / k, e % k, row, valid);
-        srow[e] = valid ? row : -1;
-    }
-    __syncthreads();
-    const int64_t D = a.D;
-    const V* g = static_cast<const V*>(a.grad) + r0 * k * D;
-    Acc* acc = static_cast<Acc*>(a.out);
-    const bool vec4 = (DT == RAVEL_F32) && (D % 4 == 0);
-    if constexpr (sizeof(V) == 2) {
-        if (vshift >= 0) {
-            // 16-bit payloads: one 16-byte gradient load and two float4 atomics per 8 elements
-            const uint32_t cmask = (1u << vshift) - 1u;
-            for (uint32_t e = threadIdx.x; e < (static_cast<uint32_t>(ns) << vshift); e += 256) {
-                const uint32_t sl = e >> vshift, c = e & cmask;
-                const int64_t row = srow[sl];
-                if (row < 0) continue;
-                const uint4 w = ld_nc_v4(g + static_cast<int64_t>(sl) * D + c * 8);
-                const float2 p0 = pair_to_float2<V>(w.x), p1 = pair_to_float2<V>(w.y);
-                const float2 p2 = pair_to_float2<V>(w.z), p3 = pair_to_float2<V>(w.w);
-                float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(acc) + row * D + c * 8);
-                atomicAdd(dst, make_float4(p0.x, p0.y, p1.x, p1.y));
-                atomicAdd(dst + 1, make_float4(p2.x, p2.y, p3.x, p3.y));
-            }
-            return;
-        }
-    }
-    if (vec4) {
-        const uint32_t d4 = static_cast<uint32_t>(D / 4);
-        for (uint32_t e = threadIdx.x; e < static_cast<uint32_t>(ns) * d4; e += 256) {
-            const uint32_t sl = e / d4, v = e % d4;
-            const int64_t row = srow[sl];
-            if (row < 0) continue;
-            const float4 x = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(g) + sl * D + v * 4);
-            atomicAdd(reinterpret_cast<float4*>(reinterpret_cast<float*>(acc) + row * D + v * 4), x);
-        }
-    } else {
-        for (uint32_t e = threadIdx.x; e < static_cast<uint32_t>(ns * D); e += 256) {
-            const uint32_t sl = e / static_cast<uint32_t>(D), d = e % static_cast<uint32_t>(D);
-            const int64_t row = srow[sl];
-            if (row < 0) continue;
-            atomicAdd(acc + row * D + d, E::to_acc(g[static_cast<int64_t>(sl) * D + d]));
-        }
-    }
-}
-
 // General latest-k backward as a gather (no atomics, deterministic): the gradient
 // of the write at sorted position q of stream s is the sum, over slots j < k whose
 // write q+j lies in q's segment, of grad_vals[r, j] over the reads r of q's address
@@ -609,13 +548,54 @@ inline size_t lk_bwd_chunk_smem(int P, int64_t k, int rcap, size_t key_bytes) {
            (static_cast<size_t>(P) + static_cast<size_t>(k) + 2) * 4 + static_cast<size_t>(rcap) * (key_bytes + 4) + 16;
 }
 
-// Convert a float accumulator [n] to the payload dtype (added to `out` when accumulating).
-template <int DT>
-__global__ void k_acc_to_dtype(const float* __restrict__ acc, typename Elem<DT>::T* __restrict__ out, int64_t n,
-                               int accumulate) {
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-        out[i] = Elem<DT>::from_acc(accumulate ? acc[i] + Elem<DT>::to_acc(out[i]) : acc[i]);
+// The same gather for rows that do not split into 2^m <= 32 vectors (odd
+// widths, rows beyond 512 bytes): one warp per write, its lanes over the row's
+// elements 32 apart.  Each element sums the same reads in the same order as
+// k_lk_bwd_gather, so every row shape is deterministic (no atomics).
+template <typename KeyT, int DT>
+__global__ void __launch_bounds__(256) k_lk_bwd_gather_rows(LkArgs a, const KeyT* rkeys, const int32_t* rridx,
+                                                            const int32_t* bstart) {
+    using E = Elem<DT>;
+    using Acc = typename E::Acc;
+    using V = typename E::T;
+    const int lane = threadIdx.x & 31;
+    const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+    const int64_t T = a.T, S = a.B * a.C, D = a.D;
+    const int k = static_cast<int>(a.k);
+    const KeyT tmask = (static_cast<KeyT>(1) << a.tbits) - 1;
+    const V* grad = static_cast<const V*>(a.grad);
+    V* out = static_cast<V*>(a.out);
+    for (int64_t gi = warp0; gi < S * T; gi += nwarps) {
+        const int64_t s = gi / T, q = gi - s * T;
+        const int64_t n_s = a.nvalid ? a.nvalid[s] : T;
+        const KeyT* wk = static_cast<const KeyT*>(a.keys) + s * T;
+        const KeyT kq = wk[q];
+        const RowMap rows_of(s, T, a.C);
+        const uint64_t orow = static_cast<uint64_t>(rows_of(kq & tmask));
+        int32_t i0 = 0, i1 = 0;
+        const KeyT aq = kq >> a.tbits;
+        if (q < n_s) {
+            int jmax = 0;  // slots j < jmax keep write q+j in q's segment
+            while (jmax < k && q + jmax < n_s && (wk[q + jmax] >> a.tbits) == aq) ++jmax;
+            const int32_t* bs = bstart + s * (T + 2);
+            i0 = bs[q + 1];
+            i1 = bs[q + 1 + jmax];
+        }
+        const KeyT* rk = rkeys + s * T;
+        const int32_t* rr = rridx + s * T;
+        for (int64_t d = lane; d < D; d += 32) {
+            Acc acc = a.accumulate ? E::to_acc(out[orow * D + d]) : Acc(0);
+            for (int32_t i = i0; i < i1; ++i) {
+                const KeyT key = rk[i];
+                if ((key >> a.tbits) != aq) continue;
+                const int jj = static_cast<int>(rr[i] - q);
+                acc += E::to_acc(grad[(static_cast<uint64_t>(rows_of(key & tmask)) * k + jj) * D + d]);
+            }
+            out[orow * D + d] = E::from_acc(acc);
+        }
+    }
 }
+
 
 }  // namespace ravel

@@ -673,8 +673,8 @@ int lk_bwd(const void* tape, int flags, const void* raddr, int addr_dtype, const
             });
         });
     }
-    // general: a gather over the read tape when a row splits into 2^m <= 32
-    // vectors, one lane each; otherwise atomics into an accumulator
+    // general: a gather over the read tape, with one lane per vector when a row
+    // splits into 2^m <= 32 vectors, else one warp per write over its elements
     {
         const int gvb = pick_vec_bytes(a.row_bytes, addr_bits(grad_vals) | addr_bits(grad_payload));
         const int64_t grv = a.row_bytes / gvb;
@@ -712,35 +712,15 @@ int lk_bwd(const void* tape, int flags, const void* raddr, int addr_dtype, const
             });
         }
     }
-    const ScratchLayout sl = scratch_layout(B, T, C, D, A, dtype, flags);
-    const bool direct = dtype == RAVEL_F32 || dtype == RAVEL_F64;
-    void* acc = grad_payload;
-    if (!direct) {
-        if (scratch == nullptr || scratch_bytes < sl.total) return RAVEL_ERR_WORKSPACE;
-        acc = static_cast<char*>(scratch) + sl.off_big;
-    }
-    const size_t acc_sz = static_cast<size_t>(N) * D * acc_bytes(dtype);
-    // float32 / float64 accumulate straight into the output: it keeps its contents when accumulating
-    if ((!direct || !accumulate) && cudaMemsetAsync(acc, 0, acc_sz, st) != cudaSuccess) return RAVEL_ERR_CUDA;
-    a.out = acc;
-    a.accumulate = 0;
-    const int64_t rpc = 512 / k;
-    const int vsh = vshift16(dtype, D, addr_bits(grad_vals) | addr_bits(acc));
+    // other row shapes: the same gather, one warp per write over the row's elements
+    a.out = grad_payload;
     return with_key(tl.kl.key64, [&](auto kt) -> int {
         using KeyT = decltype(kt);
         return with_dtype(dtype, [&](auto dtc) -> int {
             constexpr int DT = decltype(dtc)::value;
-            k_lk_bwd_general<KeyT, DT><<<static_cast<unsigned>((N + rpc - 1) / rpc), 256, 0, st>>>(a, rpc, vsh);
-            if (int e = check_launch()) return e;
-            if constexpr (DT == RAVEL_BF16 || DT == RAVEL_F16) {
-                const int64_t n = N * D;
-                k_acc_to_dtype<DT><<<grid_cap((n + 255) / 256), 256, 0, st>>>(
-                    static_cast<const float*>(acc), static_cast<typename Elem<DT>::T*>(grad_payload), n,
-                    accumulate);
-                return check_launch();
-            } else {
-                return RAVEL_OK;
-            }
+            k_lk_bwd_gather_rows<KeyT, DT><<<grid_cap((B * C * T * 32 + 255) / 256), 256, 0, st>>>(
+                a, static_cast<const KeyT*>(tv.rkeys), tv.rridx, tv.bstart);
+            return check_launch();
         });
     });
 }
@@ -975,7 +955,6 @@ int ss_bwd(const void* tape, int flags, const void* raddr, int addr_dtype, const
                                                 /*inclusive=*/0, /*reverse=*/1, scratch, sl, st);
             }
             void* accbuf = static_cast<char*>(scratch) + sl.off_big;
-            const size_t acc_sz = static_cast<size_t>(B * C * T) * D * acc_bytes(DT);
             if (tl.has_mask &&
                 cudaMemsetAsync(grad_payload, 0, static_cast<size_t>(N) * D * elem_bytes(DT), st) != cudaSuccess)
                 return RAVEL_ERR_CUDA;
@@ -986,19 +965,21 @@ int ss_bwd(const void* tape, int flags, const void* raddr, int addr_dtype, const
                                                         1, scratch, sl, st, /*merged=*/1, /*load_role=*/0);
                 if (rc >= 0) return rc;
             }
-            // rows of 2^m <= 32 vectors: a reverse inclusive scan of the read
-            // gradients over the read tape (suffix sums per address, payload dtype,
-            // in accbuf), then each write copies the suffix at its first read
-            // ranked at or after it; otherwise atomics
+            // other row shapes: a reverse inclusive scan of the read gradients over the
+            // read tape (suffix sums per address, payload dtype, in accbuf), then each
+            // write copies the suffix at its first read ranked at or after it (one lane
+            // per vector for rows of 2^m <= 32 vectors, else a warp over its elements)
             const int gvb = pick_vec_bytes(D * elem_bytes(DT), addr_bits(grad_sums) | addr_bits(grad_payload));
             const int64_t grv = D * elem_bytes(DT) / gvb;
-            if (grv >= 1 && grv <= 32 && (grv & (grv - 1)) == 0) {
+            {
                 TapeView rv = tv;
                 rv.keys = tv.rkeys;
                 rv.nvalid = nullptr;  // every read is on the read tape
                 if (int e = launch_segscan<KeyT, DT>(rv, tl, B, T, C, D, grad_sums, 0, accbuf, 1, nullptr,
                                                      /*inclusive=*/1, /*reverse=*/1, scratch, sl, st))
                     return e;
+            }
+            if (grv >= 1 && grv <= 32 && (grv & (grv - 1)) == 0) {
                 int lsh = 0;
                 while ((int64_t{1} << lsh) < grv) ++lsh;
                 const int64_t warps = (B * C * T + (32 >> lsh) - 1) / (32 >> lsh);
@@ -1014,24 +995,10 @@ int ss_bwd(const void* tape, int flags, const void* raddr, int addr_dtype, const
                     }
                 });
             }
-            if (cudaMemsetAsync(accbuf, 0, acc_sz, st) != cudaSuccess) return RAVEL_ERR_CUDA;
-            SsGenArgs g;
-            std::memset(&g, 0, sizeof(g));
-            g.keys = tv.keys; g.soff = tv.soff; g.ridx = tv.ridx;
-            g.raddr = raddr;
-            g.addr_i64 = addr_dtype == RAVEL_I64;
-            g.key32 = key32_of(B, T, C, A);
-            g.B = B; g.T = T; g.C = C; g.D = D; g.A = A;
-            g.tbits = tl.kl.tbits;
-            g.fd_C = FastDiv(static_cast<uint32_t>(C));
-            g.fd_T = FastDiv(static_cast<uint32_t>(T));
-            g.accbuf = accbuf;
-            g.grad = grad_sums;
-            g.vshift = vshift16(DT, D, addr_bits(grad_sums) | addr_bits(accbuf));
-            k_ss_scatter<KeyT, DT><<<grid_cap((N * 32 + 255) / 256), 256, 0, st>>>(g);
-            if (int e = check_launch()) return e;
-            return launch_segscan<KeyT, DT>(tv, tl, B, T, C, D, accbuf, 1, grad_payload, 0, nullptr, 1, 1,
-                                            scratch, sl, st);
+            k_ss_bwd_suffix_rows<KeyT, DT><<<grid_cap((B * C * T * 32 + 255) / 256), 256, 0, st>>>(
+                static_cast<const KeyT*>(tv.keys), static_cast<const KeyT*>(tv.rkeys), tv.bstart, tv.nvalid, accbuf,
+                grad_payload, B * C, T, C, D, tl.kl.tbits);
+            return check_launch();
         });
     });
 }

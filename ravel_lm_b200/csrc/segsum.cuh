@@ -1192,43 +1192,6 @@ __global__ void __launch_bounds__(256) k_ss_gather(SsGenArgs a) {
     }
 }
 
-// accbuf[latest(r)] += grad_sums[r] for every valid read (transpose of the gather)
-template <typename KeyT, int DT>
-__global__ void __launch_bounds__(256) k_ss_scatter(SsGenArgs a) {
-    using E = Elem<DT>;
-    using Acc = typename E::Acc;
-    using V = typename E::T;
-    const int64_t N = a.B * a.T * a.C, D = a.D;
-    const int lane = threadIdx.x & 31;
-    const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-    const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
-    if constexpr (sizeof(V) == 2) {
-        if (a.vshift >= 0) {  // 2^vshift lanes per read: a 16-byte gradient load, two float4 atomics
-            const int sh = a.vshift;
-            const int sub = lane >> sh, c = lane & ((1 << sh) - 1);
-            const int64_t per = 32 >> sh;
-            for (int64_t r0 = warp0 * per; r0 < N; r0 += nwarps * per) {
-                const int64_t r = r0 + sub;
-                if (r >= N) continue;
-                int64_t ti = 0;
-                if (!ss_valid<KeyT>(a, r, ti)) continue;
-                float f[8];
-                unpack8<V>(ld_nc_v4(static_cast<const V*>(a.grad) + r * D + c * 8), f);
-                float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.accbuf) + ti * D + c * 8);
-                atomicAdd(dst, make_float4(f[0], f[1], f[2], f[3]));
-                atomicAdd(dst + 1, make_float4(f[4], f[5], f[6], f[7]));
-            }
-            return;
-        }
-    }
-    for (int64_t r = warp0; r < N; r += nwarps) {
-        int64_t ti = 0;
-        if (!ss_valid<KeyT>(a, r, ti)) continue;
-        Acc* dst = static_cast<Acc*>(a.accbuf) + ti * D;
-        const V* g = static_cast<const V*>(a.grad) + r * D;
-        for (int64_t d = lane; d < D; d += 32) atomicAdd(dst + d, E::to_acc(g[d]));
-    }
-}
 
 // General sum backward, second half.  The first half is a reverse inclusive
 // segmented scan over the *read* tape (reads sorted by (address, t)), which
@@ -1263,6 +1226,32 @@ __global__ void __launch_bounds__(256) k_ss_bwd_suffix(const KeyT* wkeys, const 
         if (valid) x = ldg_vec<VB>(static_cast<const V*>(suffix) + (s * T + i) * D + lig * EPV);
         const RowMap rows_of(s, T, C);
         st_vec<VB>(static_cast<V*>(grad) + static_cast<uint64_t>(rows_of(wk & tmask)) * D + lig * EPV, x);
+    }
+}
+
+// k_ss_bwd_suffix for rows that do not split into 2^m <= 32 vectors: one warp per
+// write, its lanes over the row's elements 32 apart (a copy, so deterministic).
+template <typename KeyT, int DT>
+__global__ void __launch_bounds__(256) k_ss_bwd_suffix_rows(const KeyT* wkeys, const KeyT* rkeys,
+                                                            const int32_t* bstart, const int* nvalid,
+                                                            const void* suffix, void* grad, int64_t S, int64_t T,
+                                                            int64_t C, int64_t D, int tbits) {
+    using V = typename Elem<DT>::T;
+    const int lane = threadIdx.x & 31;
+    const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+    const KeyT tmask = (static_cast<KeyT>(1) << tbits) - 1;
+    for (int64_t gi = warp0; gi < S * T; gi += nwarps) {
+        const int64_t s = gi / T, q = gi - s * T;
+        const int64_t n_s = nvalid ? nvalid[s] : T;
+        if (q >= n_s) continue;  // masked writes: their rows were zeroed before
+        const KeyT wk = wkeys[gi];
+        const int32_t i = bstart[s * (T + 2) + q + 1];
+        const bool valid = i < T && (rkeys[s * T + i] >> tbits) == (wk >> tbits);
+        const RowMap rows_of(s, T, C);
+        V* dst = static_cast<V*>(grad) + static_cast<uint64_t>(rows_of(wk & tmask)) * D;
+        const V* src = static_cast<const V*>(suffix) + (s * T + i) * D;
+        for (int64_t d = lane; d < D; d += 32) dst[d] = valid ? src[d] : Elem<DT>::from_acc(typename Elem<DT>::Acc(0));
     }
 }
 
