@@ -131,6 +131,15 @@ CASES = [
     ("d512_bf16_1kb_rows_mask", 1, 1200, 2, 512, 30, 2, torch.bfloat16, False, True, "uniform"),
     ("d128_f64_1kb_general", 1, 1500, 2, 128, 40, 2, torch.float64, True, True, "uniform"),
     ("d256_bf16_general_acc_1kb", 1, 2000, 2, 256, 60, 2, torch.bfloat16, True, False, "uniform"),
+    # short streams of 128-byte rows: the one-CTA-per-stream scan (aliased and merged, masks,
+    # 16-bit and 64-bit keys, a single step)
+    ("short_general_mask_f32", 3, 1500, 4, 32, 40, 3, torch.float32, True, True, "uniform"),
+    ("short_aliased_bf16", 2, 1800, 3, 64, 50, 2, torch.bfloat16, False, False, "zipf1.05"),
+    ("short_aliased_mask_bf16", 2, 1800, 3, 64, 50, 2, torch.bfloat16, False, True, "uniform"),
+    ("short_general_f16_d64", 2, 1000, 3, 64, 30, 2, torch.float16, True, False, "uniform"),
+    ("short_key64_general_mask", 2, 1500, 2, 32, 2**31, 2, torch.float32, True, True, "huge"),
+    ("short_t1_f32", 4, 1, 3, 32, 5, 2, torch.float32, True, False, "uniform"),
+    ("short_t4096_aliased_f32", 1, 4096, 2, 32, 300, 2, torch.float32, False, False, "uniform"),
 ]
 
 
