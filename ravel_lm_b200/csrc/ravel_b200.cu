@@ -606,8 +606,10 @@ int lk_fwd_tape(const void* tape, int flags, const void* raddr, int addr_dtype, 
                 } else {
                     if (!tl.general) {
                         int64_t P = 40960 / (a.row_bytes + 16) - k;
+// Build-time knob: at most this many sorted positions per CTA of the aliased latest-k
+// forward.  Measured at config 3 (us): 128 positions 439.8, 64 positions 435.7.
 #ifndef RAVEL_LK_PMAX
-#define RAVEL_LK_PMAX 128
+#define RAVEL_LK_PMAX 64
 #endif
                         if (P > RAVEL_LK_PMAX) P = RAVEL_LK_PMAX;
                         if (P < 16) P = 16;
@@ -627,6 +629,11 @@ int lk_fwd_tape(const void* tape, int flags, const void* raddr, int addr_dtype, 
     });
 }
 
+// Build-time knob: sorted positions per CTA of the aliased latest-k backward.
+// Measured at config 3 (us, accumulate mode): 64 positions 412.6, 128 402.1, 256 404.4.
+#ifndef RAVEL_LK_BWD_P
+#define RAVEL_LK_BWD_P 128
+#endif
 // Build-time knob: 0 keeps the general latest-k backward on the per-write gather (k_lk_bwd_gather).
 #ifndef RAVEL_LK_BWD_CHUNK
 #define RAVEL_LK_BWD_CHUNK 1
@@ -654,7 +661,7 @@ int lk_bwd(const void* tape, int flags, const void* raddr, int addr_dtype, const
         const int vb = pick_vec_bytes(a.row_bytes, addr_bits(grad_vals) | addr_bits(grad_payload));
         const int64_t rv = a.row_bytes / vb;
         a.fd_rv = FastDiv(static_cast<uint32_t>(rv));
-        a.P = 128;
+        a.P = RAVEL_LK_BWD_P;
         a.nchunks = (T + a.P - 1) / a.P;
         return with_key(tl.kl.key64, [&](auto kt) -> int {
             using KeyT = decltype(kt);
